@@ -1,0 +1,13 @@
+"""flexkv_b200 — B200-native (sm_100a) FlexKV transfer data plane.
+
+``flexkv_b200.c_ext`` mirrors FlexKV's native module ``flexkv.c_ext`` for the
+KV-block gather/scatter, the tensor-parallel group and the XXH64 block
+hashes; everything runs in libflexkv_b200.so (C ABI: include/flexkv_b200.h).
+"""
+__version__ = "0.1.0"
+
+
+def lib_path() -> str:
+    """Path of the loaded libflexkv_b200.so (loads it; raises if missing)."""
+    from . import _lib
+    return _lib.lib_path()

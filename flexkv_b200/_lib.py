@@ -1,0 +1,140 @@
+"""ctypes binding of libflexkv_b200.so (the C ABI in include/flexkv_b200.h).
+
+Loading fails loudly: there is no Python or CPU fallback for any entry point.
+Build the library with ``python -m flexkv_b200.build``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+from .build import LIB_PATH
+
+c_int = ctypes.c_int
+c_i64 = ctypes.c_int64
+c_u64 = ctypes.c_uint64
+c_vp = ctypes.c_void_p
+c_char_p = ctypes.c_char_p
+P_i64 = ctypes.POINTER(ctypes.c_int64)
+P_u64 = ctypes.POINTER(ctypes.c_uint64)
+
+FKV_OK = 0
+FKV_ERR_INVALID_ARG = 1
+FKV_ERR_OUT_OF_RANGE = 2
+FKV_ERR_MISALIGNED = 3
+FKV_ERR_CUDA = 4
+FKV_ERR_UNSUPPORTED = 5
+FKV_ERR_TIMEOUT = 6
+
+
+class TransferDesc(ctypes.Structure):
+    """Mirror of ``fkv_transfer_desc`` (field order and types must match)."""
+
+    _fields_ = [
+        ("num_blocks", c_int),
+        ("start_layer_id", c_int),
+        ("num_layers", c_int),
+        ("is_host_to_device", c_int),
+        ("is_mla", c_int),
+        ("transfer_sms", c_int),
+        ("use_ce_transfer", c_int),
+        ("synchronous", c_int),
+        ("gpu_block_ids", c_vp),
+        ("cpu_block_ids", c_vp),
+        ("gpu_layer_ptrs", c_vp),
+        ("cpu_ptr", c_vp),
+        ("gpu_kv_stride_in_bytes", c_i64),
+        ("gpu_block_stride_in_bytes", c_i64),
+        ("cpu_kv_stride_in_bytes", c_i64),
+        ("cpu_layer_stride_in_bytes", c_i64),
+        ("cpu_block_stride_in_bytes", c_i64),
+        ("cpu_startoff_inside_chunks", c_i64),
+        ("chunk_size_in_bytes", c_i64),
+        ("cpu_pool_bytes", c_i64),
+        ("gpu_layer_bytes", c_i64),
+        ("ce_min_run_bytes", c_i64),
+        ("num_ce_streams", c_int),
+        ("reserved", c_int),
+    ]
+
+
+# name -> (restype, argtypes)
+_SIGNATURES = {
+    "fkv_last_error": (c_char_p, []),
+    "fkv_version": (c_char_p, []),
+    "fkv_kernel_launch_count": (c_u64, []),
+    "fkv_host_register": (c_int, [c_vp, c_i64, c_int]),
+    "fkv_host_unregister": (c_int, [c_vp]),
+    "fkv_transfer_kv_blocks": (
+        c_int,
+        [c_int, c_int, c_int, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64,
+         c_i64, c_i64, c_vp, c_int, c_int, c_int, c_int],
+    ),
+    "fkv_transfer_desc_init": (None, [ctypes.POINTER(TransferDesc)]),
+    "fkv_transfer_kv_blocks_ex": (c_int, [ctypes.POINTER(TransferDesc), c_vp]),
+    "fkv_plan_create": (c_int, [ctypes.POINTER(TransferDesc), c_int, ctypes.POINTER(c_vp)]),
+    "fkv_plan_execute": (c_int, [c_vp, c_vp]),
+    "fkv_plan_execute_ex": (c_int, [c_vp, c_vp, c_vp, c_vp]),
+    "fkv_plan_stats": (c_int, [c_vp, P_i64, P_i64, P_i64, P_i64]),
+    "fkv_plan_destroy": (None, [c_vp]),
+    "fkv_coalesce_runs": (c_i64, [c_vp, c_vp, c_i64, c_vp, c_i64]),
+    "fkv_tp_group_create": (
+        c_int, [c_int, c_int, c_vp, c_vp, c_int, c_vp, c_i64, ctypes.POINTER(c_vp)]),
+    "fkv_tp_group_transfer": (
+        c_int,
+        [c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_int,
+         c_int, c_int, c_int, c_int, c_int],
+    ),
+    "fkv_tp_group_num_gpus": (c_int, [c_vp]),
+    "fkv_tp_group_destroy": (None, [c_vp]),
+    "fkv_get_hash_size": (c_int, []),
+    "fkv_hasher_create": (c_int, [c_int, ctypes.POINTER(c_vp)]),
+    "fkv_hasher_destroy": (None, [c_vp]),
+    "fkv_hasher_reset": (c_int, [c_vp, c_vp]),
+    "fkv_hasher_update": (c_int, [c_vp, c_vp, c_i64, c_vp]),
+    "fkv_hasher_digest": (c_int, [c_vp, P_u64, c_vp]),
+    "fkv_gen_hashes": (c_int, [c_vp, c_vp, c_i64, c_int, c_vp, c_i64, c_vp]),
+    "fkv_gen_hashes_batched": (c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class FlexKVError(RuntimeError):
+    """A non-zero status from libflexkv_b200 (RuntimeError, as the
+    reference's pybind layer raises for CUDA failures, bindings.cpp:51-54)."""
+
+    def __init__(self, code: int, where: str, message: str):
+        super().__init__(f"{where} failed (status {code}): {message}")
+        self.code = code
+
+
+def load(path: str | None = None) -> ctypes.CDLL:
+    """Load (once) and return the library with argument types declared."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        p = path or os.environ.get("FLEXKV_B200_LIB", LIB_PATH)
+        if not os.path.exists(p):
+            raise ImportError(
+                f"libflexkv_b200.so not found at {p}; build it with `python -m flexkv_b200.build`")
+        lib = ctypes.CDLL(p)
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def check(rc: int, where: str) -> None:
+    if rc != FKV_OK:
+        msg = load().fkv_last_error()
+        raise FlexKVError(rc, where, msg.decode() if msg else "")
+
+
+def lib_path() -> str:
+    return load()._name

@@ -1,0 +1,152 @@
+// Host plumbing shared by every entry point of libflexkv_b200.
+#include "fkv_common.h"
+
+#include <sys/mman.h>
+
+#include <cstring>
+#include <map>
+#include <memory>
+
+namespace fkv {
+
+std::atomic<uint64_t> g_kernel_launches{0};
+
+namespace {
+thread_local std::string t_error;
+thread_local std::map<int, std::unique_ptr<ThreadDeviceCtx>> t_ctx;
+}  // namespace
+
+void set_error(const std::string &msg) { t_error = msg; }
+void clear_error() { t_error.clear(); }
+const char *last_error() { return t_error.c_str(); }
+
+int fail(int code, const std::string &msg) {
+  set_error(msg);
+  return code;
+}
+
+int fail_cuda(cudaError_t e, const char *what) {
+  std::string m = std::string(what) + ": " + cudaGetErrorName(e) + " (" +
+                  cudaGetErrorString(e) + ")";
+  set_error(m);
+  return FKV_ERR_CUDA;
+}
+
+int get_ctx(int device, ThreadDeviceCtx **out) {
+  if (device < 0) FKV_CUDA(cudaGetDevice(&device));
+  auto it = t_ctx.find(device);
+  if (it != t_ctx.end()) {
+    *out = it->second.get();
+    return FKV_OK;
+  }
+  auto ctx = std::make_unique<ThreadDeviceCtx>();
+  ctx->device = device;
+  FKV_CUDA(cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device));
+  int prev = -1;
+  FKV_CUDA(cudaGetDevice(&prev));
+  if (prev != device) FKV_CUDA(cudaSetDevice(device));
+  cudaError_t e = cudaEventCreateWithFlags(&ctx->fork_event, cudaEventDisableTiming);
+  if (e == cudaSuccess)
+    e = cudaEventCreateWithFlags(&ctx->staging_free, cudaEventDisableTiming);
+  if (prev != device) cudaSetDevice(prev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaEventCreateWithFlags");
+  *out = ctx.get();
+  t_ctx.emplace(device, std::move(ctx));
+  return FKV_OK;
+}
+
+int ensure_side_streams(ThreadDeviceCtx *ctx, int n) {
+  if ((int)ctx->side_streams.size() >= n) return FKV_OK;
+  int prev = -1;
+  FKV_CUDA(cudaGetDevice(&prev));
+  if (prev != ctx->device) FKV_CUDA(cudaSetDevice(ctx->device));
+  int rc = FKV_OK;
+  while ((int)ctx->side_streams.size() < n) {
+    cudaStream_t s;
+    cudaEvent_t ev;
+    cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+    if (e != cudaSuccess) { rc = fail_cuda(e, "cudaStreamCreateWithFlags"); break; }
+    e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    if (e != cudaSuccess) { rc = fail_cuda(e, "cudaEventCreateWithFlags"); break; }
+    ctx->side_streams.push_back(s);
+    ctx->join_events.push_back(ev);
+  }
+  if (prev != ctx->device) cudaSetDevice(prev);
+  return rc;
+}
+
+int acquire_staging(ThreadDeviceCtx *ctx, size_t bytes, char **out) {
+  if (ctx->staging_pending) {
+    FKV_CUDA(cudaEventSynchronize(ctx->staging_free));
+    ctx->staging_pending = false;
+  }
+  if (bytes > ctx->staging_cap) {
+    if (ctx->staging) FKV_CUDA(cudaFreeHost(ctx->staging));
+    ctx->staging = nullptr;
+    ctx->staging_cap = 0;
+    size_t cap = 4096;
+    while (cap < bytes) cap <<= 1;
+    FKV_CUDA(cudaHostAlloc((void **)&ctx->staging, cap, cudaHostAllocPortable));
+    ctx->staging_cap = cap;
+  }
+  *out = ctx->staging;
+  return FKV_OK;
+}
+
+int release_staging(ThreadDeviceCtx *ctx, cudaStream_t stream) {
+  FKV_CUDA(cudaEventRecord(ctx->staging_free, stream));
+  ctx->staging_pending = true;
+  return FKV_OK;
+}
+
+int pointer_is_device(const void *p, int *is_device, int *device) {
+  cudaPointerAttributes attr;
+  cudaError_t e = cudaPointerGetAttributes(&attr, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // unregistered host pointer on old runtimes
+    *is_device = 0;
+    *device = -1;
+    return FKV_OK;
+  }
+  *is_device = (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged);
+  *device = attr.device;
+  return FKV_OK;
+}
+
+}  // namespace fkv
+
+extern "C" {
+
+const char *fkv_last_error(void) { return fkv::last_error(); }
+
+const char *fkv_version(void) { return "flexkv_b200 0.1.0 (sm_100a)"; }
+
+uint64_t fkv_kernel_launch_count(void) {
+  return fkv::g_kernel_launches.load(std::memory_order_relaxed);
+}
+
+int fkv_host_register(void *ptr, int64_t bytes, int advise_hugepages) {
+  fkv::clear_error();
+  if (ptr == nullptr || bytes <= 0)
+    return fkv::fail(FKV_ERR_INVALID_ARG, "fkv_host_register: null pointer or non-positive size");
+  if (advise_hugepages) {
+    // Best effort: only helps for pages not yet touched.
+    uintptr_t a = (uintptr_t)ptr, page = 4096;
+    uintptr_t lo = (a + page - 1) & ~(page - 1);
+    uintptr_t hi = (a + (uintptr_t)bytes) & ~(page - 1);
+    if (hi > lo) madvise((void *)lo, hi - lo, MADV_HUGEPAGE);
+  }
+  cudaError_t e = cudaHostRegister(ptr, (size_t)bytes,
+                                   cudaHostRegisterPortable | cudaHostRegisterMapped);
+  if (e != cudaSuccess) return fkv::fail_cuda(e, "cudaHostRegister");
+  return FKV_OK;
+}
+
+int fkv_host_unregister(void *ptr) {
+  fkv::clear_error();
+  cudaError_t e = cudaHostUnregister(ptr);
+  if (e != cudaSuccess) return fkv::fail_cuda(e, "cudaHostUnregister");
+  return FKV_OK;
+}
+
+}  // extern "C"

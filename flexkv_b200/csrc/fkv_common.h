@@ -1,0 +1,64 @@
+// Shared host-side plumbing of libflexkv_b200: error reporting, launch
+// accounting and the per-thread, per-device resources (side streams, events,
+// pinned staging) that the transfer and hash entry points reuse.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+#include <vector>
+
+#include "../../include/flexkv_b200.h"
+
+namespace fkv {
+
+// Thread-local last error; set by fail() and returned through fkv_last_error.
+void set_error(const std::string &msg);
+void clear_error();
+const char *last_error();
+
+// Record a failure and return its code (for `return fail(...)` chains).
+int fail(int code, const std::string &msg);
+int fail_cuda(cudaError_t e, const char *what);
+
+// Count of kernels launched by this library (all threads).
+extern std::atomic<uint64_t> g_kernel_launches;
+inline void note_launch(uint64_t n = 1) { g_kernel_launches.fetch_add(n, std::memory_order_relaxed); }
+
+#define FKV_CUDA(call)                                     \
+  do {                                                     \
+    cudaError_t fkv_e_ = (call);                           \
+    if (fkv_e_ != cudaSuccess) return ::fkv::fail_cuda(fkv_e_, #call); \
+  } while (0)
+
+// Resources owned by one host thread on one device.  Created lazily, never
+// freed before process exit (CUDA teardown order at exit is unspecified).
+struct ThreadDeviceCtx {
+  int device = -1;
+  int num_sms = 0;
+  std::vector<cudaStream_t> side_streams;  // copy-engine streams
+  std::vector<cudaEvent_t> join_events;    // one per side stream
+  cudaEvent_t fork_event = nullptr;
+  // Pinned staging for small uploads (plan tables, hash state).
+  char *staging = nullptr;
+  size_t staging_cap = 0;
+  cudaEvent_t staging_free = nullptr;  // recorded after the last upload read it
+  bool staging_pending = false;
+};
+
+// Context of the calling thread for `device` (current device if -1).
+int get_ctx(int device, ThreadDeviceCtx **out);
+// Ensure `n` side streams exist in ctx.
+int ensure_side_streams(ThreadDeviceCtx *ctx, int n);
+// Pinned staging buffer of at least `bytes`, safe to overwrite now.
+int acquire_staging(ThreadDeviceCtx *ctx, size_t bytes, char **out);
+// Mark that an async copy on `stream` reads the staging buffer.
+int release_staging(ThreadDeviceCtx *ctx, cudaStream_t stream);
+
+// Classify a pointer: 1 = device memory (or managed), 0 = host.
+int pointer_is_device(const void *p, int *is_device, int *device);
+
+}  // namespace fkv

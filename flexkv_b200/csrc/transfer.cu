@@ -1,0 +1,641 @@
+// KV-block gather/scatter between a paged GPU KV cache and a page-locked
+// host pool — the B200 data plane that replaces flexkv::transfer_kv_blocks
+// (csrc/transfer.cu:26-132 of linhu-nv/FlexKV).
+//
+// Work split (decided on the host, per call):
+//   * runs of blocks whose GPU and CPU ids both advance by one are
+//     coalesced; a run whose per-(layer,kv) span reaches ce_min_run_bytes
+//     becomes one (1-D or 2-D) cudaMemcpyAsync on a side stream, so the copy
+//     engines move it with large PCIe requests;
+//   * every other chunk goes to kv_copy_kernel: a persistent grid sized by
+//     the SM budget, one warp per (layer, kv, block) chunk, 16-byte
+//     vector loads/stores with UNROLL loads in flight per lane, reading or
+//     writing the host pool through its mapped (zero-copy) address.
+//   The caller's stream forks to the side streams and joins back, so the
+//   whole transfer is ordered on the caller's stream like the reference.
+//
+// Address arithmetic is the reference's (transfer.cu:39-50, 84-93): byte
+// strides truncated to int64 units, start_layer_id offsets the CPU side
+// only, and the copied size is 16*floor(chunk/16).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "fkv_common.h"
+
+namespace fkv {
+namespace {
+
+constexpr int kThreads = 256;          // 8 warps per CTA
+constexpr int kDefaultSms = 16;        // SM budget when transfer_sms == -1
+constexpr int64_t kDefaultCeMinRunBytes = 2ll << 20;  // 2 MiB per (layer,kv) span
+constexpr int kDefaultCeStreams = 2;
+
+struct CopyParams {
+  const int64_t *gpu_ids;     // device [n]
+  const int64_t *cpu_ids;     // device [n]
+  char *const *layer_ptrs;    // device [num_layers]
+  char *cpu_base;             // device-visible host address of layer start_layer_id, + startoff
+  int64_t gpu_kv_stride;
+  int64_t gpu_block_stride;
+  int64_t cpu_layer_stride;
+  int64_t cpu_kv_stride;
+  int64_t cpu_block_stride;
+  int64_t n_vec;              // 16-byte vectors per chunk
+  uint32_t n;                 // blocks
+  uint32_t per_layer;         // kv_dim * n
+  uint32_t num_chunks;        // num_layers * kv_dim * n
+};
+
+// Coherent (not .nc) load on purpose: with .nc the assembler may legally
+// sink each store between the loads (the data is declared read-only), which
+// leaves one load per lane in flight instead of UNROLL — fatal for reads
+// that cross PCIe with microsecond latency.
+__device__ __forceinline__ uint4 ld_stream(const uint4 *p) {
+  uint4 r;
+  asm volatile("ld.global.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p)
+               : "memory");
+  return r;
+}
+
+__device__ __forceinline__ void st_stream(uint4 *p, const uint4 &v) {
+  asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// One warp copies one chunk: lane l moves vectors l, l+32, ...; each pass
+// keeps UNROLL 16-byte loads in flight per lane (UNROLL*512 bytes per warp).
+template <int UNROLL>
+__device__ __forceinline__ void copy_chunk(const uint4 *__restrict__ src,
+                                           uint4 *__restrict__ dst,
+                                           int64_t n_vec, int lane) {
+  constexpr int64_t kStep = 32 * UNROLL;
+  int64_t base = 0;
+  for (; base + kStep <= n_vec; base += kStep) {
+    uint4 r[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) r[u] = ld_stream(src + base + u * 32 + lane);
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) st_stream(dst + base + u * 32 + lane, r[u]);
+  }
+  // Remainder: fewer than 32*UNROLL vectors.
+  for (int64_t v = base + lane; v < n_vec; v += 32) st_stream(dst + v, ld_stream(src + v));
+}
+
+template <bool H2D, int UNROLL>
+__global__ void __launch_bounds__(kThreads) kv_copy_kernel(const CopyParams p) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t warp = (blockIdx.x * kThreads + threadIdx.x) >> 5;
+  const uint32_t nwarps = (gridDim.x * kThreads) >> 5;
+  for (uint32_t c = warp; c < p.num_chunks; c += nwarps) {
+    const uint32_t layer = c / p.per_layer;
+    const uint32_t rem = c - layer * p.per_layer;
+    const uint32_t kv = rem / p.n;
+    const uint32_t i = rem - kv * p.n;
+    const int64_t g = p.gpu_ids[i];
+    const int64_t h = p.cpu_ids[i];
+    char *gpu = p.layer_ptrs[layer] + kv * p.gpu_kv_stride + g * p.gpu_block_stride;
+    char *cpu = p.cpu_base + layer * p.cpu_layer_stride + kv * p.cpu_kv_stride +
+                h * p.cpu_block_stride;
+    const uint4 *src = reinterpret_cast<const uint4 *>(H2D ? cpu : gpu);
+    uint4 *dst = reinterpret_cast<uint4 *>(H2D ? gpu : cpu);
+    copy_chunk<UNROLL>(src, dst, p.n_vec, lane);
+  }
+}
+
+struct CeCopy {
+  char *dst;
+  const char *src;
+  size_t width, height, dpitch, spitch;  // height==1 -> 1-D copy
+};
+
+int env_int(const char *name, int dflt) {
+  const char *s = std::getenv(name);
+  return (s && *s) ? std::atoi(s) : dflt;
+}
+int64_t env_i64(const char *name, int64_t dflt) {
+  const char *s = std::getenv(name);
+  return (s && *s) ? std::atoll(s) : dflt;
+}
+
+// Occupancy (CTAs per SM) of each kernel instantiation, cached per device.
+struct OccCache {
+  std::mutex mu;
+  int max_pitch[64] = {0};
+  int occ[64][2][3] = {{{0}}};
+};
+OccCache g_occ;
+
+int unroll_index(int unroll) { return unroll >= 16 ? 2 : (unroll >= 8 ? 1 : 0); }
+
+template <bool H2D>
+const void *kernel_ptr(int unroll_idx) {
+  switch (unroll_idx) {
+    case 0: return (const void *)kv_copy_kernel<H2D, 4>;
+    case 1: return (const void *)kv_copy_kernel<H2D, 8>;
+    default: return (const void *)kv_copy_kernel<H2D, 16>;
+  }
+}
+
+int ctas_per_sm(int device, bool h2d, int uidx, int *out) {
+  std::lock_guard<std::mutex> lk(g_occ.mu);
+  int d = device & 63;
+  int &v = g_occ.occ[d][h2d ? 1 : 0][uidx];
+  if (v == 0) {
+    const void *k = h2d ? kernel_ptr<true>(uidx) : kernel_ptr<false>(uidx);
+    int n = 0;
+    FKV_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kThreads, 0));
+    v = std::max(n, 1);
+  }
+  *out = v;
+  return FKV_OK;
+}
+
+int max_pitch(int device, int *out) {
+  std::lock_guard<std::mutex> lk(g_occ.mu);
+  int d = device & 63;
+  if (g_occ.max_pitch[d] == 0) {
+    int mp = 0;
+    FKV_CUDA(cudaDeviceGetAttribute(&mp, cudaDevAttrMaxPitch, device));
+    g_occ.max_pitch[d] = mp > 0 ? mp : 1;
+  }
+  *out = g_occ.max_pitch[d];
+  return FKV_OK;
+}
+
+}  // namespace
+}  // namespace fkv
+
+struct fkv_plan {
+  int device = -1;
+  bool h2d = true;
+  int grid = 0;
+  int unroll_idx = 1;
+  fkv::CopyParams params{};
+  char *dev_buf = nullptr;       // layer ptrs + ids (cudaMalloc, plan-owned)
+  std::vector<fkv::CeCopy> ce;
+  int num_ce_streams = 0;
+  int64_t sm_chunks = 0, ce_bytes = 0, sm_bytes = 0;
+};
+
+namespace fkv {
+namespace {
+
+// Everything the host learns from the descriptor before any device work.
+struct HostPlan {
+  bool h2d = true;
+  int kv_dim = 2;
+  int num_layers = 0;
+  int64_t copy_bytes = 0;
+  int64_t gkv = 0, gbs = 0, cls = 0, ckv = 0, cbs = 0;
+  char *cpu_dev_base = nullptr;  // device view of cpu_ptr + start_layer*cls + startoff
+  const char *cpu_host_base = nullptr;
+  std::vector<int64_t> sm_gpu, sm_cpu;  // blocks for the SM kernel
+  std::vector<CeCopy> ce;
+  int64_t ce_bytes = 0;
+  int grid = 0;
+  int unroll_idx = 1;
+  int num_ce_streams = 0;
+};
+
+inline int64_t trunc8(int64_t b) { return (b / 8) * 8; }  // transfer.cu:86-93
+
+// Argument checks that need no CUDA call.
+int validate_desc(const fkv_transfer_desc &d) {
+  if (d.num_blocks < 0 || d.num_layers < 0)
+    return fail(FKV_ERR_INVALID_ARG, "num_blocks and num_layers must be non-negative");
+  if (d.chunk_size_in_bytes < 0)
+    return fail(FKV_ERR_INVALID_ARG, "chunk_size_in_bytes must be non-negative");
+  if (d.gpu_kv_stride_in_bytes < 0 || d.gpu_block_stride_in_bytes < 0 ||
+      d.cpu_kv_stride_in_bytes < 0 || d.cpu_layer_stride_in_bytes < 0 ||
+      d.cpu_block_stride_in_bytes < 0 || d.cpu_startoff_inside_chunks < 0 ||
+      d.start_layer_id < 0)
+    return fail(FKV_ERR_INVALID_ARG, "strides, start offset and start_layer_id must be non-negative");
+  return FKV_OK;
+}
+
+int build_host_plan(const fkv_transfer_desc &d, int device, HostPlan &hp) {
+  if (int rc = validate_desc(d)) return rc;
+  hp.h2d = d.is_host_to_device != 0;
+  hp.kv_dim = d.is_mla ? 1 : 2;
+  hp.num_layers = d.num_layers;
+  hp.copy_bytes = (d.chunk_size_in_bytes / 16) * 16;  // transfer.cu:35 floor to float4
+  if (d.num_blocks == 0 || d.num_layers == 0 || hp.copy_bytes == 0) return FKV_OK;
+  if (!d.gpu_block_ids || !d.cpu_block_ids || !d.gpu_layer_ptrs || !d.cpu_ptr)
+    return fail(FKV_ERR_INVALID_ARG, "null id array, layer pointer table or cpu pointer");
+
+  hp.gkv = trunc8(d.gpu_kv_stride_in_bytes);
+  hp.gbs = trunc8(d.gpu_block_stride_in_bytes);
+  hp.cls = trunc8(d.cpu_layer_stride_in_bytes);
+  hp.ckv = trunc8(d.cpu_kv_stride_in_bytes);
+  hp.cbs = trunc8(d.cpu_block_stride_in_bytes);
+  const int64_t startoff = trunc8(d.cpu_startoff_inside_chunks);
+  const int64_t L = d.num_layers, KV = hp.kv_dim, n = d.num_blocks;
+  if ((uint64_t)L * KV * n >= (1ull << 31))
+    return fail(FKV_ERR_INVALID_ARG, "num_layers*kv_dim*num_blocks must stay below 2^31; split the op");
+
+  // The host pool must be page-locked so the device can address it.
+  cudaPointerAttributes attr;
+  cudaError_t e = cudaPointerGetAttributes(&attr, d.cpu_ptr);
+  if (e != cudaSuccess || attr.type != cudaMemoryTypeHost || attr.devicePointer == nullptr) {
+    cudaGetLastError();
+    return fail(FKV_ERR_INVALID_ARG,
+                "cpu_ptr is not page-locked host memory (allocate it pinned or cudaHostRegister it)");
+  }
+  const int64_t base_off = (int64_t)d.start_layer_id * hp.cls + startoff;
+  hp.cpu_host_base = (const char *)d.cpu_ptr + base_off;
+  hp.cpu_dev_base = (char *)attr.devicePointer + base_off;
+
+  // Alignment of every chunk start (the vector path needs 16 bytes).
+  if (((uintptr_t)hp.cpu_dev_base & 15) || ((uintptr_t)hp.cpu_host_base & 15))
+    return fail(FKV_ERR_MISALIGNED, "cpu chunk base (cpu_ptr + start_layer*layer_stride + startoff) is not 16-byte aligned");
+  if (L > 1 && (hp.cls & 15))
+    return fail(FKV_ERR_MISALIGNED, "cpu_layer_stride_in_bytes is not a multiple of 16");
+  if (KV > 1 && ((hp.ckv & 15) || (hp.gkv & 15)))
+    return fail(FKV_ERR_MISALIGNED, "kv strides are not multiples of 16");
+  for (int64_t l = 0; l < L; ++l) {
+    if (d.gpu_layer_ptrs[l] == nullptr)
+      return fail(FKV_ERR_INVALID_ARG, "null gpu layer pointer at index " + std::to_string(l));
+    if ((uintptr_t)d.gpu_layer_ptrs[l] & 15)
+      return fail(FKV_ERR_MISALIGNED, "gpu layer pointer " + std::to_string(l) + " is not 16-byte aligned");
+  }
+
+  // Per-id checks: range, alignment, pool bounds (reference truncates ids
+  // to int, transfer.cu:41-42, so ids must fit in [0, 2^31)).
+  const int64_t cpu_extent_fixed = base_off + (L - 1) * hp.cls + (KV - 1) * hp.ckv + hp.copy_bytes;
+  const int64_t gpu_extent_fixed = (KV - 1) * hp.gkv + hp.copy_bytes;
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t g = d.gpu_block_ids[i], c = d.cpu_block_ids[i];
+    if (g < 0 || c < 0 || g >= (1ll << 31) || c >= (1ll << 31))
+      return fail(FKV_ERR_OUT_OF_RANGE, "block id out of [0, 2^31) at index " + std::to_string(i));
+    if (((g * hp.gbs) & 15) || ((c * hp.cbs) & 15))
+      return fail(FKV_ERR_MISALIGNED, "block stride times id is not 16-byte aligned at index " + std::to_string(i));
+    if (d.cpu_pool_bytes > 0 && c * hp.cbs + cpu_extent_fixed > d.cpu_pool_bytes)
+      return fail(FKV_ERR_OUT_OF_RANGE, "cpu block id " + std::to_string(c) + " at index " +
+                                            std::to_string(i) + " addresses past the cpu pool");
+    if (d.gpu_layer_bytes > 0 && g * hp.gbs + gpu_extent_fixed > d.gpu_layer_bytes)
+      return fail(FKV_ERR_OUT_OF_RANGE, "gpu block id " + std::to_string(g) + " at index " +
+                                            std::to_string(i) + " addresses past the gpu layer");
+  }
+
+  // Split into copy-engine runs and SM chunks.
+  const bool ce_all = d.use_ce_transfer != 0;
+  int64_t thr = d.ce_min_run_bytes;
+  if (thr < 0) thr = env_i64("FKV_CE_MIN_RUN_BYTES", kDefaultCeMinRunBytes);
+  int mp = 0;
+  if (int rc = max_pitch(device, &mp)) return rc;
+  const size_t cb = (size_t)hp.copy_bytes;
+  const bool contig = (hp.gbs == hp.copy_bytes && hp.cbs == hp.copy_bytes);
+  auto pitch_ok = [&](int64_t p) { return p >= hp.copy_bytes && p <= mp; };
+  hp.sm_gpu.reserve(n);
+  hp.sm_cpu.reserve(n);
+  int64_t i = 0;
+  while (i < n) {
+    int64_t r = 1;
+    const int64_t g0 = d.gpu_block_ids[i], c0 = d.cpu_block_ids[i];
+    while (i + r < n && d.gpu_block_ids[i + r] == g0 + r && d.cpu_block_ids[i + r] == c0 + r) ++r;
+    const bool to_ce = ce_all || (thr > 0 && r * hp.copy_bytes >= thr);
+    if (!to_ce) {
+      for (int64_t k = 0; k < r; ++k) {
+        hp.sm_gpu.push_back(g0 + k);
+        hp.sm_cpu.push_back(c0 + k);
+      }
+      i += r;
+      continue;
+    }
+    for (int64_t l = 0; l < L; ++l) {
+      char *gl = (char *)d.gpu_layer_ptrs[l] + g0 * hp.gbs;
+      char *cl = (char *)hp.cpu_host_base + l * hp.cls + c0 * hp.cbs;
+      auto emit = [&](char *g, char *c, size_t w, size_t h, size_t gp, size_t cp) {
+        CeCopy x;
+        x.width = w;
+        x.height = h;
+        if (hp.h2d) { x.dst = g; x.src = c; x.dpitch = gp; x.spitch = cp; }
+        else        { x.dst = c; x.src = g; x.dpitch = cp; x.spitch = gp; }
+        hp.ce.push_back(x);
+        hp.ce_bytes += (int64_t)(w * h);
+      };
+      const int64_t span = r * hp.copy_bytes;
+      if (contig && (KV == 1 || (hp.gkv >= span && hp.ckv >= span && hp.gkv <= mp && hp.ckv <= mp))) {
+        // The run is contiguous on both sides: one row per kv half.
+        emit(gl, cl, (size_t)span, (size_t)KV, (size_t)hp.gkv, (size_t)hp.ckv);
+      } else if (r == 1 && KV > 1 && pitch_ok(hp.gkv) && pitch_ok(hp.ckv)) {
+        emit(gl, cl, cb, (size_t)KV, (size_t)hp.gkv, (size_t)hp.ckv);
+      } else {
+        for (int64_t kv = 0; kv < KV; ++kv) {
+          char *g = gl + kv * hp.gkv, *c = cl + kv * hp.ckv;
+          if (contig) {
+            emit(g, c, (size_t)span, 1, 0, 0);
+          } else if (pitch_ok(hp.gbs) && pitch_ok(hp.cbs)) {
+            emit(g, c, cb, (size_t)r, (size_t)hp.gbs, (size_t)hp.cbs);
+          } else {
+            for (int64_t k = 0; k < r; ++k) emit(g + k * hp.gbs, c + k * hp.cbs, cb, 1, 0, 0);
+          }
+        }
+      }
+    }
+    i += r;
+  }
+
+  // SM budget -> persistent grid.
+  if (!hp.sm_gpu.empty()) {
+    ThreadDeviceCtx *ctx = nullptr;
+    if (int rc = get_ctx(device, &ctx)) return rc;
+    int sms = d.transfer_sms;
+    if (sms <= 0) sms = env_int("FKV_TRANSFER_SMS", kDefaultSms);
+    sms = std::min(sms, ctx->num_sms);
+    hp.unroll_idx = unroll_index(env_int("FKV_UNROLL", 8));
+    int occ = 1;
+    if (int rc = ctas_per_sm(device, hp.h2d, hp.unroll_idx, &occ)) return rc;
+    const int64_t chunks = L * KV * (int64_t)hp.sm_gpu.size();
+    const int64_t warps_per_cta = kThreads / 32;
+    int64_t grid = (int64_t)sms * occ;
+    grid = std::min<int64_t>(grid, (chunks + warps_per_cta - 1) / warps_per_cta);
+    hp.grid = (int)std::max<int64_t>(grid, 1);
+  }
+  hp.num_ce_streams = d.num_ce_streams > 0 ? d.num_ce_streams : env_int("FKV_CE_STREAMS", kDefaultCeStreams);
+  hp.num_ce_streams = std::max(1, std::min(hp.num_ce_streams, 8));
+  return FKV_OK;
+}
+
+// Device table layout: [layer_ptrs L][gpu_ids n][cpu_ids n] (int64 words).
+size_t table_bytes(const HostPlan &hp) {
+  return 8 * ((size_t)hp.num_layers + 2 * hp.sm_gpu.size());
+}
+
+void fill_table(const HostPlan &hp, const fkv_transfer_desc &d, int64_t *t) {
+  const size_t L = hp.num_layers, n = hp.sm_gpu.size();
+  for (size_t l = 0; l < L; ++l) t[l] = (int64_t)(uintptr_t)d.gpu_layer_ptrs[l];
+  std::memcpy(t + L, hp.sm_gpu.data(), n * 8);
+  std::memcpy(t + L + n, hp.sm_cpu.data(), n * 8);
+}
+
+CopyParams make_params(const HostPlan &hp, char *dev_table) {
+  CopyParams p{};
+  const size_t L = hp.num_layers, n = hp.sm_gpu.size();
+  int64_t *t = reinterpret_cast<int64_t *>(dev_table);
+  p.layer_ptrs = reinterpret_cast<char *const *>(t);
+  p.gpu_ids = t + L;
+  p.cpu_ids = t + L + n;
+  p.cpu_base = hp.cpu_dev_base;
+  p.gpu_kv_stride = hp.gkv;
+  p.gpu_block_stride = hp.gbs;
+  p.cpu_layer_stride = hp.cls;
+  p.cpu_kv_stride = hp.ckv;
+  p.cpu_block_stride = hp.cbs;
+  p.n_vec = hp.copy_bytes / 16;
+  p.n = (uint32_t)n;
+  p.per_layer = (uint32_t)(hp.kv_dim * n);
+  p.num_chunks = (uint32_t)(L * hp.kv_dim * n);
+  return p;
+}
+
+int launch_copy(bool h2d, int uidx, int grid, const CopyParams &p, cudaStream_t s) {
+  if (h2d) {
+    switch (uidx) {
+      case 0: kv_copy_kernel<true, 4><<<grid, kThreads, 0, s>>>(p); break;
+      case 1: kv_copy_kernel<true, 8><<<grid, kThreads, 0, s>>>(p); break;
+      default: kv_copy_kernel<true, 16><<<grid, kThreads, 0, s>>>(p); break;
+    }
+  } else {
+    switch (uidx) {
+      case 0: kv_copy_kernel<false, 4><<<grid, kThreads, 0, s>>>(p); break;
+      case 1: kv_copy_kernel<false, 8><<<grid, kThreads, 0, s>>>(p); break;
+      default: kv_copy_kernel<false, 16><<<grid, kThreads, 0, s>>>(p); break;
+    }
+  }
+  FKV_CUDA(cudaGetLastError());
+  note_launch();
+  return FKV_OK;
+}
+
+int issue_ce(ThreadDeviceCtx *ctx, const std::vector<CeCopy> &ce, int nstreams,
+             bool h2d, cudaStream_t s) {
+  if (ce.empty()) return FKV_OK;
+  if (int rc = ensure_side_streams(ctx, nstreams)) return rc;
+  FKV_CUDA(cudaEventRecord(ctx->fork_event, s));
+  for (int k = 0; k < nstreams; ++k) FKV_CUDA(cudaStreamWaitEvent(ctx->side_streams[k], ctx->fork_event, 0));
+  const cudaMemcpyKind kind = h2d ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost;
+  // Contiguous blocks of descriptors per stream keep each engine's
+  // accesses sequential.
+  const size_t per = (ce.size() + nstreams - 1) / nstreams;
+  for (size_t j = 0; j < ce.size(); ++j) {
+    const CeCopy &x = ce[j];
+    cudaStream_t ss = ctx->side_streams[std::min<size_t>(j / per, nstreams - 1)];
+    if (x.height <= 1) {
+      FKV_CUDA(cudaMemcpyAsync(x.dst, x.src, x.width, kind, ss));
+    } else {
+      FKV_CUDA(cudaMemcpy2DAsync(x.dst, x.dpitch, x.src, x.spitch, x.width, x.height, kind, ss));
+    }
+  }
+  for (int k = 0; k < nstreams; ++k) {
+    FKV_CUDA(cudaEventRecord(ctx->join_events[k], ctx->side_streams[k]));
+    FKV_CUDA(cudaStreamWaitEvent(s, ctx->join_events[k], 0));
+  }
+  return FKV_OK;
+}
+
+int current_device(int *dev) {
+  FKV_CUDA(cudaGetDevice(dev));
+  return FKV_OK;
+}
+
+}  // namespace
+}  // namespace fkv
+
+using namespace fkv;
+
+extern "C" {
+
+void fkv_transfer_desc_init(fkv_transfer_desc *d) {
+  std::memset(d, 0, sizeof(*d));
+  d->transfer_sms = -1;
+  d->synchronous = 1;
+  d->ce_min_run_bytes = -1;
+  d->num_ce_streams = 0;
+  d->is_host_to_device = 1;
+}
+
+int64_t fkv_coalesce_runs(const int64_t *g, const int64_t *c, int64_t n, int64_t *out,
+                          int64_t max_runs) {
+  int64_t runs = 0, i = 0;
+  while (i < n) {
+    int64_t r = 1;
+    while (i + r < n && g[i + r] == g[i] + r && c[i + r] == c[i] + r) ++r;
+    if (runs >= max_runs) return -1;
+    out[3 * runs] = g[i];
+    out[3 * runs + 1] = c[i];
+    out[3 * runs + 2] = r;
+    ++runs;
+    i += r;
+  }
+  return runs;
+}
+
+int fkv_transfer_kv_blocks_ex(const fkv_transfer_desc *d, void *stream_) {
+  clear_error();
+  if (!d) return fail(FKV_ERR_INVALID_ARG, "null descriptor");
+  if (int rc = validate_desc(*d)) return rc;
+  if (d->num_blocks == 0 || d->num_layers == 0 || d->chunk_size_in_bytes < 16) return FKV_OK;
+  cudaStream_t s = (cudaStream_t)stream_;
+  int device = 0;
+  if (int rc = current_device(&device)) return rc;
+  HostPlan hp;
+  if (int rc = build_host_plan(*d, device, hp)) return rc;
+  ThreadDeviceCtx *ctx = nullptr;
+  if (int rc = get_ctx(device, &ctx)) return rc;
+
+  char *dev_table = nullptr;
+  if (!hp.sm_gpu.empty()) {
+    const size_t tb = table_bytes(hp);
+    char *stage = nullptr;
+    if (int rc = acquire_staging(ctx, tb, &stage)) return rc;
+    fill_table(hp, *d, reinterpret_cast<int64_t *>(stage));
+    FKV_CUDA(cudaMallocAsync((void **)&dev_table, tb, s));
+    FKV_CUDA(cudaMemcpyAsync(dev_table, stage, tb, cudaMemcpyHostToDevice, s));
+    if (int rc = release_staging(ctx, s)) return rc;
+    CopyParams p = make_params(hp, dev_table);
+    if (int rc = launch_copy(hp.h2d, hp.unroll_idx, hp.grid, p, s)) {
+      cudaFreeAsync(dev_table, s);
+      return rc;
+    }
+  }
+  int rc = issue_ce(ctx, hp.ce, hp.num_ce_streams, hp.h2d, s);
+  if (dev_table) {
+    cudaError_t e = cudaFreeAsync(dev_table, s);
+    if (rc == FKV_OK && e != cudaSuccess) rc = fail_cuda(e, "cudaFreeAsync");
+  }
+  if (rc != FKV_OK) return rc;
+  if (d->synchronous) FKV_CUDA(cudaStreamSynchronize(s));  // transfer.cu:131
+  return FKV_OK;
+}
+
+int fkv_transfer_kv_blocks(int num_blocks, int start_layer_id, int num_layers,
+                           const int64_t *gpu_block_ids, void *const *gpu_layer_ptrs,
+                           int64_t gpu_kv_stride_in_bytes, int64_t gpu_block_stride_in_bytes,
+                           const int64_t *cpu_block_ids, void *cpu_ptr,
+                           int64_t cpu_kv_stride_in_bytes, int64_t cpu_layer_stride_in_bytes,
+                           int64_t cpu_block_stride_in_bytes, int64_t cpu_startoff_inside_chunks,
+                           int64_t chunk_size_in_bytes, void *stream, int transfer_sms,
+                           int is_host_to_device, int use_ce_transfer, int is_mla) {
+  fkv_transfer_desc d;
+  fkv_transfer_desc_init(&d);
+  d.num_blocks = num_blocks;
+  d.start_layer_id = start_layer_id;
+  d.num_layers = num_layers;
+  d.gpu_block_ids = gpu_block_ids;
+  d.gpu_layer_ptrs = gpu_layer_ptrs;
+  d.gpu_kv_stride_in_bytes = gpu_kv_stride_in_bytes;
+  d.gpu_block_stride_in_bytes = gpu_block_stride_in_bytes;
+  d.cpu_block_ids = cpu_block_ids;
+  d.cpu_ptr = cpu_ptr;
+  d.cpu_kv_stride_in_bytes = cpu_kv_stride_in_bytes;
+  d.cpu_layer_stride_in_bytes = cpu_layer_stride_in_bytes;
+  d.cpu_block_stride_in_bytes = cpu_block_stride_in_bytes;
+  d.cpu_startoff_inside_chunks = cpu_startoff_inside_chunks;
+  d.chunk_size_in_bytes = chunk_size_in_bytes;
+  d.transfer_sms = transfer_sms;
+  d.is_host_to_device = is_host_to_device;
+  d.use_ce_transfer = use_ce_transfer;
+  d.is_mla = is_mla;
+  return fkv_transfer_kv_blocks_ex(&d, stream);
+}
+
+int fkv_plan_create(const fkv_transfer_desc *d, int device, fkv_plan **out) {
+  clear_error();
+  if (!d || !out) return fail(FKV_ERR_INVALID_ARG, "null descriptor or output");
+  *out = nullptr;
+  if (int rc = validate_desc(*d)) return rc;
+  int prev = 0;
+  if (int rc = current_device(&prev)) return rc;
+  if (device < 0) device = prev;
+  if (device != prev) FKV_CUDA(cudaSetDevice(device));
+  HostPlan hp;
+  int rc = build_host_plan(*d, device, hp);
+  fkv_plan *p = nullptr;
+  if (rc == FKV_OK) {
+    p = new fkv_plan();
+    p->device = device;
+    p->h2d = hp.h2d;
+    p->grid = hp.grid;
+    p->unroll_idx = hp.unroll_idx;
+    p->ce = std::move(hp.ce);
+    p->num_ce_streams = hp.num_ce_streams;
+    p->ce_bytes = hp.ce_bytes;
+    p->sm_chunks = (int64_t)hp.num_layers * hp.kv_dim * (int64_t)hp.sm_gpu.size();
+    p->sm_bytes = p->sm_chunks * hp.copy_bytes;
+    if (!hp.sm_gpu.empty()) {
+      const size_t tb = table_bytes(hp);
+      std::vector<int64_t> host(tb / 8);
+      fill_table(hp, *d, host.data());
+      cudaError_t e = cudaMalloc((void **)&p->dev_buf, tb);
+      if (e == cudaSuccess) e = cudaMemcpy(p->dev_buf, host.data(), tb, cudaMemcpyHostToDevice);
+      if (e != cudaSuccess) {
+        rc = fail_cuda(e, "plan table upload");
+      } else {
+        p->params = make_params(hp, p->dev_buf);
+      }
+    }
+    if (rc != FKV_OK) {
+      if (p->dev_buf) cudaFree(p->dev_buf);
+      delete p;
+      p = nullptr;
+    }
+  }
+  if (device != prev) cudaSetDevice(prev);
+  *out = p;
+  return rc;
+}
+
+int fkv_plan_execute_ex(fkv_plan *p, void *stream_, void *ev_start, void *ev_end) {
+  clear_error();
+  if (!p) return fail(FKV_ERR_INVALID_ARG, "null plan");
+  cudaStream_t s = (cudaStream_t)stream_;
+  int prev = 0;
+  if (int rc = current_device(&prev)) return rc;
+  if (prev != p->device) FKV_CUDA(cudaSetDevice(p->device));
+  ThreadDeviceCtx *ctx = nullptr;
+  int rc = get_ctx(p->device, &ctx);
+  if (rc == FKV_OK && ev_start) {
+    cudaError_t e = cudaEventRecord((cudaEvent_t)ev_start, s);
+    if (e != cudaSuccess) rc = fail_cuda(e, "cudaEventRecord");
+  }
+  if (rc == FKV_OK && p->sm_chunks > 0) rc = launch_copy(p->h2d, p->unroll_idx, p->grid, p->params, s);
+  if (rc == FKV_OK && ev_end) {
+    cudaError_t e = cudaEventRecord((cudaEvent_t)ev_end, s);
+    if (e != cudaSuccess) rc = fail_cuda(e, "cudaEventRecord");
+  }
+  if (rc == FKV_OK) rc = issue_ce(ctx, p->ce, p->num_ce_streams, p->h2d, s);
+  if (prev != p->device) cudaSetDevice(prev);
+  return rc;
+}
+
+int fkv_plan_execute(fkv_plan *p, void *stream_) {
+  return fkv_plan_execute_ex(p, stream_, nullptr, nullptr);
+}
+
+int fkv_plan_stats(const fkv_plan *p, int64_t *sm_chunks, int64_t *ce_copies, int64_t *ce_bytes,
+                   int64_t *sm_bytes) {
+  if (!p) return fail(FKV_ERR_INVALID_ARG, "null plan");
+  if (sm_chunks) *sm_chunks = p->sm_chunks;
+  if (ce_copies) *ce_copies = (int64_t)p->ce.size();
+  if (ce_bytes) *ce_bytes = p->ce_bytes;
+  if (sm_bytes) *sm_bytes = p->sm_bytes;
+  return FKV_OK;
+}
+
+void fkv_plan_destroy(fkv_plan *p) {
+  if (!p) return;
+  if (p->dev_buf) cudaFree(p->dev_buf);
+  delete p;
+}
+
+}  // extern "C"

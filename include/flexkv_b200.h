@@ -1,0 +1,218 @@
+/*
+ * flexkv_b200 — C ABI of the B200-native FlexKV transfer data plane.
+ *
+ * Plain pointers, sizes and status codes; no torch types.  Every entry
+ * point returns FKV_OK (0) or a positive FKV_ERR_* code; the message of the
+ * last failure on the calling thread is returned by fkv_last_error().
+ *
+ * Reference interfaces replaced (paths inside linhu-nv/FlexKV):
+ *   fkv_transfer_kv_blocks      <- flexkv::transfer_kv_blocks
+ *                                  csrc/transfer.cuh:23-30, csrc/transfer.cu:63-132
+ *                                  (called through csrc/bindings.cpp:25-55)
+ *   fkv_tp_group_*              <- flexkv::TPTransferThreadGroup
+ *                                  csrc/tp_transfer_thread_group.h:30-57,
+ *                                  csrc/tp_transfer_thread_group.cpp:23-109
+ *   fkv_hasher_*, fkv_gen_hashes, fkv_get_hash_size
+ *                               <- flexkv::Hasher / gen_hashes / get_hash_size
+ *                                  csrc/cache_utils.h:10-28, csrc/hash.cpp:15-66
+ *   fkv_host_register           <- cudaHostRegister helper, flexkv/transfer/worker.py:35-47
+ *
+ * Byte-layout contract (identical to the reference kernel, transfer.cu:39-59):
+ *   for layer l in [0,L), kv in [0,kv_dim), i in [0,N):
+ *     cpu = cpu_ptr + (l+start_layer_id)*cpu_layer_stride + kv*cpu_kv_stride
+ *                   + cpu_block_ids[i]*cpu_block_stride + cpu_startoff
+ *     gpu = gpu_layer_ptrs[l] + kv*gpu_kv_stride + gpu_block_ids[i]*gpu_block_stride
+ *     copy 16*floor(chunk/16) bytes, direction by is_host_to_device.
+ *   Strides and the start offset are truncated to multiples of 8 bytes, as
+ *   the reference's int64-unit conversion does (transfer.cu:84-93).
+ */
+#ifndef FLEXKV_B200_H_
+#define FLEXKV_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define FKV_OK 0
+#define FKV_ERR_INVALID_ARG 1  /* bad shape/size/flag combination           */
+#define FKV_ERR_OUT_OF_RANGE 2 /* a block id addresses outside a pool       */
+#define FKV_ERR_MISALIGNED 3   /* a chunk address is not 16-byte aligned    */
+#define FKV_ERR_CUDA 4         /* a CUDA runtime call failed                */
+#define FKV_ERR_UNSUPPORTED 5  /* feature not provided by this build        */
+#define FKV_ERR_TIMEOUT 6      /* a bounded wait ran out                    */
+
+/* Message of the last failure on this thread ("" if none). */
+const char *fkv_last_error(void);
+/* Library version string. */
+const char *fkv_version(void);
+/* Number of CUDA kernels this library launched so far (all threads). */
+uint64_t fkv_kernel_launch_count(void);
+
+/* ---- host pool registration (worker.py:35-47) -------------------------- */
+/* Page-lock [ptr, ptr+bytes) for zero-copy device access (Portable|Mapped).
+ * advise_hugepages != 0 first asks the kernel for transparent huge pages on
+ * the range (only effective before the pages are first touched). */
+int fkv_host_register(void *ptr, int64_t bytes, int advise_hugepages);
+int fkv_host_unregister(void *ptr);
+
+/* ---- KV block gather/scatter ------------------------------------------ */
+
+/* Drop-in for flexkv::transfer_kv_blocks (transfer.cu:63-132).
+ * gpu_block_ids / cpu_block_ids / gpu_layer_ptrs are HOST arrays (pinned or
+ * pageable); cpu_ptr is a page-locked host pool; stream is a cudaStream_t
+ * (NULL = legacy default stream).  transfer_sms = -1 picks the default SM
+ * budget.  use_ce_transfer != 0 routes every chunk through the copy engines
+ * (coalesced into runs); otherwise long contiguous runs go to the copy
+ * engines and the rest to the SM copy kernel.  Synchronous on return, like
+ * the reference (transfer.cu:131).  Unlike the reference it validates
+ * alignment and (when the pool sizes are known, see _ex) bounds on the host
+ * and returns an error instead of faulting. */
+int fkv_transfer_kv_blocks(int num_blocks, int start_layer_id, int num_layers,
+                           const int64_t *gpu_block_ids,
+                           void *const *gpu_layer_ptrs,
+                           int64_t gpu_kv_stride_in_bytes,
+                           int64_t gpu_block_stride_in_bytes,
+                           const int64_t *cpu_block_ids, void *cpu_ptr,
+                           int64_t cpu_kv_stride_in_bytes,
+                           int64_t cpu_layer_stride_in_bytes,
+                           int64_t cpu_block_stride_in_bytes,
+                           int64_t cpu_startoff_inside_chunks,
+                           int64_t chunk_size_in_bytes, void *stream,
+                           int transfer_sms, int is_host_to_device,
+                           int use_ce_transfer, int is_mla);
+
+/* Full descriptor of one transfer (superset of the reference arguments). */
+typedef struct fkv_transfer_desc {
+  int num_blocks;
+  int start_layer_id;
+  int num_layers;
+  int is_host_to_device;
+  int is_mla;
+  int transfer_sms;       /* -1 = default                                  */
+  int use_ce_transfer;    /* 1 = copy engines only                         */
+  int synchronous;        /* 1 = stream-synchronize before returning       */
+  const int64_t *gpu_block_ids;
+  const int64_t *cpu_block_ids;
+  void *const *gpu_layer_ptrs;
+  void *cpu_ptr;
+  int64_t gpu_kv_stride_in_bytes;
+  int64_t gpu_block_stride_in_bytes;
+  int64_t cpu_kv_stride_in_bytes;
+  int64_t cpu_layer_stride_in_bytes;
+  int64_t cpu_block_stride_in_bytes;
+  int64_t cpu_startoff_inside_chunks;
+  int64_t chunk_size_in_bytes;
+  int64_t cpu_pool_bytes;    /* >0: bounds-check every CPU chunk           */
+  int64_t gpu_layer_bytes;   /* >0: bounds-check every GPU chunk per layer */
+  int64_t ce_min_run_bytes;  /* <0 default; 0 = SM kernel only; else runs
+                                whose per-(layer,kv) span reaches this many
+                                bytes go to the copy engines              */
+  int num_ce_streams;        /* <=0 default                               */
+  int reserved;
+} fkv_transfer_desc;
+
+/* Zero-fill *d and set the defaults (transfer_sms=-1, synchronous=1,
+ * ce_min_run_bytes=-1, num_ce_streams=0). */
+void fkv_transfer_desc_init(fkv_transfer_desc *d);
+
+int fkv_transfer_kv_blocks_ex(const fkv_transfer_desc *d, void *stream);
+
+/* Two-phase form: plan once (validate, coalesce runs, upload ids to the
+ * device), execute many times.  Execute is asynchronous on the stream and
+ * launches the SM kernel plus the copy-engine copies of the plan. */
+typedef struct fkv_plan fkv_plan;
+int fkv_plan_create(const fkv_transfer_desc *d, int device, fkv_plan **out);
+int fkv_plan_execute(fkv_plan *plan, void *stream);
+/* As fkv_plan_execute; when non-NULL, the cudaEvent_t handles are recorded
+ * on `stream` immediately before and after the SM copy kernel (both at the
+ * same point when the plan has no SM chunks), so the kernel can be timed
+ * apart from the overlapping copy-engine work. */
+int fkv_plan_execute_ex(fkv_plan *plan, void *stream, void *kernel_start_event,
+                        void *kernel_end_event);
+/* Number of SM-kernel chunks and copy-engine copies in the plan. */
+int fkv_plan_stats(const fkv_plan *plan, int64_t *sm_chunks,
+                   int64_t *ce_copies, int64_t *ce_bytes, int64_t *sm_bytes);
+void fkv_plan_destroy(fkv_plan *plan);
+
+/* Host-side run coalescing (pure host logic, no CUDA): writes up to
+ * max_runs triples (gpu_start, cpu_start, length) of maximal runs where
+ * both ids advance by one, returns the run count (or -1 when max_runs is
+ * too small). */
+int64_t fkv_coalesce_runs(const int64_t *gpu_block_ids,
+                          const int64_t *cpu_block_ids, int64_t num_blocks,
+                          int64_t *runs_out, int64_t max_runs);
+
+/* ---- tensor-parallel group (tp_transfer_thread_group.cpp) -------------- */
+typedef struct fkv_tp_group fkv_tp_group;
+
+/* gpu_layer_ptrs is rank-major [num_gpus][num_layers]; device_ids[i] is the
+ * CUDA device of rank i (the reference uses dp_group_id*num_gpus+i,
+ * tp_transfer_thread_group.cpp:41,81).  One persistent host thread and one
+ * stream per rank. cpu_pool_bytes > 0 enables CPU bounds checks. */
+int fkv_tp_group_create(int num_gpus, int dp_group_id, const int *device_ids,
+                        void *const *gpu_layer_ptrs, int num_layers,
+                        void *cpu_ptr, int64_t cpu_pool_bytes,
+                        fkv_tp_group **out);
+/* Same arguments as TPTransferThreadGroup::tp_group_transfer
+ * (tp_transfer_thread_group.cpp:48-59).  Rank i moves its gpu_chunk bytes to
+ * CPU offset i*gpu_chunk inside each CPU chunk (0 for MLA).  Layer pointers
+ * of rank i are gpu_layer_ptrs[i*num_layers + layer_id + l]. */
+int fkv_tp_group_transfer(fkv_tp_group *g, const int64_t *gpu_block_ids,
+                          const int64_t *cpu_block_ids, int num_blocks,
+                          int64_t gpu_kv_stride_in_bytes,
+                          int64_t gpu_block_stride_in_bytes,
+                          int64_t gpu_chunk_size_in_bytes,
+                          int64_t cpu_kv_stride_in_bytes,
+                          int64_t cpu_layer_stride_in_bytes,
+                          int64_t cpu_block_stride_in_bytes,
+                          int64_t cpu_chunk_size_in_bytes, int transfer_sms,
+                          int is_host_to_device, int use_ce_transfer,
+                          int layer_id, int layer_granularity, int is_mla);
+int fkv_tp_group_num_gpus(const fkv_tp_group *g);
+void fkv_tp_group_destroy(fkv_tp_group *g);
+
+/* ---- XXH64 block hashing (hash.cpp) ------------------------------------ */
+typedef struct fkv_hasher fkv_hasher;
+
+/* sizeof(XXH64 digest) = 8 (hash.cpp:15). */
+int fkv_get_hash_size(void);
+
+/* A streaming XXH64 (seed 0) whose state lives in device memory of
+ * `device`; all mixing arithmetic runs in CUDA kernels. */
+int fkv_hasher_create(int device, fkv_hasher **out);
+void fkv_hasher_destroy(fkv_hasher *h);
+int fkv_hasher_reset(fkv_hasher *h, void *stream);
+/* data may be host or device memory; returns after the state is updated. */
+int fkv_hasher_update(fkv_hasher *h, const void *data, int64_t size,
+                      void *stream);
+int fkv_hasher_digest(fkv_hasher *h, uint64_t *out, void *stream);
+
+/* gen_hashes (hash.cpp:47-66): for block b, update the hasher with tokens
+ * [b*tpb,(b+1)*tpb) (int64) and store digest() — the XXH64 of the running
+ * prefix — into block_hashes[b].  token_ids / block_hashes may each be
+ * host or device memory.  The hasher keeps the state after the last block.
+ * num_blocks must equal num_tokens / tokens_per_block. */
+int fkv_gen_hashes(fkv_hasher *h, const int64_t *token_ids, int64_t num_tokens,
+                   int tokens_per_block, uint64_t *block_hashes,
+                   int64_t num_blocks, void *stream);
+
+/* Batched gen_hashes over independent sequences, each with a fresh seed-0
+ * hasher: sequence s owns tokens [seq_offsets[s], seq_offsets[s+1]) and
+ * writes floor(len_s/tpb) digests starting at block_hashes[block_offset_s],
+ * block_offset_s being the running sum of the previous sequences' counts.
+ * seq_offsets is a host array of num_seqs+1 entries; token_ids and
+ * block_hashes may be host or device memory. */
+int fkv_gen_hashes_batched(const int64_t *token_ids,
+                           const int64_t *seq_offsets, int num_seqs,
+                           int tokens_per_block, uint64_t *block_hashes,
+                           void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLEXKV_B200_H_ */

@@ -1,0 +1,143 @@
+"""TEST INFRASTRUCTURE ONLY — ctypes wrapper of the CPU oracle (oracle.c)
+and of the reference's own transfer.cu built into oracle/_ref.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline and
+reference legs use this module, as the checker or the baseline.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from typing import List, Optional, Sequence
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "_build", "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libref_transfer.so")
+
+_c_i64 = ctypes.c_int64
+_c_int = ctypes.c_int
+_vp = ctypes.c_void_p
+
+
+def build(with_reference: bool = True) -> None:
+    """Build liboracle.so (and the reference transfer.cu when its tree is
+    present).  Outputs stay under oracle/_build and oracle/_ref."""
+    target = "all" if with_reference else "_build/liboracle.so"
+    subprocess.run(["make", "-s", "-C", HERE, target], check=True)
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(ORACLE_SO):
+            build(with_reference=False)
+        L = ctypes.CDLL(ORACLE_SO)
+        L.oracle_transfer_kv_blocks.restype = _c_int
+        L.oracle_transfer_kv_blocks.argtypes = [
+            _c_int, _c_int, _c_int, _vp, _vp, _c_i64, _c_i64, _vp, _vp, _c_i64, _c_i64, _c_i64,
+            _c_i64, _c_i64, _c_int, _c_int, _c_int]
+        L.oracle_xxh64_state_size.restype = ctypes.c_size_t
+        L.oracle_xxh64_reset.argtypes = [_vp, ctypes.c_uint64]
+        L.oracle_xxh64_update.argtypes = [_vp, _vp, ctypes.c_size_t]
+        L.oracle_xxh64_digest.restype = ctypes.c_uint64
+        L.oracle_xxh64_digest.argtypes = [_vp]
+        L.oracle_xxh64.restype = ctypes.c_uint64
+        L.oracle_xxh64.argtypes = [_vp, ctypes.c_size_t, ctypes.c_uint64]
+        L.oracle_gen_hashes.argtypes = [_vp, _vp, _c_int, _vp, _c_i64]
+        L.oracle_gen_hashes_batched.argtypes = [_vp, _vp, _c_int, _c_int, _vp]
+        _lib = L
+    return _lib
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def transfer(num_blocks: int, start_layer_id: int, gpu_block_ids: np.ndarray,
+             gpu_layers: Sequence[np.ndarray], gpu_kv_stride: int, gpu_block_stride: int,
+             cpu_block_ids: np.ndarray, cpu_pool: np.ndarray, cpu_kv_stride: int,
+             cpu_layer_stride: int, cpu_block_stride: int, cpu_startoff: int, chunk: int,
+             is_host_to_device: bool, is_mla: bool, num_threads: int = 1) -> None:
+    """Run the reference copy semantics on host arrays in place.  gpu_layers
+    are byte images (uint8 arrays) of the per-layer GPU tensors."""
+    g = np.ascontiguousarray(gpu_block_ids, dtype=np.int64)
+    c = np.ascontiguousarray(cpu_block_ids, dtype=np.int64)
+    ptrs = np.array([_ptr(x) for x in gpu_layers], dtype=np.uint64)
+    lib().oracle_transfer_kv_blocks(
+        int(num_blocks), int(start_layer_id), len(gpu_layers), _ptr(g), _ptr(ptrs),
+        int(gpu_kv_stride), int(gpu_block_stride), _ptr(c), _ptr(cpu_pool), int(cpu_kv_stride),
+        int(cpu_layer_stride), int(cpu_block_stride), int(cpu_startoff), int(chunk),
+        int(bool(is_host_to_device)), int(bool(is_mla)), int(num_threads))
+
+
+class XXH64:
+    """Streaming XXH64 oracle."""
+
+    def __init__(self, seed: int = 0):
+        self._st = ctypes.create_string_buffer(int(lib().oracle_xxh64_state_size()))
+        lib().oracle_xxh64_reset(self._st, seed)
+
+    def update(self, data: bytes | np.ndarray) -> "XXH64":
+        b = np.frombuffer(bytes(data), dtype=np.uint8) if isinstance(data, (bytes, bytearray)) \
+            else np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+        lib().oracle_xxh64_update(self._st, _ptr(b) if b.size else None, b.size)
+        return self
+
+    def digest(self) -> int:
+        return int(lib().oracle_xxh64_digest(self._st))
+
+    def gen_hashes(self, token_ids: np.ndarray, tokens_per_block: int) -> np.ndarray:
+        t = np.ascontiguousarray(token_ids, dtype=np.int64)
+        nb = t.size // tokens_per_block
+        out = np.zeros(nb, dtype=np.uint64)
+        if nb:
+            lib().oracle_gen_hashes(self._st, _ptr(t), int(tokens_per_block), _ptr(out), nb)
+        return out
+
+
+def xxh64(data: bytes | np.ndarray, seed: int = 0) -> int:
+    return XXH64(seed).update(data).digest()
+
+
+def gen_hashes(token_ids: np.ndarray, tokens_per_block: int) -> np.ndarray:
+    return XXH64(0).gen_hashes(token_ids, tokens_per_block)
+
+
+def gen_hashes_batched(token_ids: np.ndarray, seq_offsets: Sequence[int],
+                       tokens_per_block: int) -> np.ndarray:
+    t = np.ascontiguousarray(token_ids, dtype=np.int64)
+    offs = np.ascontiguousarray(seq_offsets, dtype=np.int64)
+    n = offs.size - 1
+    total = int(sum((offs[i + 1] - offs[i]) // tokens_per_block for i in range(n)))
+    out = np.zeros(max(total, 1), dtype=np.uint64)
+    lib().oracle_gen_hashes_batched(_ptr(t), _ptr(offs), n, int(tokens_per_block), _ptr(out))
+    return out[:total]
+
+
+# ---- the reference's own transfer.cu (GPU), built by oracle/Makefile ------
+
+_ref = None
+
+
+def reference_available() -> bool:
+    return os.path.exists(REF_SO)
+
+
+def ref_lib() -> ctypes.CDLL:
+    global _ref
+    if _ref is None:
+        if not reference_available():
+            raise FileNotFoundError(f"{REF_SO} not built (needs the reference tree at build time)")
+        L = ctypes.CDLL(REF_SO)
+        L.ref_transfer_kv_blocks.restype = _c_int
+        L.ref_transfer_kv_blocks.argtypes = [
+            _c_int, _c_int, _c_int, _vp, _vp, _c_i64, _c_i64, _vp, _vp, _c_i64, _c_i64, _c_i64,
+            _c_i64, _c_i64, _vp, _c_int, _c_int, _c_int, _c_int]
+        _ref = L
+    return _ref
