@@ -69,16 +69,20 @@ def make_batch(n, gpu_pool, cpu_pool, seed, run_frac, max_run):
         lens.append(r)
         left -= r
     lens += [1] * (n - n_run)
-    nruns = sum(1 for r in lens if r > 1)
 
     def starts(pool):
-        slots = rng.permutation(pool // max_run)[:nruns]
-        used = np.zeros(pool, dtype=bool)
-        for s in slots:
-            used[s * max_run:(s + 1) * max_run] = True
-        singles = rng.choice(np.flatnonzero(~used), size=len(lens) - nruns, replace=False)
-        its, iss = iter(slots), iter(singles)
-        return [int(next(its)) * max_run if r > 1 else int(next(iss)) for r in lens]
+        # Segments in a random order, separated by random gaps sharing the
+        # pool's free space: disjoint, and spread over the whole pool.
+        assert n <= pool, "pool smaller than the batch"
+        cuts = np.sort(rng.integers(0, pool - n + 1, len(lens)))
+        gaps = np.diff(np.concatenate([[0], cuts]))
+        st = [0] * len(lens)
+        pos = 0
+        for j, idx in enumerate(rng.permutation(len(lens))):
+            pos += int(gaps[j])
+            st[idx] = pos
+            pos += lens[idx]
+        return st
 
     gs, cs = starts(gpu_pool), starts(cpu_pool)
     g, c = [], []
@@ -277,6 +281,10 @@ def run_ours(args, ws, rank, local, cfg):
     for k in range(W):
         step(k)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(K)]
+    for row in evs:  # torch creates the CUDA event on first record
+        for e in row:
+            e.record(stream)
+    torch.cuda.synchronize()
     sampler = ClockSampler(local)
     with sampler:
         barrier(ws)

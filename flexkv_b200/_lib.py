@@ -55,7 +55,7 @@ class TransferDesc(ctypes.Structure):
         ("gpu_layer_bytes", c_i64),
         ("ce_min_run_bytes", c_i64),
         ("num_ce_streams", c_int),
-        ("reserved", c_int),
+        ("ce_schedule", c_int),
     ]
 
 

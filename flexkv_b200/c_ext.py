@@ -19,8 +19,8 @@ Differences a caller can observe, all on inputs the reference mishandles:
     tensor device instead of dp_group_id*num_gpus+i, and indexes rank i's
     layer pointers with the full layer count (tp_transfer_thread_group.cpp
     :70,77 use layer_granularity; identical for full-layer ops).
-Extra keyword-only options (ce_min_run_bytes, synchronous, gpu_layer_bytes)
-default to the reference behaviour.
+Extra keyword-only options (ce_min_run_bytes, ce_schedule, synchronous,
+gpu_layer_bytes) default to the reference behaviour.
 """
 from __future__ import annotations
 
@@ -81,7 +81,7 @@ def _fill_desc(d: TransferDesc, gpu_ids: torch.Tensor, cpu_ids: torch.Tensor,
                chunk_size_in_bytes: int, start_layer_id: int, transfer_sms: int,
                is_host_to_device: bool, use_ce_transfer: bool, is_mla: bool,
                ce_min_run_bytes: Optional[int], synchronous: bool, gpu_layer_bytes: int,
-               cpu_startoff_inside_chunks: int = 0) -> None:
+               cpu_startoff_inside_chunks: int = 0, ce_schedule: Optional[int] = None) -> None:
     _lib.load().fkv_transfer_desc_init(ctypes.byref(d))
     if gpu_ids.numel() != cpu_ids.numel():
         raise RuntimeError("gpu and cpu block id tensors differ in length")
@@ -107,6 +107,7 @@ def _fill_desc(d: TransferDesc, gpu_ids: torch.Tensor, cpu_ids: torch.Tensor,
     d.cpu_pool_bytes = _nbytes(cpu_tensor)
     d.gpu_layer_bytes = int(gpu_layer_bytes)
     d.ce_min_run_bytes = -1 if ce_min_run_bytes is None else int(ce_min_run_bytes)
+    d.ce_schedule = -1 if ce_schedule is None else int(ce_schedule)
 
 
 def transfer_kv_blocks(gpu_block_id_tensor: torch.Tensor, gpu_layer_ptrs_tensor: torch.Tensor,
@@ -117,7 +118,8 @@ def transfer_kv_blocks(gpu_block_id_tensor: torch.Tensor, gpu_layer_ptrs_tensor:
                        start_layer_id: int, transfer_sms: int = -1,
                        is_host_to_device: bool = True, use_ce_transfer: bool = False,
                        is_mla: bool = False, *, ce_min_run_bytes: Optional[int] = None,
-                       synchronous: bool = True, gpu_layer_bytes: int = 0) -> None:
+                       synchronous: bool = True, gpu_layer_bytes: int = 0,
+                       ce_schedule: Optional[int] = None) -> None:
     """Move (layer, kv, block) chunks between GPU layers and the host pool
     (bindings.cpp:25-55 -> transfer.cu:63-132) on the current CUDA stream.
     ``gpu_layer_ptrs_tensor`` is an int64 CPU tensor of per-layer device
@@ -133,7 +135,7 @@ def transfer_kv_blocks(gpu_block_id_tensor: torch.Tensor, gpu_layer_ptrs_tensor:
                gpu_block_stride_in_bytes, cpu_kv_stride_in_bytes, cpu_layer_stride_in_bytes,
                cpu_block_stride_in_bytes, chunk_size_in_bytes, start_layer_id, transfer_sms,
                is_host_to_device, use_ce_transfer, is_mla, ce_min_run_bytes, synchronous,
-               gpu_layer_bytes)
+               gpu_layer_bytes, ce_schedule=ce_schedule)
     check(_lib.load().fkv_transfer_kv_blocks_ex(ctypes.byref(d), _stream_handle()),
           "transfer_kv_blocks")
 
@@ -148,7 +150,8 @@ class TransferPlan:
                  cpu_kv_stride_in_bytes, cpu_layer_stride_in_bytes, cpu_block_stride_in_bytes,
                  chunk_size_in_bytes, start_layer_id, transfer_sms=-1, is_host_to_device=True,
                  use_ce_transfer=False, is_mla=False, *, ce_min_run_bytes=None,
-                 gpu_layer_bytes=0, cpu_startoff_inside_chunks=0, device: int = -1):
+                 gpu_layer_bytes=0, cpu_startoff_inside_chunks=0, ce_schedule=None,
+                 device: int = -1):
         self._lib = _lib.load()
         self._handle = None
         gpu_ids = _host_i64(gpu_block_id_tensor, "gpu_block_id_tensor")
@@ -160,7 +163,7 @@ class TransferPlan:
                    gpu_block_stride_in_bytes, cpu_kv_stride_in_bytes, cpu_layer_stride_in_bytes,
                    cpu_block_stride_in_bytes, chunk_size_in_bytes, start_layer_id, transfer_sms,
                    is_host_to_device, use_ce_transfer, is_mla, ce_min_run_bytes, False,
-                   gpu_layer_bytes, cpu_startoff_inside_chunks)
+                   gpu_layer_bytes, cpu_startoff_inside_chunks, ce_schedule)
         h = ctypes.c_void_p()
         check(self._lib.fkv_plan_create(ctypes.byref(d), int(device), ctypes.byref(h)),
               "fkv_plan_create")
@@ -170,12 +173,16 @@ class TransferPlan:
                 kernel_events: Optional[tuple] = None) -> None:
         """Launch the plan on ``stream`` (default: current stream).  With
         ``kernel_events=(start, end)`` (torch.cuda.Event, timing enabled)
-        the events bracket the SM copy kernel alone."""
+        the events bracket the SM copy kernel alone.  torch creates an
+        event's CUDA handle on its first record(), so each event must have
+        been recorded once before it is passed here."""
         s = int(stream.cuda_stream) if stream is not None else _stream_handle()
         if kernel_events is None:
             check(self._lib.fkv_plan_execute(self._handle, s), "fkv_plan_execute")
         else:
             a, b = kernel_events
+            if not a.cuda_event or not b.cuda_event:
+                raise RuntimeError("kernel_events must have been recorded once (no CUDA handle yet)")
             check(self._lib.fkv_plan_execute_ex(self._handle, s, a.cuda_event, b.cuda_event),
                   "fkv_plan_execute_ex")
 

@@ -3,9 +3,12 @@
 
 #include <sys/mman.h>
 
+#include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
+#include <mutex>
 
 namespace fkv {
 
@@ -97,6 +100,53 @@ int release_staging(ThreadDeviceCtx *ctx, cudaStream_t stream) {
   FKV_CUDA(cudaEventRecord(ctx->staging_free, stream));
   ctx->staging_pending = true;
   return FKV_OK;
+}
+
+namespace {
+std::mutex g_pool_mu;
+cudaMemPool_t g_pools[64] = {nullptr};
+}  // namespace
+
+int scratch_alloc(int device, size_t bytes, cudaStream_t s, void **out) {
+  if (device < 0) FKV_CUDA(cudaGetDevice(&device));
+  cudaMemPool_t pool;
+  {
+    std::lock_guard<std::mutex> lk(g_pool_mu);
+    pool = g_pools[device & 63];
+    if (!pool) {
+      cudaMemPoolProps props;
+      std::memset(&props, 0, sizeof(props));
+      props.allocType = cudaMemAllocationTypePinned;
+      props.handleTypes = cudaMemHandleTypeNone;
+      props.location.type = cudaMemLocationTypeDevice;
+      props.location.id = device;
+      FKV_CUDA(cudaMemPoolCreate(&pool, &props));
+      uint64_t keep = UINT64_MAX;
+      FKV_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+      g_pools[device & 63] = pool;
+    }
+  }
+  FKV_CUDA(cudaMallocFromPoolAsync(out, bytes < 256 ? 256 : bytes, pool, s));
+  return FKV_OK;
+}
+
+int scratch_free(void *p, cudaStream_t s) {
+  if (p) FKV_CUDA(cudaFreeAsync(p, s));
+  return FKV_OK;
+}
+
+bool profiling() {
+  static const bool on = [] {
+    const char *e = std::getenv("FKV_PROFILE");
+    return e && *e == '1';
+  }();
+  return on;
+}
+
+double now_us() {
+  return std::chrono::duration<double, std::micro>(
+             std::chrono::steady_clock::now().time_since_epoch())
+      .count();
 }
 
 int pointer_is_device(const void *p, int *is_device, int *device) {

@@ -51,6 +51,14 @@ struct ThreadDeviceCtx {
 
 // Context of the calling thread for `device` (current device if -1).
 int get_ctx(int device, ThreadDeviceCtx **out);
+// Stream-ordered scratch from a library-owned memory pool of `device` that
+// keeps its memory cached (release threshold = max), so per-call
+// allocations never remap physical memory after a synchronize.
+int scratch_alloc(int device, size_t bytes, cudaStream_t s, void **out);
+int scratch_free(void *p, cudaStream_t s);
+// Host-phase timing to stderr when FKV_PROFILE=1 (diagnostics only).
+bool profiling();
+double now_us();
 // Ensure `n` side streams exist in ctx.
 int ensure_side_streams(ThreadDeviceCtx *ctx, int n);
 // Pinned staging buffer of at least `bytes`, safe to overwrite now.

@@ -35,6 +35,7 @@ constexpr int kThreads = 256;          // 8 warps per CTA
 constexpr int kDefaultSms = 16;        // SM budget when transfer_sms == -1
 constexpr int64_t kDefaultCeMinRunBytes = 2ll << 20;  // 2 MiB per (layer,kv) span
 constexpr int kDefaultCeStreams = 2;
+constexpr int kDefaultCeSchedule = 1;  // copy engines first, then the SM kernel
 
 struct CopyParams {
   const int64_t *gpu_ids;     // device [n]
@@ -55,13 +56,22 @@ struct CopyParams {
 // Coherent (not .nc) load on purpose: with .nc the assembler may legally
 // sink each store between the loads (the data is declared read-only), which
 // leaves one load per lane in flight instead of UNROLL — fatal for reads
-// that cross PCIe with microsecond latency.
+// that cross PCIe with microsecond latency.  PF256 adds the L2 256-byte
+// prefetch-size hint (a tuning variant for reads of host memory).
+template <bool PF256>
 __device__ __forceinline__ uint4 ld_stream(const uint4 *p) {
   uint4 r;
-  asm volatile("ld.global.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p)
-               : "memory");
+  if (PF256) {
+    asm volatile("ld.global.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p)
+                 : "memory");
+  } else {
+    asm volatile("ld.global.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p)
+                 : "memory");
+  }
   return r;
 }
 
@@ -73,7 +83,7 @@ __device__ __forceinline__ void st_stream(uint4 *p, const uint4 &v) {
 
 // One warp copies one chunk: lane l moves vectors l, l+32, ...; each pass
 // keeps UNROLL 16-byte loads in flight per lane (UNROLL*512 bytes per warp).
-template <int UNROLL>
+template <int UNROLL, bool PF256>
 __device__ __forceinline__ void copy_chunk(const uint4 *__restrict__ src,
                                            uint4 *__restrict__ dst,
                                            int64_t n_vec, int lane) {
@@ -82,15 +92,15 @@ __device__ __forceinline__ void copy_chunk(const uint4 *__restrict__ src,
   for (; base + kStep <= n_vec; base += kStep) {
     uint4 r[UNROLL];
 #pragma unroll
-    for (int u = 0; u < UNROLL; ++u) r[u] = ld_stream(src + base + u * 32 + lane);
+    for (int u = 0; u < UNROLL; ++u) r[u] = ld_stream<PF256>(src + base + u * 32 + lane);
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) st_stream(dst + base + u * 32 + lane, r[u]);
   }
   // Remainder: fewer than 32*UNROLL vectors.
-  for (int64_t v = base + lane; v < n_vec; v += 32) st_stream(dst + v, ld_stream(src + v));
+  for (int64_t v = base + lane; v < n_vec; v += 32) st_stream(dst + v, ld_stream<PF256>(src + v));
 }
 
-template <bool H2D, int UNROLL>
+template <bool H2D, int UNROLL, bool PF256>
 __global__ void __launch_bounds__(kThreads) kv_copy_kernel(const CopyParams p) {
   const int lane = threadIdx.x & 31;
   const uint32_t warp = (blockIdx.x * kThreads + threadIdx.x) >> 5;
@@ -107,7 +117,7 @@ __global__ void __launch_bounds__(kThreads) kv_copy_kernel(const CopyParams p) {
                 h * p.cpu_block_stride;
     const uint4 *src = reinterpret_cast<const uint4 *>(H2D ? cpu : gpu);
     uint4 *dst = reinterpret_cast<uint4 *>(H2D ? gpu : cpu);
-    copy_chunk<UNROLL>(src, dst, p.n_vec, lane);
+    copy_chunk<UNROLL, PF256>(src, dst, p.n_vec, lane);
   }
 }
 
@@ -126,31 +136,40 @@ int64_t env_i64(const char *name, int64_t dflt) {
   return (s && *s) ? std::atoll(s) : dflt;
 }
 
-// Occupancy (CTAs per SM) of each kernel instantiation, cached per device.
-struct OccCache {
-  std::mutex mu;
-  int max_pitch[64] = {0};
-  int occ[64][2][3] = {{{0}}};
-};
-OccCache g_occ;
-
-int unroll_index(int unroll) { return unroll >= 16 ? 2 : (unroll >= 8 ? 1 : 0); }
+// Kernel variants: index = unroll_idx (0:4, 1:8, 2:16) + 3 * pf256.
+constexpr int kNumVariants = 6;
 
 template <bool H2D>
-const void *kernel_ptr(int unroll_idx) {
-  switch (unroll_idx) {
-    case 0: return (const void *)kv_copy_kernel<H2D, 4>;
-    case 1: return (const void *)kv_copy_kernel<H2D, 8>;
-    default: return (const void *)kv_copy_kernel<H2D, 16>;
+const void *kernel_ptr(int variant) {
+  switch (variant) {
+    case 0: return (const void *)kv_copy_kernel<H2D, 4, false>;
+    case 1: return (const void *)kv_copy_kernel<H2D, 8, false>;
+    case 2: return (const void *)kv_copy_kernel<H2D, 16, false>;
+    case 3: return (const void *)kv_copy_kernel<H2D, 4, true>;
+    case 4: return (const void *)kv_copy_kernel<H2D, 8, true>;
+    default: return (const void *)kv_copy_kernel<H2D, 16, true>;
   }
 }
 
-int ctas_per_sm(int device, bool h2d, int uidx, int *out) {
+int variant_index(int unroll, int pf256) {
+  const int u = unroll >= 16 ? 2 : (unroll >= 8 ? 1 : 0);
+  return u + (pf256 ? 3 : 0);
+}
+
+// Occupancy (CTAs per SM) of each kernel variant, cached per device.
+struct OccCache {
+  std::mutex mu;
+  int max_pitch[64] = {0};
+  int occ[64][2][kNumVariants] = {{{0}}};
+};
+OccCache g_occ;
+
+int ctas_per_sm(int device, bool h2d, int variant, int *out) {
   std::lock_guard<std::mutex> lk(g_occ.mu);
   int d = device & 63;
-  int &v = g_occ.occ[d][h2d ? 1 : 0][uidx];
+  int &v = g_occ.occ[d][h2d ? 1 : 0][variant];
   if (v == 0) {
-    const void *k = h2d ? kernel_ptr<true>(uidx) : kernel_ptr<false>(uidx);
+    const void *k = h2d ? kernel_ptr<true>(variant) : kernel_ptr<false>(variant);
     int n = 0;
     FKV_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kThreads, 0));
     v = std::max(n, 1);
@@ -183,6 +202,7 @@ struct fkv_plan {
   char *dev_buf = nullptr;       // layer ptrs + ids (cudaMalloc, plan-owned)
   std::vector<fkv::CeCopy> ce;
   int num_ce_streams = 0;
+  int ce_schedule = 0;
   int64_t sm_chunks = 0, ce_bytes = 0, sm_bytes = 0;
 };
 
@@ -204,6 +224,7 @@ struct HostPlan {
   int grid = 0;
   int unroll_idx = 1;
   int num_ce_streams = 0;
+  int ce_schedule = 0;
 };
 
 inline int64_t trunc8(int64_t b) { return (b / 8) * 8; }  // transfer.cu:86-93
@@ -352,7 +373,7 @@ int build_host_plan(const fkv_transfer_desc &d, int device, HostPlan &hp) {
     int sms = d.transfer_sms;
     if (sms <= 0) sms = env_int("FKV_TRANSFER_SMS", kDefaultSms);
     sms = std::min(sms, ctx->num_sms);
-    hp.unroll_idx = unroll_index(env_int("FKV_UNROLL", 8));
+    hp.unroll_idx = variant_index(env_int("FKV_UNROLL", 8), env_int("FKV_LD_PF256", 0));
     int occ = 1;
     if (int rc = ctas_per_sm(device, hp.h2d, hp.unroll_idx, &occ)) return rc;
     const int64_t chunks = L * KV * (int64_t)hp.sm_gpu.size();
@@ -363,6 +384,9 @@ int build_host_plan(const fkv_transfer_desc &d, int device, HostPlan &hp) {
   }
   hp.num_ce_streams = d.num_ce_streams > 0 ? d.num_ce_streams : env_int("FKV_CE_STREAMS", kDefaultCeStreams);
   hp.num_ce_streams = std::max(1, std::min(hp.num_ce_streams, 8));
+  hp.ce_schedule = d.ce_schedule >= 0 ? d.ce_schedule : env_int("FKV_CE_SCHEDULE", kDefaultCeSchedule);
+  if (hp.ce_schedule < 0 || hp.ce_schedule > 2)
+    return fail(FKV_ERR_INVALID_ARG, "ce_schedule must be -1 (default), 0, 1 or 2");
   return FKV_OK;
 }
 
@@ -398,34 +422,23 @@ CopyParams make_params(const HostPlan &hp, char *dev_table) {
   return p;
 }
 
-int launch_copy(bool h2d, int uidx, int grid, const CopyParams &p, cudaStream_t s) {
-  if (h2d) {
-    switch (uidx) {
-      case 0: kv_copy_kernel<true, 4><<<grid, kThreads, 0, s>>>(p); break;
-      case 1: kv_copy_kernel<true, 8><<<grid, kThreads, 0, s>>>(p); break;
-      default: kv_copy_kernel<true, 16><<<grid, kThreads, 0, s>>>(p); break;
-    }
-  } else {
-    switch (uidx) {
-      case 0: kv_copy_kernel<false, 4><<<grid, kThreads, 0, s>>>(p); break;
-      case 1: kv_copy_kernel<false, 8><<<grid, kThreads, 0, s>>>(p); break;
-      default: kv_copy_kernel<false, 16><<<grid, kThreads, 0, s>>>(p); break;
-    }
-  }
-  FKV_CUDA(cudaGetLastError());
+int launch_copy(bool h2d, int variant, int grid, const CopyParams &p, cudaStream_t s) {
+  const void *k = h2d ? kernel_ptr<true>(variant) : kernel_ptr<false>(variant);
+  void *args[] = {const_cast<CopyParams *>(&p)};
+  FKV_CUDA(cudaLaunchKernel(k, dim3(grid), dim3(kThreads), args, 0, s));
   note_launch();
   return FKV_OK;
 }
 
-int issue_ce(ThreadDeviceCtx *ctx, const std::vector<CeCopy> &ce, int nstreams,
-             bool h2d, cudaStream_t s) {
-  if (ce.empty()) return FKV_OK;
+// Fork the side streams from `s`, enqueue the copy-engine descriptors on
+// them (contiguous slices per stream keep each engine's accesses
+// sequential) and, when `join`, make `s` wait for all of them.
+int fork_ce(ThreadDeviceCtx *ctx, const std::vector<CeCopy> &ce, int nstreams, bool h2d,
+            cudaStream_t s) {
   if (int rc = ensure_side_streams(ctx, nstreams)) return rc;
   FKV_CUDA(cudaEventRecord(ctx->fork_event, s));
   for (int k = 0; k < nstreams; ++k) FKV_CUDA(cudaStreamWaitEvent(ctx->side_streams[k], ctx->fork_event, 0));
   const cudaMemcpyKind kind = h2d ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost;
-  // Contiguous blocks of descriptors per stream keep each engine's
-  // accesses sequential.
   const size_t per = (ce.size() + nstreams - 1) / nstreams;
   for (size_t j = 0; j < ce.size(); ++j) {
     const CeCopy &x = ce[j];
@@ -436,11 +449,47 @@ int issue_ce(ThreadDeviceCtx *ctx, const std::vector<CeCopy> &ce, int nstreams,
       FKV_CUDA(cudaMemcpy2DAsync(x.dst, x.dpitch, x.src, x.spitch, x.width, x.height, kind, ss));
     }
   }
+  return FKV_OK;
+}
+
+int join_ce(ThreadDeviceCtx *ctx, int nstreams, cudaStream_t s) {
   for (int k = 0; k < nstreams; ++k) {
     FKV_CUDA(cudaEventRecord(ctx->join_events[k], ctx->side_streams[k]));
     FKV_CUDA(cudaStreamWaitEvent(s, ctx->join_events[k], 0));
   }
   return FKV_OK;
+}
+
+// Enqueue one transfer on `s`: the SM kernel (bracketed by the optional
+// events) and the copy-engine descriptors, ordered by `schedule`:
+//   0 — concurrent: copy engines on side streams forked from `s`, joined back;
+//   1 — copy engines first (on side streams, joined), then the kernel;
+//   2 — the kernel first, then the copy engines.
+// A serial order keeps the two kinds of host-link traffic apart.
+int enqueue_transfer(ThreadDeviceCtx *ctx, bool h2d, int variant, int grid, const CopyParams *p,
+                     bool has_sm, const std::vector<CeCopy> &ce, int nstreams, int schedule,
+                     cudaStream_t s, cudaEvent_t ev_start, cudaEvent_t ev_end) {
+  auto kernel = [&]() -> int {
+    if (ev_start) FKV_CUDA(cudaEventRecord(ev_start, s));
+    if (has_sm)
+      if (int rc = launch_copy(h2d, variant, grid, *p, s)) return rc;
+    if (ev_end) FKV_CUDA(cudaEventRecord(ev_end, s));
+    return FKV_OK;
+  };
+  if (ce.empty()) return kernel();
+  if (schedule == 0) {  // fork before the kernel so both run together
+    if (int rc = fork_ce(ctx, ce, nstreams, h2d, s)) return rc;
+    if (int rc = kernel()) return rc;
+    return join_ce(ctx, nstreams, s);
+  }
+  if (schedule == 1) {
+    if (int rc = fork_ce(ctx, ce, nstreams, h2d, s)) return rc;
+    if (int rc = join_ce(ctx, nstreams, s)) return rc;
+    return kernel();
+  }
+  if (int rc = kernel()) return rc;
+  if (int rc = fork_ce(ctx, ce, nstreams, h2d, s)) return rc;
+  return join_ce(ctx, nstreams, s);
 }
 
 int current_device(int *dev) {
@@ -461,6 +510,7 @@ void fkv_transfer_desc_init(fkv_transfer_desc *d) {
   d->synchronous = 1;
   d->ce_min_run_bytes = -1;
   d->num_ce_streams = 0;
+  d->ce_schedule = -1;
   d->is_host_to_device = 1;
 }
 
@@ -486,6 +536,7 @@ int fkv_transfer_kv_blocks_ex(const fkv_transfer_desc *d, void *stream_) {
   if (int rc = validate_desc(*d)) return rc;
   if (d->num_blocks == 0 || d->num_layers == 0 || d->chunk_size_in_bytes < 16) return FKV_OK;
   cudaStream_t s = (cudaStream_t)stream_;
+  const double tstart = profiling() ? now_us() : 0;
   int device = 0;
   if (int rc = current_device(&device)) return rc;
   HostPlan hp;
@@ -493,28 +544,40 @@ int fkv_transfer_kv_blocks_ex(const fkv_transfer_desc *d, void *stream_) {
   ThreadDeviceCtx *ctx = nullptr;
   if (int rc = get_ctx(device, &ctx)) return rc;
 
+  const bool prof = profiling();
+  const double t0 = prof ? now_us() : 0;
   char *dev_table = nullptr;
+  CopyParams p{};
   if (!hp.sm_gpu.empty()) {
     const size_t tb = table_bytes(hp);
     char *stage = nullptr;
     if (int rc = acquire_staging(ctx, tb, &stage)) return rc;
     fill_table(hp, *d, reinterpret_cast<int64_t *>(stage));
-    FKV_CUDA(cudaMallocAsync((void **)&dev_table, tb, s));
-    FKV_CUDA(cudaMemcpyAsync(dev_table, stage, tb, cudaMemcpyHostToDevice, s));
-    if (int rc = release_staging(ctx, s)) return rc;
-    CopyParams p = make_params(hp, dev_table);
-    if (int rc = launch_copy(hp.h2d, hp.unroll_idx, hp.grid, p, s)) {
-      cudaFreeAsync(dev_table, s);
-      return rc;
+    if (int rc = scratch_alloc(device, tb, s, (void **)&dev_table)) return rc;
+    cudaError_t e = cudaMemcpyAsync(dev_table, stage, tb, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) {
+      scratch_free(dev_table, s);
+      return fail_cuda(e, "cudaMemcpyAsync(plan table)");
     }
+    if (int rc = release_staging(ctx, s)) return rc;
+    p = make_params(hp, dev_table);
   }
-  int rc = issue_ce(ctx, hp.ce, hp.num_ce_streams, hp.h2d, s);
+  const double t1 = prof ? now_us() : 0;
+  int rc = enqueue_transfer(ctx, hp.h2d, hp.unroll_idx, hp.grid, &p, !hp.sm_gpu.empty(), hp.ce,
+                            hp.num_ce_streams, hp.ce_schedule, s, nullptr, nullptr);
   if (dev_table) {
-    cudaError_t e = cudaFreeAsync(dev_table, s);
-    if (rc == FKV_OK && e != cudaSuccess) rc = fail_cuda(e, "cudaFreeAsync");
+    int rf = scratch_free(dev_table, s);
+    if (rc == FKV_OK) rc = rf;
   }
   if (rc != FKV_OK) return rc;
+  const double t2 = prof ? now_us() : 0;
   if (d->synchronous) FKV_CUDA(cudaStreamSynchronize(s));  // transfer.cu:131
+  if (prof) {
+    const double t3 = now_us();
+    std::fprintf(stderr, "[fkv] transfer %s n=%d: plan %.1fus upload %.1fus enqueue %.1fus sync %.1fus (sm %zu blocks, ce %zu copies)\n",
+                 hp.h2d ? "h2d" : "d2h", d->num_blocks, t0 - tstart, t1 - t0, t2 - t1, t3 - t2,
+                 hp.sm_gpu.size(), hp.ce.size());
+  }
   return FKV_OK;
 }
 
@@ -569,6 +632,7 @@ int fkv_plan_create(const fkv_transfer_desc *d, int device, fkv_plan **out) {
     p->unroll_idx = hp.unroll_idx;
     p->ce = std::move(hp.ce);
     p->num_ce_streams = hp.num_ce_streams;
+    p->ce_schedule = hp.ce_schedule;
     p->ce_bytes = hp.ce_bytes;
     p->sm_chunks = (int64_t)hp.num_layers * hp.kv_dim * (int64_t)hp.sm_gpu.size();
     p->sm_bytes = p->sm_chunks * hp.copy_bytes;
@@ -604,16 +668,10 @@ int fkv_plan_execute_ex(fkv_plan *p, void *stream_, void *ev_start, void *ev_end
   if (prev != p->device) FKV_CUDA(cudaSetDevice(p->device));
   ThreadDeviceCtx *ctx = nullptr;
   int rc = get_ctx(p->device, &ctx);
-  if (rc == FKV_OK && ev_start) {
-    cudaError_t e = cudaEventRecord((cudaEvent_t)ev_start, s);
-    if (e != cudaSuccess) rc = fail_cuda(e, "cudaEventRecord");
-  }
-  if (rc == FKV_OK && p->sm_chunks > 0) rc = launch_copy(p->h2d, p->unroll_idx, p->grid, p->params, s);
-  if (rc == FKV_OK && ev_end) {
-    cudaError_t e = cudaEventRecord((cudaEvent_t)ev_end, s);
-    if (e != cudaSuccess) rc = fail_cuda(e, "cudaEventRecord");
-  }
-  if (rc == FKV_OK) rc = issue_ce(ctx, p->ce, p->num_ce_streams, p->h2d, s);
+  if (rc == FKV_OK)
+    rc = enqueue_transfer(ctx, p->h2d, p->unroll_idx, p->grid, &p->params, p->sm_chunks > 0, p->ce,
+                          p->num_ce_streams, p->ce_schedule, s, (cudaEvent_t)ev_start,
+                          (cudaEvent_t)ev_end);
   if (prev != p->device) cudaSetDevice(prev);
   return rc;
 }

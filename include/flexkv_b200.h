@@ -112,11 +112,13 @@ typedef struct fkv_transfer_desc {
                                 whose per-(layer,kv) span reaches this many
                                 bytes go to the copy engines              */
   int num_ce_streams;        /* <=0 default                               */
-  int reserved;
+  int ce_schedule;           /* -1 default; 0 copy engines concurrent with
+                                the SM kernel; 1 copy engines first; 2 SM
+                                kernel first                              */
 } fkv_transfer_desc;
 
 /* Zero-fill *d and set the defaults (transfer_sms=-1, synchronous=1,
- * ce_min_run_bytes=-1, num_ce_streams=0). */
+ * ce_min_run_bytes=-1, num_ce_streams=0, ce_schedule=-1). */
 void fkv_transfer_desc_init(fkv_transfer_desc *d);
 
 int fkv_transfer_kv_blocks_ex(const fkv_transfer_desc *d, void *stream);

@@ -122,6 +122,24 @@ def view_transfer(case: Case, gpu_layers: List[np.ndarray], cpu_pool: np.ndarray
                     cpu_pool[cs:cs + copy] = gl[gs:gs + copy]
 
 
+def place_segments(rng, lens: List[int], pool: int) -> List[int]:
+    """Start ids for segments of the given lengths, disjoint inside
+    [0, pool): segments are laid out in a random order separated by random
+    gaps that share the pool's free space."""
+    n = sum(lens)
+    assert n <= pool, "pool smaller than the requested blocks"
+    k = len(lens)
+    cuts = np.sort(rng.integers(0, pool - n + 1, k))
+    gaps = np.diff(np.concatenate([[0], cuts]))
+    starts = [0] * k
+    pos = 0
+    for j, idx in enumerate(rng.permutation(k)):
+        pos += int(gaps[j])
+        starts[idx] = pos
+        pos += lens[idx]
+    return starts
+
+
 def make_ids(n: int, gpu_pool: int, cpu_pool: int, seed: int, run_frac: float = 0.0,
              max_run: int = 64, distinct: bool = True):
     """Block-id pairs: with run_frac > 0, that fraction of the n blocks sits
@@ -142,21 +160,7 @@ def make_ids(n: int, gpu_pool: int, cpu_pool: int, seed: int, run_frac: float = 
     lens += [1] * (n - n_run)
 
     def segments(pool: int) -> List[int]:
-        # Runs get distinct slots of max_run ids (random slot order);
-        # singletons are sampled from the ids no run slot covers.
-        nslots = pool // max_run
-        nruns = sum(1 for r in lens if r > 1)
-        assert nslots > nruns, "pool too small for the requested runs"
-        slots = rng.permutation(nslots)[:nruns]
-        used = np.zeros(pool, dtype=bool)
-        for s in slots:
-            used[s * max_run:(s + 1) * max_run] = True
-        free = np.flatnonzero(~used)
-        nsing = len(lens) - nruns
-        assert free.size >= nsing, "pool too small for the requested singletons"
-        singles = rng.choice(free, size=nsing, replace=False)
-        it_slots, it_single = iter(slots), iter(singles)
-        return [int(next(it_slots)) * max_run if r > 1 else int(next(it_single)) for r in lens]
+        return place_segments(rng, lens, pool)
 
     gs, cs = segments(gpu_pool), segments(cpu_pool)
     order = rng.permutation(len(lens))

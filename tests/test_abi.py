@@ -45,7 +45,7 @@ def test_desc_init_defaults_and_layout():
     ctypes.memset(ctypes.byref(d), 0x5A, ctypes.sizeof(d))
     _lib.load().fkv_transfer_desc_init(ctypes.byref(d))
     assert (d.transfer_sms, d.synchronous, d.ce_min_run_bytes, d.num_ce_streams) == (-1, 1, -1, 0)
-    assert d.num_blocks == 0 and d.cpu_pool_bytes == 0 and d.reserved == 0 and d.is_host_to_device == 1
+    assert d.num_blocks == 0 and d.cpu_pool_bytes == 0 and d.ce_schedule == -1 and d.is_host_to_device == 1
 
 
 def py_runs(g, c):

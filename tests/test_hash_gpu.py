@@ -121,4 +121,4 @@ def test_hash_utils_style_usage():
     assert np.array_equal(block_hashes.numpy(), O.gen_hashes(toks.numpy(), 16))
     h = c_ext.Hasher()
     h.update(toks[:5 * 16])
-    assert h.digest() == int(block_hashes[4])
+    assert h.digest() == int(block_hashes.numpy()[4])

@@ -65,7 +65,7 @@ RANDOM_CASES = [
     (Case("mla_tpb64", 5, 1, 576, 64, 96, 160, "BLOCKWISE", is_mla=True), 64, 0.5, True),
     (Case("tp8_slice", 6, 1, 128, 64, 64, 96, "BLOCKWISE", tp=8), 48, 0.3, True),
     (Case("small_chunk", 3, 1, 8, 1, 512, 1024), 400, 0.5, True),  # 16-byte chunks
-    (Case("dup_ids", 4, 2, 64, 16, 64, 64), 80, 0.0, False),
+    (Case("dup_ids", 4, 2, 64, 16, 64, 64), 48, 0.0, False),
 ]
 
 
