@@ -96,6 +96,11 @@ _SIGNATURES = {
     "fkv_hasher_digest": (c_int, [c_vp, P_u64, c_vp]),
     "fkv_gen_hashes": (c_int, [c_vp, c_vp, c_i64, c_int, c_vp, c_i64, c_vp]),
     "fkv_gen_hashes_batched": (c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp]),
+    "fkv_transfer_kv_blocks_noalloc": (
+        c_int,
+        [c_int, c_int, c_int, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64,
+         c_i64, c_i64, c_i64, c_vp, c_int, c_int, c_int],
+    ),
 }
 
 _lock = threading.Lock()

@@ -697,3 +697,151 @@ void fkv_plan_destroy(fkv_plan *p) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of fkv_transfer_kv_blocks.
+//
+// Some callers cannot allocate device memory at the moment they move KV
+// blocks: an engine that hands the whole GPU to its own caching allocator
+// and forbids outside cudaMalloc, a host thread running under a strict
+// memory budget, or code that must not trigger the implicit
+// synchronization an allocation can cause.  This entry point keeps its
+// scratch (the layer-pointer table and the two block-id arrays the copy
+// kernel reads) in the file-scope device array below instead of the
+// library's memory pool, and never calls an allocating CUDA routine.
+//
+// Limits: at most kNoAllocMaxLayers layers and kNoAllocMaxBlocks blocks per
+// call (132 KiB of device memory, held by every GPU that loads this library
+// until the process exits).  Only the SM copy kernel is used (no copy
+// engines, no side streams).  Every call shares the one array and
+// overwrites the part it uses; the call is synchronous, so calls made one
+// after another are safe, while calls that overlap on the GPU (from several
+// host threads or streams at once) race on the array.  The first call on a
+// device resolves the array's device address with cudaGetSymbolAddress
+// (with that device current); make that first call before any stream
+// capture.
+// ---------------------------------------------------------------------------
+namespace fkv {
+namespace {
+
+constexpr int kNoAllocMaxLayers = 512;
+constexpr int kNoAllocMaxBlocks = 8192;
+constexpr int kNoAllocWords = kNoAllocMaxLayers + 2 * kNoAllocMaxBlocks;
+
+static __device__ __align__(256) int64_t g_noalloc_table[kNoAllocWords];
+
+// Device address of g_noalloc_table per device, resolved once per device.
+std::mutex g_noalloc_mu;
+int64_t *g_noalloc_addr[64] = {nullptr};
+
+int noalloc_table(int device, int64_t **out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  int64_t *&p = g_noalloc_addr[device & 63];
+  if (p == nullptr) {
+    void *addr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_table);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaGetSymbolAddress(g_noalloc_table)");
+    p = static_cast<int64_t *>(addr);
+  }
+  *out = p;
+  return FKV_OK;
+}
+
+}  // namespace
+}  // namespace fkv
+
+extern "C" int fkv_transfer_kv_blocks_noalloc(
+    int num_blocks, int start_layer_id, int num_layers, const int64_t *gpu_block_ids,
+    void *const *gpu_layer_ptrs, int64_t gpu_kv_stride_in_bytes, int64_t gpu_block_stride_in_bytes,
+    const int64_t *cpu_block_ids, void *cpu_ptr, int64_t cpu_kv_stride_in_bytes,
+    int64_t cpu_layer_stride_in_bytes, int64_t cpu_block_stride_in_bytes,
+    int64_t cpu_startoff_inside_chunks, int64_t chunk_size_in_bytes, int64_t cpu_pool_bytes,
+    int64_t gpu_layer_bytes, void *stream_, int transfer_sms, int is_host_to_device, int is_mla) {
+  clear_error();
+  if (num_blocks > kNoAllocMaxBlocks)
+    return fail(FKV_ERR_INVALID_ARG, "fkv_transfer_kv_blocks_noalloc: num_blocks exceeds the limit of 8192");
+  if (num_layers > kNoAllocMaxLayers)
+    return fail(FKV_ERR_INVALID_ARG, "fkv_transfer_kv_blocks_noalloc: num_layers exceeds the limit of 512");
+  if (num_blocks < 0 || num_layers < 0 || chunk_size_in_bytes < 0 || start_layer_id < 0 ||
+      gpu_kv_stride_in_bytes < 0 || gpu_block_stride_in_bytes < 0 || cpu_kv_stride_in_bytes < 0 ||
+      cpu_layer_stride_in_bytes < 0 || cpu_block_stride_in_bytes < 0 ||
+      cpu_startoff_inside_chunks < 0)
+    return fail(FKV_ERR_INVALID_ARG, "fkv_transfer_kv_blocks_noalloc: negative size, stride or offset");
+  const int64_t copy_bytes = (chunk_size_in_bytes / 16) * 16;  // transfer.cu:35
+  if (num_blocks == 0 || num_layers == 0 || copy_bytes == 0) return FKV_OK;
+  if (!gpu_block_ids || !cpu_block_ids || !gpu_layer_ptrs || !cpu_ptr)
+    return fail(FKV_ERR_INVALID_ARG, "fkv_transfer_kv_blocks_noalloc: null id array, layer table or cpu pointer");
+  cudaStream_t s = (cudaStream_t)stream_;
+  int device = 0;
+  FKV_CUDA(cudaGetDevice(&device));
+  int64_t *table = nullptr;
+  if (int rc = noalloc_table(device, &table)) return rc;
+
+  const int kv_dim = is_mla ? 1 : 2;
+  const int64_t gkv = trunc8(gpu_kv_stride_in_bytes), gbs = trunc8(gpu_block_stride_in_bytes);
+  const int64_t cls = trunc8(cpu_layer_stride_in_bytes), ckv = trunc8(cpu_kv_stride_in_bytes);
+  const int64_t cbs = trunc8(cpu_block_stride_in_bytes);
+  const int64_t base_off = (int64_t)start_layer_id * cls + trunc8(cpu_startoff_inside_chunks);
+  cudaPointerAttributes attr;
+  cudaError_t e = cudaPointerGetAttributes(&attr, cpu_ptr);
+  if (e != cudaSuccess || attr.type != cudaMemoryTypeHost || attr.devicePointer == nullptr) {
+    cudaGetLastError();
+    return fail(FKV_ERR_INVALID_ARG, "fkv_transfer_kv_blocks_noalloc: cpu_ptr is not page-locked host memory");
+  }
+  char *cpu_dev_base = (char *)attr.devicePointer + base_off;
+  if (((uintptr_t)cpu_dev_base & 15) || (num_layers > 1 && (cls & 15)) ||
+      (kv_dim > 1 && ((ckv & 15) || (gkv & 15))))
+    return fail(FKV_ERR_MISALIGNED, "fkv_transfer_kv_blocks_noalloc: cpu base or strides not 16-byte aligned");
+  for (int l = 0; l < num_layers; ++l)
+    if (gpu_layer_ptrs[l] == nullptr || ((uintptr_t)gpu_layer_ptrs[l] & 15))
+      return fail(FKV_ERR_MISALIGNED, "fkv_transfer_kv_blocks_noalloc: null or misaligned gpu layer pointer");
+  const int64_t cpu_fixed = base_off + (int64_t)(num_layers - 1) * cls + (kv_dim - 1) * ckv + copy_bytes;
+  const int64_t gpu_fixed = (kv_dim - 1) * gkv + copy_bytes;
+  for (int i = 0; i < num_blocks; ++i) {
+    const int64_t g = gpu_block_ids[i], c = cpu_block_ids[i];
+    if (g < 0 || c < 0 || g >= (1ll << 31) || c >= (1ll << 31))
+      return fail(FKV_ERR_OUT_OF_RANGE, "fkv_transfer_kv_blocks_noalloc: block id out of [0, 2^31)");
+    if (((g * gbs) & 15) || ((c * cbs) & 15))
+      return fail(FKV_ERR_MISALIGNED, "fkv_transfer_kv_blocks_noalloc: block stride times id is not 16-byte aligned");
+    if (cpu_pool_bytes > 0 && c * cbs + cpu_fixed > cpu_pool_bytes)
+      return fail(FKV_ERR_OUT_OF_RANGE, "fkv_transfer_kv_blocks_noalloc: cpu block id addresses past the cpu pool");
+    if (gpu_layer_bytes > 0 && g * gbs + gpu_fixed > gpu_layer_bytes)
+      return fail(FKV_ERR_OUT_OF_RANGE, "fkv_transfer_kv_blocks_noalloc: gpu block id addresses past the gpu layer");
+  }
+
+  // Table layout as in the pooled path: [layer ptrs L][gpu ids n][cpu ids n].
+  static_assert(sizeof(void *) == sizeof(int64_t), "64-bit pointers expected");
+  FKV_CUDA(cudaMemcpyAsync(table, gpu_layer_ptrs, (size_t)num_layers * 8, cudaMemcpyHostToDevice, s));
+  FKV_CUDA(cudaMemcpyAsync(table + num_layers, gpu_block_ids, (size_t)num_blocks * 8,
+                           cudaMemcpyHostToDevice, s));
+  FKV_CUDA(cudaMemcpyAsync(table + num_layers + num_blocks, cpu_block_ids, (size_t)num_blocks * 8,
+                           cudaMemcpyHostToDevice, s));
+
+  CopyParams p{};
+  p.layer_ptrs = reinterpret_cast<char *const *>(table);
+  p.gpu_ids = table + num_layers;
+  p.cpu_ids = table + num_layers + num_blocks;
+  p.cpu_base = cpu_dev_base;
+  p.gpu_kv_stride = gkv;
+  p.gpu_block_stride = gbs;
+  p.cpu_layer_stride = cls;
+  p.cpu_kv_stride = ckv;
+  p.cpu_block_stride = cbs;
+  p.n_vec = copy_bytes / 16;
+  p.n = (uint32_t)num_blocks;
+  p.per_layer = (uint32_t)(kv_dim * num_blocks);
+  p.num_chunks = (uint32_t)(num_layers * kv_dim * num_blocks);
+
+  int num_sms = 0;
+  FKV_CUDA(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device));
+  int sms = transfer_sms > 0 ? std::min(transfer_sms, num_sms) : std::min(kDefaultSms, num_sms);
+  const bool h2d = is_host_to_device != 0;
+  const int variant = variant_index(8, 0);
+  int occ = 1;
+  if (int rc = ctas_per_sm(device, h2d, variant, &occ)) return rc;
+  const int64_t warps_per_cta = kThreads / 32;
+  int64_t grid = std::min<int64_t>((int64_t)sms * occ, ((int64_t)p.num_chunks + warps_per_cta - 1) / warps_per_cta);
+  if (int rc = launch_copy(h2d, variant, (int)std::max<int64_t>(grid, 1), p, s)) return rc;
+  FKV_CUDA(cudaStreamSynchronize(s));  // the shared table is free again on return
+  return FKV_OK;
+}

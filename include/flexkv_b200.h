@@ -85,6 +85,33 @@ int fkv_transfer_kv_blocks(int num_blocks, int start_layer_id, int num_layers,
                            int transfer_sms, int is_host_to_device,
                            int use_ce_transfer, int is_mla);
 
+/* Allocation-free variant of fkv_transfer_kv_blocks, with no counterpart in
+ * the reference.  For callers that cannot allocate device memory while they
+ * move KV blocks (an engine whose caching allocator owns the GPU, a thread
+ * under a strict memory budget): the copy kernel's scratch (layer-pointer
+ * table and block-id arrays) lives in a 132 KiB file-scope device array
+ * that every GPU loading this library holds until exit, instead of the
+ * library's memory pool.  At most 8192 blocks and 512 layers per call
+ * (larger requests return FKV_ERR_INVALID_ARG); SM copy kernel only.
+ * Synchronous.  All calls share the one array, so calls that overlap on the
+ * GPU (several threads or streams at once) race.  The first call on a
+ * device resolves the array's address (cudaGetSymbolAddress with that
+ * device current); make it before any stream capture.  cpu_pool_bytes /
+ * gpu_layer_bytes > 0 enable the bounds checks. */
+int fkv_transfer_kv_blocks_noalloc(int num_blocks, int start_layer_id, int num_layers,
+                                   const int64_t *gpu_block_ids,
+                                   void *const *gpu_layer_ptrs,
+                                   int64_t gpu_kv_stride_in_bytes,
+                                   int64_t gpu_block_stride_in_bytes,
+                                   const int64_t *cpu_block_ids, void *cpu_ptr,
+                                   int64_t cpu_kv_stride_in_bytes,
+                                   int64_t cpu_layer_stride_in_bytes,
+                                   int64_t cpu_block_stride_in_bytes,
+                                   int64_t cpu_startoff_inside_chunks,
+                                   int64_t chunk_size_in_bytes, int64_t cpu_pool_bytes,
+                                   int64_t gpu_layer_bytes, void *stream,
+                                   int transfer_sms, int is_host_to_device, int is_mla);
+
 /* Full descriptor of one transfer (superset of the reference arguments). */
 typedef struct fkv_transfer_desc {
   int num_blocks;
