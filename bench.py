@@ -158,25 +158,34 @@ def barrier(ws):
     if ws > 1:
         import torch.distributed as dist
         dist.barrier()
-    torch.cuda.synchronize()
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+
+
+def _reduce(ws, x: float, op: str) -> float:
+    """All-reduce one float over the ranks (timing plumbing only, never data)."""
+    if ws == 1:
+        return x
+    import torch.distributed as dist
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+    return float(t.item())
 
 
 def max_over_ranks(ws, x: float) -> float:
-    if ws == 1:
-        return x
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return _reduce(ws, x, "max")
 
 
 def sum_over_ranks(ws, x: float) -> float:
-    if ws == 1:
-        return x
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
+    return _reduce(ws, x, "sum")
+
+
+def rank_batches(cfg: dict, cpu_blocks: int, local: int, nbatches: int = 4):
+    """The block-id batches of one data-parallel rank: its own seeds, its
+    own pools, no id shared with another rank's work."""
+    return [make_batch(cfg["batch"], cfg["gpu_blocks"], cpu_blocks, 1000 * local + s,
+                       cfg["run_frac"], cfg["max_run"]) for s in range(nbatches)]
 
 
 def mem_available_bytes() -> int:
@@ -232,14 +241,56 @@ class Setup:
         t2 = time.time()
         log(f"[rank{local}] gpu pool {L}x{self.gpu_layer_bytes / 2**30:.2f} GiB in {t1 - t0:.1f}s, "
             f"cpu pool {cpu_bytes / 2**30:.1f} GiB registered in {t2 - t1:.1f}s")
-        self.batches = [make_batch(cfg["batch"], cfg["gpu_blocks"], cpu_blocks,
-                                   1000 * local + s, cfg["run_frac"], cfg["max_run"])
-                        for s in range(nbatches)]
+        self.batches = rank_batches(cfg, cpu_blocks, local, nbatches)
         self.batch_bytes = cfg["batch"] * self.block_bytes
 
     def close(self):
         from flexkv_b200 import c_ext
         c_ext.cudaHostUnregister(self.cpu)
+
+
+def measure_extras(S, plans, stream, K):
+    """Two extra figures on the same pools: the host link's copy-engine peak
+    (one large contiguous cudaMemcpyAsync each way from the pinned pool, the
+    measured roofline of the link) and the duplex rate (the H2D of batch k
+    and the D2H of batch k+1 in flight together on two streams)."""
+    n = min(S.batch_bytes, 2 << 30)
+    gbuf = torch.empty(n, dtype=torch.uint8, device="cuda")
+    hbuf = S.cpu.view(torch.uint8)[:n]
+    peak = {}
+    for name, fn in (("h2d", lambda: gbuf.copy_(hbuf, non_blocking=True)),
+                     ("d2h", lambda: hbuf.copy_(gbuf, non_blocking=True))):
+        fn()
+        ts = []
+        for _ in range(3):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        peak[name] = round(n / (statistics.median(ts) / 1e3) / 1e9, 2)
+    del gbuf
+    side = torch.cuda.Stream()
+    ts = []
+    for k in range(max(K, 3)):
+        h = plans[k % len(plans)][0]
+        d = plans[(k + 1) % len(plans)][1]
+        a, b, c = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        a.record(stream)
+        side.wait_event(a)
+        h.execute(stream=stream)
+        d.execute(stream=side)
+        c.record(side)
+        stream.wait_event(c)
+        b.record(stream)
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    duplex = 2 * S.batch_bytes / (statistics.median(ts) / 1e3) / 1e9
+    return {"link_peak_measured": dict(peak, unit="GB/s", bytes=n,
+                                       how="one contiguous cudaMemcpyAsync each way from the pinned pool, median of 3"),
+            "duplex": {"value": round(duplex, 2), "unit": "GB/s",
+                       "how": "H2D of batch k and D2H of batch k+1 at once on two streams (median step)"}}
 
 
 def run_ours(args, ws, rank, local, cfg):
@@ -321,6 +372,7 @@ def run_ours(args, ws, rank, local, cfg):
         e2e_s = time.perf_counter() - w0
         barrier(ws)
     clocks = sampler.summary()
+    extras = {} if args.no_extras else measure_extras(S, plans, stream, K)
 
     h2d_ms = [evs[k][0].elapsed_time(evs[k][3]) for k in range(K)]
     d2h_ms = [evs[k][3].elapsed_time(evs[k][6]) for k in range(K)]
@@ -334,33 +386,45 @@ def run_ours(args, ws, rank, local, cfg):
     bb = S.batch_bytes
     h2d_gbs = bb / (statistics.mean(h2d_ms) / 1e3) / 1e9
     d2h_gbs = bb / (statistics.mean(d2h_ms) / 1e3) / 1e9
-    # Dominant kernel: the SM copy kernel of the direction with more SM time.
-    kern = []
-    for name, ms, st in (("kv_copy_kernel<H2D>", kh_ms, stats[0]), ("kv_copy_kernel<D2H>", kd_ms, stats[1])):
-        if st["sm_chunks"] > 0 and statistics.mean(ms) > 0:
-            kern.append((statistics.mean(ms), name, st["sm_bytes"]))
+    # Roofline of the transfer op (the SM kernel plus the copy-engine runs it
+    # overlaps with share one host link, so the op is the unit that meets the
+    # link's bound).  Headline: the slower direction.  Peak: the link's
+    # copy-engine rate measured live on the same pool (MEASURED_PEAKS.json
+    # has no host-link figure), with the nominal PCIe Gen5 x16 rate beside it.
+    # DRAM traffic per op: the algorithmic bytes times the (read+write)/payload
+    # ratio of the kernel's ncu capture (profiles/kv_copy_kernel_cfg2_small_full.md).
+    TRAFFIC_RATIO = {"h2d": 0.781, "d2h": 1.016}
     out = None
     if rank == 0:
-        op_roof = {"bound": "pcie", "unit": "GB/s", "peak": PCIE_GEN5_X16_GBS,
-                   "peak_source": "nominal PCIe Gen5 x16 per direction (MEASURED_PEAKS.json has no host-link figure)",
-                   "h2d": round(h2d_gbs, 2), "d2h": round(d2h_gbs, 2),
-                   "frac_h2d": round(h2d_gbs / PCIE_GEN5_X16_GBS, 4),
-                   "frac_d2h": round(d2h_gbs / PCIE_GEN5_X16_GBS, 4)}
-        if kern:
-            ms, name, sm_bytes = max(kern)
-            ach = sm_bytes / (ms / 1e3) / 1e9
-            roof = {"bound": "pcie", "kernel": name, "achieved": round(ach, 2),
-                    "peak": PCIE_GEN5_X16_GBS, "unit": "GB/s", "frac": round(ach / PCIE_GEN5_X16_GBS, 4),
-                    "traffic": None, "bytes_per_launch": sm_bytes, "avg_launch_ms": round(ms, 3),
-                    "peak_source": op_roof["peak_source"]}
-        else:
-            roof = dict(op_roof, kernel="copy engines only", achieved=None, frac=None, traffic=None)
+        lp = extras.get("link_peak_measured")
+        dirs = {"h2d": (h2d_gbs, kh_ms, stats[0]), "d2h": (d2h_gbs, kd_ms, stats[1])}
+        head = min(dirs, key=lambda d: dirs[d][0])
+        ach, kms, st = dirs[head]
+        peak = lp[head] if lp else PCIE_GEN5_X16_GBS
+        roof = {"bound": "pcie", "kernel": f"transfer op {head.upper()} (kv_copy_kernel + copy-engine runs)",
+                "achieved": round(ach, 2), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
+                "traffic": int(bb * TRAFFIC_RATIO[head]),
+                "peak_source": ("measured live: one contiguous cudaMemcpyAsync of 2 GiB on the same "
+                                "pinned pool (MEASURED_PEAKS.json has no host-link figure)") if lp else
+                               "nominal PCIe Gen5 x16 (no live measurement in this run)",
+                "nominal_peak": PCIE_GEN5_X16_GBS, "frac_of_nominal": round(ach / PCIE_GEN5_X16_GBS, 4),
+                "per_direction": {d: {"achieved": round(v[0], 2),
+                                      "peak": (lp[d] if lp else PCIE_GEN5_X16_GBS),
+                                      "frac": round(v[0] / (lp[d] if lp else PCIE_GEN5_X16_GBS), 4)}
+                                  for d, v in dirs.items()}}
+        if st["sm_chunks"] > 0 and statistics.mean(kms) > 0:
+            kmean = statistics.mean(kms)
+            roof["sm_kernel"] = {"name": f"kv_copy_kernel<{head.upper()}>",
+                                 "bytes_per_launch": st["sm_bytes"], "avg_launch_ms": round(kmean, 3),
+                                 "achieved_alongside_copy_engines": round(st["sm_bytes"] / kmean / 1e6, 2),
+                                 "copy_engine_bytes_per_op": st["ce_bytes"]}
         out = {
             "metric": "KV GB/s per GPU and box (H2D/D2H, 1/2/4/8 B200), % of PCIe Gen5 x16 peak",
             "value": round(value, 3), "unit": "GB/s", "n_gpus": ws, "steps": K, "warmup": W,
             "ms_per_step": round(max_elapsed / K, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16 (byte copy)", "data": "synthetic",
-            "config": {"workload": args.config, "layout": args.layout, "mode": args.mode,
+            "config": {"workload": args.config + (" (reduced: profiling case)" if (args.batch or args.gpu_blocks) else ""),
+                       "layout": args.layout, "mode": args.mode,
                        "layers": cfg["layers"], "kv_heads": cfg["heads"], "head_dim": cfg["head_dim"],
                        "tokens_per_block": cfg["tpb"], "batch_blocks": cfg["batch"],
                        "batch_bytes_per_direction": bb, "gpu_pool_blocks": cfg["gpu_blocks"],
@@ -371,7 +435,7 @@ def run_ours(args, ws, rank, local, cfg):
             "per_direction_gbs": {"h2d": round(h2d_gbs, 2), "d2h": round(d2h_gbs, 2)},
             "blocks_per_s": round(value * 1e9 / S.block_bytes, 1),
             "box_roofline_frac": round(value / (PCIE_GEN5_X16_GBS * ws), 4),
-            "roofline": roof, "op_roofline": op_roof,
+            "roofline": roof,
             "plan": {"h2d": stats[0], "d2h": stats[1]},
             "e2e": {"value": round(e2e, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": int(bb + 16 * cfg["batch"] + 8 * cfg["layers"]),
@@ -379,6 +443,7 @@ def run_ours(args, ws, rank, local, cfg):
                     "how": "flexkv_b200.c_ext.transfer_kv_blocks, pinned host id tensors, synchronous calls, wall clock"},
             "gpu_launches": int(launches), "clocks": clocks,
         }
+        out.update(extras)
     for p in plans:
         for x in p:
             x.close()
@@ -496,6 +561,10 @@ def main():
     ap.add_argument("--transfer-sms", type=int, default=-1)
     ap.add_argument("--cpu-blocks", type=int, default=0, help="override the CPU pool size")
     ap.add_argument("--cpu-baseline-seconds", type=float, default=8.0)
+    ap.add_argument("--batch", type=int, default=0, help="override blocks per batch (profiling case)")
+    ap.add_argument("--gpu-blocks", type=int, default=0, help="override the GPU pool size")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the link-peak and duplex measurements (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3 (timing rule)")
@@ -505,7 +574,11 @@ def main():
     if args.impl == "reference":
         os.environ["WORLD_SIZE"] = "1"  # no process group: rank 0 alone
     ws, rank, local = dist_setup()
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.batch:
+        cfg["batch"] = args.batch
+    if args.gpu_blocks:
+        cfg["gpu_blocks"] = args.gpu_blocks
     if args.impl == "reference":
         out, S = run_reference(args, ws, rank, local, cfg)
     else:
