@@ -1,25 +1,32 @@
 #!/usr/bin/env python
 """Benchmark of the FlexKV transfer data plane on B200 (one JSON line).
 
-Workload (Llama-3-8B KV shape): 32 layers, 8 KV heads,
-head_dim 128, 16 tokens per block, bf16 (32 KiB chunks, 2 MiB per block over
-all layers).  GPU pool 16384 blocks (32 one-GiB layer tensors), pinned CPU
-pool up to 32768 blocks (64 GiB; scaled to the box's RAM and recorded).  A
-step moves one 2048-block batch host->device and one device->host (4 GiB
-each way); block ids are a seeded permutation with 50% of the blocks in joint
-contiguous runs of length U[1,64] and 50% scattered singletons; four batches
-rotate so consecutive steps touch different blocks.  Every batch is far
-larger than L2 (no flush needed).
+Default workload (Llama-3-8B KV shape): 32 layers, 8 KV
+heads, head_dim 128, 16 tokens per block, bf16 (32 KiB chunks, 2 MiB per
+block over all layers).  GPU pool 16384 blocks (32 one-GiB layer tensors),
+pinned CPU pool up to 32768 blocks (64 GiB; scaled to the box's RAM and
+recorded).  A step moves one 2048-block batch host->device and another
+device->host (4 GiB each way), one after the other as FlexKV's worker does;
+block ids are seeded permutations with 50% of the blocks in joint contiguous
+runs of length U[1,64] and 50% scattered singletons; four steps rotate so
+consecutive steps touch different blocks.  Every batch is far larger than L2
+(no flush needed).
 
-  value  — device-timed GB/s (CUDA events on the launch stream) with plans
-           (ids validated, coalesced and resident on the device) prepared
-           before the timed region.
+Other configurations (--config): cfg5_dsv3_mla (DeepSeek-V3 MLA latent KV,
+1024-block batches, runs of 128 : singletons 1:1, both directions at once),
+cfg4_qwen2_7b (Qwen2-7B shape, 256 requests of U[1,32] scattered blocks per
+step, mixed get/put, directions overlapped).
+
+  value  — device-timed GB/s (CUDA events on the launch streams) of plans
+           prepared before the timed region (ids validated, coalesced and
+           resident on the device).
   e2e    — GB/s through the reference-facing call
            flexkv_b200.c_ext.transfer_kv_blocks with host id tensors, wall
-           clock, synchronous per call like the reference.
+           clock (synchronous calls, or async per direction when the
+           workload overlaps directions).
   --impl reference — the reference's own transfer.cu built from its source
-           (oracle/_ref) driven the way its worker drives it
-           (transfer_sms=8, pinned id tensors, synchronous).
+           (oracle/_ref) driven the way its worker drives it: one op at a
+           time, transfer_sms=8, pinned id tensors, synchronous.
 
 Multi-GPU (torchrun): every rank runs the same per-GPU workload on its own
 GPU and pools (data parallel, no collective on the data path); value is the
@@ -43,29 +50,38 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 PCIE_GEN5_X16_GBS = 63.0  # 32 GT/s * 16 lanes * 128/130 / 8, per direction
+METRIC = "KV GB/s per GPU and box (H2D/D2H, 1/2/4/8 B200), % of PCIe Gen5 x16 peak"
 
 CONFIGS = {
     "cfg2_llama3_8b": dict(layers=32, heads=8, head_dim=128, tpb=16, gpu_blocks=16384,
-                           cpu_blocks=32768, batch=2048, run_frac=0.5, max_run=64),
+                           cpu_blocks=32768, batch=2048, run_frac=0.5, max_run=64,
+                           kind="batch", concurrent=False, layout="LAYERWISE"),
     "cfg5_dsv3_mla": dict(layers=61, heads=1, head_dim=576, tpb=64, gpu_blocks=8192,
-                          cpu_blocks=16384, batch=1024, run_frac=0.5, max_run=128, mla=True),
+                          cpu_blocks=16384, batch=1024, run_frac=0.5, max_run=128, fixed_run=True,
+                          mla=True, kind="batch", concurrent=True, layout="BLOCKWISE"),
     "cfg4_qwen2_7b": dict(layers=28, heads=4, head_dim=128, tpb=16, gpu_blocks=8192,
-                          cpu_blocks=16384, batch=4224, run_frac=0.0, max_run=1),
+                          cpu_blocks=16384, requests=256, max_req_blocks=32, run_frac=0.0,
+                          max_run=1, kind="requests", concurrent=True, layout="LAYERWISE"),
 }
+# DRAM traffic per payload byte of the SM copy kernel, from its ncu capture
+# (profiles/kv_copy_kernel_cfg2_small_full.md): H2D writes, D2H reads.
+TRAFFIC_RATIO = {"h2d": 0.781, "d2h": 1.016}
 
 
 def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
-def make_batch(n, gpu_pool, cpu_pool, seed, run_frac, max_run):
+def make_batch(n, gpu_pool, cpu_pool, seed, run_frac, max_run, fixed_run=False):
     """Joint runs (both ids advance by one) covering run_frac of the blocks,
-    lengths U[1,max_run]; the rest scattered singletons; shuffled run order."""
+    lengths U[1,max_run] (or exactly max_run); the rest scattered singletons;
+    runs and singletons in a shuffled order, spread over both pools."""
     rng = np.random.default_rng(seed)
     n_run = int(round(n * run_frac))
     lens, left = [], n_run
     while left > 0:
-        r = int(min(left, rng.integers(1, max_run + 1)))
+        r = max_run if fixed_run else int(rng.integers(1, max_run + 1))
+        r = min(left, r)
         lens.append(r)
         left -= r
     lens += [1] * (n - n_run)
@@ -90,6 +106,32 @@ def make_batch(n, gpu_pool, cpu_pool, seed, run_frac, max_run):
         g += range(gs[i], gs[i] + lens[i])
         c += range(cs[i], cs[i] + lens[i])
     return np.array(g, dtype=np.int64), np.array(c, dtype=np.int64)
+
+
+def rank_steps(cfg: dict, cpu_blocks: int, local: int, nsteps: int = 4):
+    """The ops of each step of one data-parallel rank: its own seeds, its own
+    pools, no id shared with another rank's work.  An op is (gpu_ids,
+    cpu_ids, is_host_to_device)."""
+    steps = []
+    for s in range(nsteps):
+        seed = 1000 * local + 10 * s
+        if cfg["kind"] == "batch":
+            ops = []
+            for j, h2d in enumerate((True, False)):
+                g, c = make_batch(cfg["batch"], cfg["gpu_blocks"], cpu_blocks, seed + j,
+                                  cfg["run_frac"], cfg["max_run"], cfg.get("fixed_run", False))
+                ops.append((g, c, h2d))
+        else:
+            rng = np.random.default_rng(seed)
+            sizes = rng.integers(1, cfg["max_req_blocks"] + 1, cfg["requests"])
+            g, c = make_batch(int(sizes.sum()), cfg["gpu_blocks"], cpu_blocks, seed + 1, 0.0, 1)
+            dirs = rng.integers(0, 2, cfg["requests"]).astype(bool)
+            ops, o = [], 0
+            for n, h2d in zip(sizes.tolist(), dirs.tolist()):
+                ops.append((g[o:o + n], c[o:o + n], bool(h2d)))
+                o += n
+        steps.append(ops)
+    return steps
 
 
 class ClockSampler:
@@ -181,13 +223,6 @@ def sum_over_ranks(ws, x: float) -> float:
     return _reduce(ws, x, "sum")
 
 
-def rank_batches(cfg: dict, cpu_blocks: int, local: int, nbatches: int = 4):
-    """The block-id batches of one data-parallel rank: its own seeds, its
-    own pools, no id shared with another rank's work."""
-    return [make_batch(cfg["batch"], cfg["gpu_blocks"], cpu_blocks, 1000 * local + s,
-                       cfg["run_frac"], cfg["max_run"]) for s in range(nbatches)]
-
-
 def mem_available_bytes() -> int:
     with open("/proc/meminfo") as f:
         for line in f:
@@ -197,28 +232,28 @@ def mem_available_bytes() -> int:
 
 
 class Setup:
-    """Pools, layouts and id batches of one rank."""
+    """Pools, layouts and per-step ops of one rank."""
 
-    def __init__(self, cfg: dict, layout: str, ws: int, local: int, cpu_blocks_override: int = 0,
-                 nbatches: int = 4):
+    def __init__(self, cfg: dict, layout: str, ws: int, local: int, cpu_blocks_override: int = 0):
         from flexkv_b200 import c_ext
         from flexkv_b200.layout import KVCacheLayout, KVCacheLayoutType
         self.cfg = cfg
-        mla = cfg.get("mla", False)
-        self.kv = 1 if mla else 2
+        self.mla = cfg.get("mla", False)
+        self.kv = 1 if self.mla else 2
         L, H, D, tpb = cfg["layers"], cfg["heads"], cfg["head_dim"], cfg["tpb"]
         self.chunk = tpb * H * D * 2
         self.block_bytes = L * self.kv * self.chunk
         cpu_blocks = cfg["cpu_blocks"]
-        avail = mem_available_bytes()
-        fit = int(0.55 * avail / max(ws, 1) / self.block_bytes)
+        fit = int(0.55 * mem_available_bytes() / max(ws, 1) / self.block_bytes)
+        min_blocks = 2 * cfg.get("batch", cfg.get("requests", 1) * cfg.get("max_req_blocks", 1))
         if cpu_blocks_override:
             cpu_blocks = cpu_blocks_override
         elif fit < cpu_blocks:
-            cpu_blocks = max(fit, cfg["batch"] * 2)
+            cpu_blocks = max(fit, min_blocks)
         self.cpu_blocks = cpu_blocks
-        self.gpu_layout = KVCacheLayout(KVCacheLayoutType.LAYERWISE, L, cfg["gpu_blocks"], tpb, H, D, mla)
-        self.cpu_layout = KVCacheLayout(KVCacheLayoutType[layout], L, cpu_blocks, tpb, H, D, mla)
+        self.gpu_layout = KVCacheLayout(KVCacheLayoutType.LAYERWISE, L, cfg["gpu_blocks"], tpb, H, D,
+                                        self.mla)
+        self.cpu_layout = KVCacheLayout(KVCacheLayoutType[layout], L, cpu_blocks, tpb, H, D, self.mla)
         per = self.gpu_layout.div_layer(L)
         e = 2
         self.g_kv, self.g_blk = per.get_kv_stride() * e, per.get_block_stride() * e
@@ -241,26 +276,40 @@ class Setup:
         t2 = time.time()
         log(f"[rank{local}] gpu pool {L}x{self.gpu_layer_bytes / 2**30:.2f} GiB in {t1 - t0:.1f}s, "
             f"cpu pool {cpu_bytes / 2**30:.1f} GiB registered in {t2 - t1:.1f}s")
-        self.batches = rank_batches(cfg, cpu_blocks, local, nbatches)
-        self.batch_bytes = cfg["batch"] * self.block_bytes
+        self.steps = rank_steps(cfg, cpu_blocks, local)
+        self.step_bytes = {d: sum(len(g) for g, c, h in self.steps[0] if h == (d == "h2d")) * self.block_bytes
+                           for d in ("h2d", "d2h")}
 
     def close(self):
         from flexkv_b200 import c_ext
         c_ext.cudaHostUnregister(self.cpu)
 
 
-def measure_extras(S, plans, stream, K):
-    """Two extra figures on the same pools: the host link's copy-engine peak
-    (one large contiguous cudaMemcpyAsync each way from the pinned pool, the
-    measured roofline of the link) and the duplex rate (the H2D of batch k
-    and the D2H of batch k+1 in flight together on two streams)."""
-    n = min(S.batch_bytes, 2 << 30)
-    gbuf = torch.empty(n, dtype=torch.uint8, device="cuda")
-    hbuf = S.cpu.view(torch.uint8)[:n]
+def mode_kwargs(args):
+    if args.mode == "sm":
+        return {"ce_min_run_bytes": 0}, False
+    if args.mode == "ce":
+        return {}, True
+    if args.mode == "hybrid":
+        return {"ce_min_run_bytes": args.ce_min_run_bytes}, False
+    return {}, False
+
+
+def measure_link_peaks(S, stream):
+    """The host link's copy-engine rate on the same pinned pool: one large
+    contiguous cudaMemcpyAsync each way, and both ways at once (the measured
+    roofline of the path)."""
+    n = min(max(S.step_bytes.values()), 2 << 30)
+    g1 = torch.empty(n, dtype=torch.uint8, device="cuda")
+    g2 = torch.empty(n, dtype=torch.uint8, device="cuda")
+    h1 = S.cpu.view(torch.uint8)[:n]
+    h2 = S.cpu.view(torch.uint8)[n:2 * n]
+    side = torch.cuda.Stream()
     peak = {}
-    for name, fn in (("h2d", lambda: gbuf.copy_(hbuf, non_blocking=True)),
-                     ("d2h", lambda: hbuf.copy_(gbuf, non_blocking=True))):
+
+    def timed(fn):
         fn()
+        torch.cuda.synchronize()
         ts = []
         for _ in range(3):
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -269,184 +318,309 @@ def measure_extras(S, plans, stream, K):
             b.record(stream)
             torch.cuda.synchronize()
             ts.append(a.elapsed_time(b))
-        peak[name] = round(n / (statistics.median(ts) / 1e3) / 1e9, 2)
-    del gbuf
-    side = torch.cuda.Stream()
-    ts = []
-    for k in range(max(K, 3)):
-        h = plans[k % len(plans)][0]
-        d = plans[(k + 1) % len(plans)][1]
-        a, b, c = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-        a.record(stream)
-        side.wait_event(a)
-        h.execute(stream=stream)
-        d.execute(stream=side)
-        c.record(side)
-        stream.wait_event(c)
-        b.record(stream)
-        torch.cuda.synchronize()
-        ts.append(a.elapsed_time(b))
-    duplex = 2 * S.batch_bytes / (statistics.median(ts) / 1e3) / 1e9
-    return {"link_peak_measured": dict(peak, unit="GB/s", bytes=n,
-                                       how="one contiguous cudaMemcpyAsync each way from the pinned pool, median of 3"),
-            "duplex": {"value": round(duplex, 2), "unit": "GB/s",
-                       "how": "H2D of batch k and D2H of batch k+1 at once on two streams (median step)"}}
+        return statistics.median(ts)
+
+    peak["h2d"] = round(n / timed(lambda: g1.copy_(h1, non_blocking=True)) / 1e6, 2)
+    peak["d2h"] = round(n / timed(lambda: h1.copy_(g1, non_blocking=True)) / 1e6, 2)
+
+    def both():
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        side.wait_event(ev)
+        g1.copy_(h1, non_blocking=True)
+        with torch.cuda.stream(side):
+            h2.copy_(g2, non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(side)
+        stream.wait_event(done)
+
+    peak["duplex_total"] = round(2 * n / timed(both) / 1e6, 2)
+    del g1, g2
+    return dict(peak, unit="GB/s", bytes=n,
+                how="contiguous cudaMemcpyAsync from the pinned pool (each way, and both at once), median of 3")
 
 
-def run_ours(args, ws, rank, local, cfg):
+def measure_hash():
+    """XXH64 block hashing: one 1M-token sequence (65536 blocks of 16) and a
+    batch of 256 requests of U[1,32] blocks, on the GPU (device buffers, and
+    host buffers end to end) against the CPU restatement of hash.cpp's loop
+    (oracle, one thread, update+digest per block like the reference)."""
     from flexkv_b200 import c_ext
-    S = Setup(cfg, args.layout, ws, local, args.cpu_blocks)
-    mode_kw = {}
-    use_ce = False
-    if args.mode == "sm":
-        mode_kw["ce_min_run_bytes"] = 0
-    elif args.mode == "ce":
-        use_ce = True
-    elif args.mode == "hybrid":
-        mode_kw["ce_min_run_bytes"] = args.ce_min_run_bytes
-    plans = []
-    for g, c in S.batches:
-        pair = []
-        for h2d in (True, False):
-            pair.append(c_ext.TransferPlan(
-                torch.from_numpy(g), S.ptrs, S.g_kv, S.g_blk, torch.from_numpy(c), S.cpu, S.c_kv,
-                S.c_layer, S.c_blk, S.chunk, 0, args.transfer_sms, h2d, use_ce,
-                cfg.get("mla", False), gpu_layer_bytes=S.gpu_layer_bytes, **mode_kw))
-        plans.append(pair)
-    stats = [p.stats() for p in plans[0]]
-    stream = torch.cuda.current_stream()
-    K, W = args.steps, args.warmup
+    from oracle import oracle as O
+    rng = np.random.default_rng(4)
+    toks = rng.integers(0, 152064, 1 << 20).astype(np.int32).astype(np.int64)
+    tpb = 16
+    nb = toks.size // tpb
+    out = {}
+    h = c_ext.Hasher()
+    dev_t = torch.from_numpy(toks).cuda()
+    dev_o = torch.zeros(nb, dtype=torch.uint64, device="cuda")
+    host_t = torch.from_numpy(toks).pin_memory()
+    host_o = torch.zeros(nb, dtype=torch.uint64)
 
-    def step(k, evs=None):
-        h, d = plans[k % len(plans)]
-        if evs is None:
-            h.execute()
-            d.execute()
-        else:
-            evs[0].record(stream)
-            h.execute(kernel_events=(evs[1], evs[2]))
-            evs[3].record(stream)
-            d.execute(kernel_events=(evs[4], evs[5]))
-            evs[6].record(stream)
+    def gpu_dev():
+        h.reset()
+        c_ext.gen_hashes(h, dev_t, tpb, dev_o)
+        torch.cuda.synchronize()
+
+    def gpu_host():
+        h.reset()
+        c_ext.gen_hashes(h, host_t, tpb, host_o)
+
+    def best(fn, n=5):
+        fn()
+        ts = []
+        for _ in range(n):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return min(ts)
+
+    t_dev, t_host = best(gpu_dev), best(gpu_host)
+    t_cpu = best(lambda: O.gen_hashes(toks, tpb), 3)
+    if not np.array_equal(host_o.numpy(), O.gen_hashes(toks, tpb)):
+        raise RuntimeError("GPU block hashes differ from the oracle")
+    nbytes = toks.nbytes
+    out["single_sequence_1M_tokens"] = {
+        "blocks": nb, "gpu_device_ms": round(t_dev * 1e3, 3), "gpu_host_buffers_ms": round(t_host * 1e3, 3),
+        "cpu_port_1thread_ms": round(t_cpu * 1e3, 3),
+        "gpu_device_gbs": round(nbytes / t_dev / 1e9, 2), "cpu_port_gbs": round(nbytes / t_cpu / 1e9, 2)}
+    sizes = rng.integers(1, 33, 256) * tpb
+    offs = np.concatenate([[0], np.cumsum(sizes)]).tolist()
+    rt = rng.integers(0, 152064, int(sizes.sum())).astype(np.int64)
+    rt_dev = torch.from_numpy(rt).cuda()
+    rt_host = torch.from_numpy(rt).pin_memory()
+
+    def b_dev():
+        c_ext.gen_hashes_batched(rt_dev, offs, tpb)
+        torch.cuda.synchronize()
+
+    t_bd = best(b_dev)
+    t_bh = best(lambda: c_ext.gen_hashes_batched(rt_host, offs, tpb))
+    t_bc = best(lambda: O.gen_hashes_batched(rt, offs, tpb), 3)
+    out["batched_256_requests"] = {
+        "tokens": int(sizes.sum()), "gpu_device_ms": round(t_bd * 1e3, 3),
+        "gpu_host_buffers_ms": round(t_bh * 1e3, 3), "cpu_port_1thread_ms": round(t_bc * 1e3, 3),
+        "gpu_device_mtokens_s": round(sizes.sum() / t_bd / 1e6, 1),
+        "cpu_port_mtokens_s": round(sizes.sum() / t_bc / 1e6, 1)}
+    h.close()
+    return out
+
+
+def run_ours(args, ws, rank, local, cfg, layout, with_hash):
+    from flexkv_b200 import c_ext
+    S = Setup(cfg, layout, ws, local, args.cpu_blocks)
+    kw, use_ce = mode_kwargs(args)
+    conc = cfg["concurrent"]
+    plans = [[c_ext.TransferPlan(torch.from_numpy(g), S.ptrs, S.g_kv, S.g_blk, torch.from_numpy(c),
+                                 S.cpu, S.c_kv, S.c_layer, S.c_blk, S.chunk, 0, args.transfer_sms,
+                                 h2d, use_ce, S.mla, gpu_layer_bytes=S.gpu_layer_bytes, **kw)
+              for g, c, h2d in ops] for ops in S.steps]
+    stream = torch.cuda.current_stream()
+    side = torch.cuda.Stream()
+    K, W = args.steps, args.warmup
+    track_kernels = cfg["kind"] == "batch"
+
+    def new_events(n):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        for e in evs:  # torch creates the CUDA event on its first record
+            e.record(stream)
+        return evs
+
+    def run_step(k, rec=None):
+        """Enqueue step k; rec collects events for timing (None = untimed)."""
+        ops, ps = S.steps[k % len(S.steps)], plans[k % len(plans)]
+        start = rec["start"] if rec is not None else torch.cuda.Event()
+        start.record(stream)
+        if conc:
+            side.wait_event(start)
+        for i, ((g, c, h2d), p) in enumerate(zip(ops, ps)):
+            st = stream if (h2d or not conc) else side
+            if rec is not None and not conc:
+                rec["op"][i][0].record(st)
+            if rec is not None and track_kernels:
+                p.execute(stream=st, kernel_events=(rec["k"][i][0], rec["k"][i][1]))
+            else:
+                p.execute(stream=st)
+            if rec is not None and not conc:
+                rec["op"][i][1].record(st)
+        if conc:
+            if rec is not None:
+                rec["end_side"].record(side)
+                rec["end_main"].record(stream)
+            done = torch.cuda.Event()
+            done.record(side)
+            stream.wait_event(done)
+        if rec is not None:
+            rec["end"].record(stream)
 
     for k in range(W):
-        step(k)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(K)]
-    for row in evs:  # torch creates the CUDA event on first record
-        for e in row:
-            e.record(stream)
+        run_step(k)
+    torch.cuda.synchronize()
+    recs = []
+    for k in range(K):
+        nops = len(S.steps[(W + k) % len(S.steps)])
+        e = new_events(4 + 2 * nops + (2 * nops if track_kernels else 0))
+        rec = {"start": e[0], "end": e[1], "end_main": e[2], "end_side": e[3],
+               "op": [(e[4 + 2 * i], e[5 + 2 * i]) for i in range(nops)]}
+        if track_kernels:
+            b = 4 + 2 * nops
+            rec["k"] = [(e[b + 2 * i], e[b + 2 * i + 1]) for i in range(nops)]
+        recs.append(rec)
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
     with sampler:
         barrier(ws)
         launches0 = c_ext.kernel_launch_count()
-        t_start = torch.cuda.Event(enable_timing=True)
-        t_end = torch.cuda.Event(enable_timing=True)
-        t_start.record(stream)
         for k in range(K):
-            step(W + k, evs[k])
-        t_end.record(stream)
+            run_step(W + k, recs[k])
         torch.cuda.synchronize()
         launches = c_ext.kernel_launch_count() - launches0
         barrier(ws)
-        elapsed_ms = t_start.elapsed_time(t_end)
-        # e2e through the reference-facing call, host id tensors, synchronous
-        host_ids = [(torch.from_numpy(g).pin_memory(), torch.from_numpy(c).pin_memory())
-                    for g, c in S.batches]
+        elapsed_ms = recs[0]["start"].elapsed_time(recs[-1]["end"])
+        # e2e through the reference-facing call with host id tensors
+        host_ops = [[(torch.from_numpy(g).pin_memory(), torch.from_numpy(c).pin_memory(), h)
+                     for g, c, h in ops] for ops in S.steps]
 
-        def call(k, h2d):
-            g, c = host_ids[k % len(host_ids)]
-            c_ext.transfer_kv_blocks(g, S.ptrs, S.g_kv, S.g_blk, c, S.cpu, S.c_kv, S.c_layer,
-                                     S.c_blk, S.chunk, 0, args.transfer_sms, h2d, use_ce,
-                                     cfg.get("mla", False), **mode_kw)
+        def e2e_step(k):
+            for g, c, h2d in host_ops[k % len(host_ops)]:
+                st = stream if (h2d or not conc) else side
+                with torch.cuda.stream(st):
+                    c_ext.transfer_kv_blocks(g, S.ptrs, S.g_kv, S.g_blk, c, S.cpu, S.c_kv,
+                                             S.c_layer, S.c_blk, S.chunk, 0, args.transfer_sms, h2d,
+                                             use_ce, S.mla, synchronous=not conc, **kw)
+            if conc:
+                torch.cuda.synchronize()
 
         for k in range(W):
-            call(k, True)
-            call(k, False)
+            e2e_step(k)
         barrier(ws)
         w0 = time.perf_counter()
         for k in range(K):
-            call(W + k, True)
-            call(W + k, False)
+            e2e_step(W + k)
         torch.cuda.synchronize()
         e2e_s = time.perf_counter() - w0
         barrier(ws)
     clocks = sampler.summary()
-    extras = {} if args.no_extras else measure_extras(S, plans, stream, K)
+    extras = {}
+    if not args.no_extras:
+        extras["link_peak_measured"] = measure_link_peaks(S, stream)
+        if not conc and cfg["kind"] == "batch":
+            ts = []  # the same steps with both directions in flight together
+            for k in range(max(K, 3)):
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                side.wait_event(a)
+                hp, dp = plans[k % len(plans)]
+                hp.execute(stream=stream)
+                dp.execute(stream=side)
+                c = torch.cuda.Event()
+                c.record(side)
+                stream.wait_event(c)
+                b.record(stream)
+                torch.cuda.synchronize()
+                ts.append(a.elapsed_time(b))
+            extras["duplex"] = {"value": round(sum(S.step_bytes.values()) / statistics.median(ts) / 1e6, 2),
+                                "unit": "GB/s",
+                                "how": "the same steps with the H2D and the D2H batch in flight together on two streams"}
+        if with_hash and rank == 0 and ws == 1:
+            extras["hash"] = measure_hash()
 
-    h2d_ms = [evs[k][0].elapsed_time(evs[k][3]) for k in range(K)]
-    d2h_ms = [evs[k][3].elapsed_time(evs[k][6]) for k in range(K)]
-    kh_ms = [evs[k][1].elapsed_time(evs[k][2]) for k in range(K)]
-    kd_ms = [evs[k][4].elapsed_time(evs[k][5]) for k in range(K)]
+    # Per-direction rates.
+    dir_ms = {"h2d": [], "d2h": []}
+    kern_ms = {"h2d": [], "d2h": []}
+    for k, rec in enumerate(recs):
+        ops = S.steps[(W + k) % len(S.steps)]
+        if conc:
+            dir_ms["h2d"].append(rec["start"].elapsed_time(rec["end_main"]))
+            dir_ms["d2h"].append(rec["start"].elapsed_time(rec["end_side"]))
+        else:
+            for d in ("h2d", "d2h"):
+                dir_ms[d].append(sum(rec["op"][i][0].elapsed_time(rec["op"][i][1])
+                                     for i, op in enumerate(ops) if op[2] == (d == "h2d")))
+        if track_kernels:
+            for i, op in enumerate(ops):
+                kern_ms["h2d" if op[2] else "d2h"].append(rec["k"][i][0].elapsed_time(rec["k"][i][1]))
+    sb = S.step_bytes
+    rate = {d: sb[d] / (statistics.mean(dir_ms[d]) / 1e3) / 1e9 for d in ("h2d", "d2h")
+            if sb[d] and statistics.mean(dir_ms[d]) > 0}
+    step_total = sb["h2d"] + sb["d2h"]
     max_elapsed = max_over_ranks(ws, elapsed_ms)
     max_e2e = max_over_ranks(ws, e2e_s)
-    total_bytes = sum_over_ranks(ws, 2.0 * K * S.batch_bytes)
+    total_bytes = sum_over_ranks(ws, float(K * step_total))
     value = total_bytes / (max_elapsed / 1e3) / 1e9
     e2e = total_bytes / max_e2e / 1e9
-    bb = S.batch_bytes
-    h2d_gbs = bb / (statistics.mean(h2d_ms) / 1e3) / 1e9
-    d2h_gbs = bb / (statistics.mean(d2h_ms) / 1e3) / 1e9
-    # Roofline of the transfer op (the SM kernel plus the copy-engine runs it
-    # overlaps with share one host link, so the op is the unit that meets the
-    # link's bound).  Headline: the slower direction.  Peak: the link's
-    # copy-engine rate measured live on the same pool (MEASURED_PEAKS.json
-    # has no host-link figure), with the nominal PCIe Gen5 x16 rate beside it.
-    # DRAM traffic per op: the algorithmic bytes times the (read+write)/payload
-    # ratio of the kernel's ncu capture (profiles/kv_copy_kernel_cfg2_small_full.md).
-    TRAFFIC_RATIO = {"h2d": 0.781, "d2h": 1.016}
     out = None
     if rank == 0:
         lp = extras.get("link_peak_measured")
-        dirs = {"h2d": (h2d_gbs, kh_ms, stats[0]), "d2h": (d2h_gbs, kd_ms, stats[1])}
-        head = min(dirs, key=lambda d: dirs[d][0])
-        ach, kms, st = dirs[head]
-        peak = lp[head] if lp else PCIE_GEN5_X16_GBS
-        roof = {"bound": "pcie", "kernel": f"transfer op {head.upper()} (kv_copy_kernel + copy-engine runs)",
-                "achieved": round(ach, 2), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
-                "traffic": int(bb * TRAFFIC_RATIO[head]),
-                "peak_source": ("measured live: one contiguous cudaMemcpyAsync of 2 GiB on the same "
-                                "pinned pool (MEASURED_PEAKS.json has no host-link figure)") if lp else
-                               "nominal PCIe Gen5 x16 (no live measurement in this run)",
-                "nominal_peak": PCIE_GEN5_X16_GBS, "frac_of_nominal": round(ach / PCIE_GEN5_X16_GBS, 4),
-                "per_direction": {d: {"achieved": round(v[0], 2),
-                                      "peak": (lp[d] if lp else PCIE_GEN5_X16_GBS),
-                                      "frac": round(v[0] / (lp[d] if lp else PCIE_GEN5_X16_GBS), 4)}
-                                  for d, v in dirs.items()}}
-        if st["sm_chunks"] > 0 and statistics.mean(kms) > 0:
-            kmean = statistics.mean(kms)
-            roof["sm_kernel"] = {"name": f"kv_copy_kernel<{head.upper()}>",
-                                 "bytes_per_launch": st["sm_bytes"], "avg_launch_ms": round(kmean, 3),
-                                 "achieved_alongside_copy_engines": round(st["sm_bytes"] / kmean / 1e6, 2),
-                                 "copy_engine_bytes_per_op": st["ce_bytes"]}
+        if conc:
+            ach = step_total / (elapsed_ms / K / 1e3) / 1e9
+            peak = lp["duplex_total"] if lp else 2 * PCIE_GEN5_X16_GBS
+            roof = {"bound": "pcie", "kernel": "transfer step, both directions in flight "
+                    "(kv_copy_kernel + copy-engine runs)", "achieved": round(ach, 2), "peak": peak,
+                    "unit": "GB/s", "frac": round(ach / peak, 4),
+                    "traffic": int(sb["h2d"] * TRAFFIC_RATIO["h2d"] + sb["d2h"] * TRAFFIC_RATIO["d2h"]),
+                    "traffic_unit": "DRAM bytes per step",
+                    "peak_source": ("measured live: contiguous cudaMemcpyAsync both ways at once on the "
+                                    "same pinned pool (MEASURED_PEAKS.json has no host-link figure)") if lp else
+                                   "nominal 2 x PCIe Gen5 x16",
+                    "nominal_peak": 2 * PCIE_GEN5_X16_GBS,
+                    "frac_of_nominal": round(ach / (2 * PCIE_GEN5_X16_GBS), 4)}
+        else:
+            head = min(rate, key=rate.get)
+            peak = lp[head] if lp else PCIE_GEN5_X16_GBS
+            nops_head = len([o for o in S.steps[0] if o[2] == (head == "h2d")])
+            roof = {"bound": "pcie", "kernel": f"transfer op {head.upper()} (kv_copy_kernel + copy-engine runs)",
+                    "achieved": round(rate[head], 2), "peak": peak, "unit": "GB/s",
+                    "frac": round(rate[head] / peak, 4),
+                    "traffic": int(sb[head] * TRAFFIC_RATIO[head] / max(nops_head, 1)),
+                    "traffic_unit": "DRAM bytes per op",
+                    "peak_source": ("measured live: one contiguous cudaMemcpyAsync of up to 2 GiB on the "
+                                    "same pinned pool (MEASURED_PEAKS.json has no host-link figure)") if lp else
+                                   "nominal PCIe Gen5 x16 (no live measurement in this run)",
+                    "nominal_peak": PCIE_GEN5_X16_GBS,
+                    "frac_of_nominal": round(rate[head] / PCIE_GEN5_X16_GBS, 4),
+                    "per_direction": {d: {"achieved": round(rate[d], 2),
+                                          "peak": (lp[d] if lp else PCIE_GEN5_X16_GBS),
+                                          "frac": round(rate[d] / (lp[d] if lp else PCIE_GEN5_X16_GBS), 4)}
+                                      for d in rate}}
+        if track_kernels:
+            st0 = {("h2d" if op[2] else "d2h"): p.stats() for op, p in zip(S.steps[0], plans[0])}
+            roof["sm_kernel"] = {
+                d: {"bytes_per_launch": st0[d]["sm_bytes"], "copy_engine_bytes_per_op": st0[d]["ce_bytes"],
+                    "avg_launch_ms": round(statistics.mean(kern_ms[d]), 3),
+                    "achieved_alongside_copy_engines": round(st0[d]["sm_bytes"] / statistics.mean(kern_ms[d]) / 1e6, 2)}
+                for d in st0 if kern_ms[d] and statistics.mean(kern_ms[d]) > 0}
+        nids = sum(len(g) for g, c, h in S.steps[0])
         out = {
-            "metric": "KV GB/s per GPU and box (H2D/D2H, 1/2/4/8 B200), % of PCIe Gen5 x16 peak",
-            "value": round(value, 3), "unit": "GB/s", "n_gpus": ws, "steps": K, "warmup": W,
-            "ms_per_step": round(max_elapsed / K, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16 (byte copy)", "data": "synthetic",
+            "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": ws, "steps": K,
+            "warmup": W, "ms_per_step": round(max_elapsed / K, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (byte copy)", "data": "synthetic",
             "config": {"workload": args.config + (" (reduced: profiling case)" if (args.batch or args.gpu_blocks) else ""),
-                       "layout": args.layout, "mode": args.mode,
+                       "layout": layout, "mode": args.mode,
+                       "directions": "concurrent" if conc else "sequential",
                        "layers": cfg["layers"], "kv_heads": cfg["heads"], "head_dim": cfg["head_dim"],
-                       "tokens_per_block": cfg["tpb"], "batch_blocks": cfg["batch"],
-                       "batch_bytes_per_direction": bb, "gpu_pool_blocks": cfg["gpu_blocks"],
-                       "cpu_pool_blocks": S.cpu_blocks, "cpu_pool_blocks_requested": cfg["cpu_blocks"],
-                       "run_frac": cfg["run_frac"], "max_run": cfg["max_run"],
+                       "tokens_per_block": cfg["tpb"], "mla": S.mla, "chunk_bytes": S.chunk,
+                       "ops_per_step": len(S.steps[0]), "step_bytes": sb,
+                       "gpu_pool_blocks": cfg["gpu_blocks"], "cpu_pool_blocks": S.cpu_blocks,
+                       "cpu_pool_blocks_requested": cfg["cpu_blocks"],
                        "transfer_sms": args.transfer_sms, "parallelism": f"dp{ws} (independent)",
-                       "l2": "inputs larger than L2 (4 GiB per batch), no flush"},
-            "per_direction_gbs": {"h2d": round(h2d_gbs, 2), "d2h": round(d2h_gbs, 2)},
+                       "l2": "inputs larger than L2, no flush"},
+            "per_direction_gbs": {d: round(v, 2) for d, v in rate.items()},
             "blocks_per_s": round(value * 1e9 / S.block_bytes, 1),
-            "box_roofline_frac": round(value / (PCIE_GEN5_X16_GBS * ws), 4),
+            "box_roofline_frac": round(value / (PCIE_GEN5_X16_GBS * ws * (2 if conc else 1)), 4),
             "roofline": roof,
-            "plan": {"h2d": stats[0], "d2h": stats[1]},
             "e2e": {"value": round(e2e, 3), "unit": "GB/s",
-                    "h2d_bytes_per_step": int(bb + 16 * cfg["batch"] + 8 * cfg["layers"]),
-                    "d2h_bytes_per_step": int(bb),
-                    "how": "flexkv_b200.c_ext.transfer_kv_blocks, pinned host id tensors, synchronous calls, wall clock"},
+                    "h2d_bytes_per_step": int(sb["h2d"] + 16 * nids + 8 * cfg["layers"] * len(S.steps[0])),
+                    "d2h_bytes_per_step": int(sb["d2h"]),
+                    "how": "flexkv_b200.c_ext.transfer_kv_blocks per op, pinned host id tensors, wall clock"},
             "gpu_launches": int(launches), "clocks": clocks,
         }
         out.update(extras)
-    for p in plans:
-        for x in p:
-            x.close()
+    for ps in plans:
+        for p in ps:
+            p.close()
     return out, S
 
 
@@ -457,7 +631,7 @@ def cpu_baseline(S, seconds: float = 8.0):
     from oracle import oracle as O
     cfg = S.cfg
     n = 256
-    g, c = make_batch(n, 512, S.cpu_blocks, 77, cfg["run_frac"], cfg["max_run"])
+    g, c = make_batch(n, 512, S.cpu_blocks, 77, cfg["run_frac"], cfg["max_run"], cfg.get("fixed_run", False))
     layer_bytes = S.gpu_layer_bytes * 512 // cfg["gpu_blocks"]
     imgs = [np.empty(layer_bytes, dtype=np.uint8) for _ in range(cfg["layers"])]
     cpu = S.cpu.view(torch.uint8).numpy()
@@ -467,80 +641,74 @@ def cpu_baseline(S, seconds: float = 8.0):
     while time.perf_counter() - t0 < seconds:
         for h2d in (True, False):
             O.transfer(n, 0, g, imgs, g_kv, S.g_blk, c, cpu, S.c_kv, S.c_layer, S.c_blk, 0,
-                       S.chunk, h2d, cfg.get("mla", False), num_threads=threads)
+                       S.chunk, h2d, S.mla, num_threads=threads)
             moved += n * S.block_bytes
-    dt = time.perf_counter() - t0
+    dt = max(time.perf_counter() - t0, 1e-9)
     return {"value": round(moved / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"{n}-block {S.cpu_layout.type.value} gather+scatter between the host pool and "
                       f"host images of the GPU layers, repeated for {dt:.1f}s"}
 
 
-def run_reference(args, ws, rank, local, cfg):
-    """The reference's transfer.cu (oracle/_ref) the way its worker calls it."""
+def run_reference(args, ws, rank, local, cfg, layout):
+    """The reference's transfer.cu (oracle/_ref) the way its worker calls it:
+    one op at a time, synchronous, transfer_sms=8, pinned ids."""
     from oracle import oracle as O
-    if rank != 0:
-        return None, None
     if not O.reference_available():
         return {"impl": "reference", "unavailable": "oracle/_ref/libref_transfer.so not built "
                 "(needs the reference tree at build time)"}, None
-    S = Setup(cfg, args.layout, 1, local, args.cpu_blocks)
+    S = Setup(cfg, layout, 1, local, args.cpu_blocks)
     ref = O.ref_lib()
     ptrs = S.ptrs.pin_memory()
-    ids = [(torch.from_numpy(g).pin_memory(), torch.from_numpy(c).pin_memory()) for g, c in S.batches]
+    host_ops = [[(torch.from_numpy(g).pin_memory(), torch.from_numpy(c).pin_memory(), h)
+                 for g, c, h in ops] for ops in S.steps]
     stream = torch.cuda.current_stream().cuda_stream
     sms = 8  # flexkv/common/config.py:50-51 worker default
 
-    def call(k, h2d, use_ce=False):
-        g, c = ids[k % len(ids)]
+    def call(g, c, h2d, use_ce=False):
         rc = ref.ref_transfer_kv_blocks(len(g), 0, len(S.layers), g.data_ptr(), ptrs.data_ptr(),
                                         S.g_kv, S.g_blk, c.data_ptr(), S.cpu.data_ptr(), S.c_kv,
                                         S.c_layer, S.c_blk, 0, S.chunk, stream, sms, int(h2d),
-                                        int(use_ce), int(cfg.get("mla", False)))
+                                        int(use_ce), int(S.mla))
         if rc != 0:
             raise RuntimeError(f"reference transfer_kv_blocks CUDA error {rc}")
 
     K, W = args.steps, args.warmup
     for k in range(W):
-        call(k, True)
-        call(k, False)
+        for g, c, h in host_ops[k % len(host_ops)]:
+            call(g, c, h)
     sampler = ClockSampler(local)
+    per = {"h2d": 0.0, "d2h": 0.0}
     with sampler:
         torch.cuda.synchronize()
-        per = {"h2d": [], "d2h": []}
         t0 = time.perf_counter()
         for k in range(K):
-            a = time.perf_counter()
-            call(W + k, True)
-            b = time.perf_counter()
-            call(W + k, False)
-            per["h2d"].append(b - a)
-            per["d2h"].append(time.perf_counter() - b)
+            for g, c, h in host_ops[(W + k) % len(host_ops)]:
+                a = time.perf_counter()
+                call(g, c, h)
+                per["h2d" if h else "d2h"] += time.perf_counter() - a
         dt = time.perf_counter() - t0
         # CE mode (one cudaMemcpyAsync per chunk), one step
         a = time.perf_counter()
-        call(W + K, True, use_ce=True)
-        b = time.perf_counter()
-        call(W + K, False, use_ce=True)
-        ce = (time.perf_counter() - a, b - a, time.perf_counter() - b)
-    bb = S.batch_bytes
-    value = 2 * K * bb / dt / 1e9
+        for g, c, h in host_ops[0]:
+            call(g, c, h, use_ce=True)
+        ce_dt = time.perf_counter() - a
+    sb = S.step_bytes
+    step_total = sb["h2d"] + sb["d2h"]
+    value = K * step_total / dt / 1e9
     out = {
-        "impl": "reference",
-        "metric": "KV GB/s per GPU and box (H2D/D2H, 1/2/4/8 B200), % of PCIe Gen5 x16 peak",
-        "value": round(value, 3), "unit": "GB/s", "n_gpus": ws, "steps": K, "warmup": W,
-        "ms_per_step": round(dt / K * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16 (byte copy)", "data": "synthetic",
-        "config": {"workload": args.config, "layout": args.layout, "transfer_sms": sms,
-                   "batch_blocks": cfg["batch"], "cpu_pool_blocks": S.cpu_blocks,
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": ws,
+        "steps": K, "warmup": W, "ms_per_step": round(dt / K * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (byte copy)", "data": "synthetic",
+        "config": {"workload": args.config, "layout": layout, "transfer_sms": sms,
+                   "directions": "sequential (one op at a time, as the reference worker)",
+                   "ops_per_step": len(S.steps[0]), "step_bytes": sb, "cpu_pool_blocks": S.cpu_blocks,
                    "parallelism": "rank 0 only"},
-        "per_direction_gbs": {"h2d": round(bb / statistics.mean(per["h2d"]) / 1e9, 2),
-                              "d2h": round(bb / statistics.mean(per["d2h"]) / 1e9, 2)},
-        "ce_mode": {"value": round(2 * bb / ce[0] / 1e9, 3), "h2d": round(bb / ce[1] / 1e9, 2),
-                    "d2h": round(bb / ce[2] / 1e9, 2), "unit": "GB/s",
+        "per_direction_gbs": {d: round(K * sb[d] / per[d] / 1e9, 2) for d in per if per[d] > 0},
+        "ce_mode": {"value": round(step_total / ce_dt / 1e9, 3), "unit": "GB/s",
                     "how": "use_ce_transfer=True: one cudaMemcpyAsync per (layer,kv,block) chunk, one step"},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": 1, "kind": "reference",
                          "sample": "the reference's transfer.cu kernel (transfer_sms=8) driven from one "
-                                   "host thread with pinned ids, synchronous per call, full batches"},
+                                   "host thread with pinned ids, synchronous per op, full steps"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "clocks": sampler.summary(),
@@ -555,7 +723,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2_llama3_8b")
-    ap.add_argument("--layout", choices=["LAYERWISE", "BLOCKWISE"], default="LAYERWISE")
+    ap.add_argument("--layout", choices=["LAYERWISE", "BLOCKWISE"], default=None,
+                    help="host pool layout (default: the configuration's)")
     ap.add_argument("--mode", choices=["auto", "sm", "ce", "hybrid"], default="auto")
     ap.add_argument("--ce-min-run-bytes", type=int, default=1 << 20)
     ap.add_argument("--transfer-sms", type=int, default=-1)
@@ -564,7 +733,7 @@ def main():
     ap.add_argument("--batch", type=int, default=0, help="override blocks per batch (profiling case)")
     ap.add_argument("--gpu-blocks", type=int, default=0, help="override the GPU pool size")
     ap.add_argument("--no-extras", action="store_true",
-                    help="skip the link-peak and duplex measurements (profiling runs)")
+                    help="skip the link-peak, duplex and hash measurements (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3 (timing rule)")
@@ -579,10 +748,12 @@ def main():
         cfg["batch"] = args.batch
     if args.gpu_blocks:
         cfg["gpu_blocks"] = args.gpu_blocks
+    layout = args.layout or cfg["layout"]
+    with_hash = args.config == "cfg2_llama3_8b" and not (args.batch or args.gpu_blocks)
     if args.impl == "reference":
-        out, S = run_reference(args, ws, rank, local, cfg)
+        out, S = run_reference(args, ws, rank, local, cfg, layout)
     else:
-        out, S = run_ours(args, ws, rank, local, cfg)
+        out, S = run_ours(args, ws, rank, local, cfg, layout, with_hash)
         if rank == 0 and ws == 1:
             out["cpu_baseline"] = cpu_baseline(S, args.cpu_baseline_seconds)
         elif rank == 0:

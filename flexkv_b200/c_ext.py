@@ -27,6 +27,7 @@ from __future__ import annotations
 import ctypes
 from typing import List, Optional, Sequence
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -337,9 +338,10 @@ def gen_hashes_batched(token_ids: torch.Tensor, seq_offsets: Sequence[int], toke
     hasher (one SequenceMeta each, block.py:49-57).  Sequence s is
     token_ids[seq_offsets[s]:seq_offsets[s+1]]; its floor(len/tpb) hashes
     follow those of sequence s-1 in the output."""
-    offs = torch.as_tensor(list(seq_offsets), dtype=torch.int64)
-    n = offs.numel() - 1
-    total = int(sum((int(offs[i + 1]) - int(offs[i])) // tokens_per_block for i in range(n)))
+    offs_np = np.ascontiguousarray(np.asarray(seq_offsets, dtype=np.int64))
+    offs = torch.from_numpy(offs_np)
+    n = offs_np.size - 1
+    total = int((np.diff(offs_np) // tokens_per_block).sum()) if n > 0 else 0
     if block_hashes is None:
         block_hashes = torch.zeros(total, dtype=torch.uint64, device=token_ids.device)
     if block_hashes.numel() < total:

@@ -168,6 +168,55 @@ __device__ __forceinline__ void stage_tile(uint64_t *buf, const XxhState &s, con
   cp_async_commit();
 }
 
+// One shared-memory tile of kt stripes (tile and block boundaries coincide:
+// SPB divides the 256 stripes of a tile and kt is a multiple of SPB).  The
+// raw words of the next group are loaded from shared memory before the
+// current group's rounds, and the current group's x*P2 products are formed
+// from registers, so nothing on the in-order issue path waits for a load;
+// the per-stripe work left on the dependent chain is add, rotate, multiply.
+// After every SPB stripes the lane values are the snapshot of one block.
+template <int SPB>
+__device__ __forceinline__ void chain_tile_blocks(const uint64_t *buf, int kt, int j, int lane,
+                                                  uint64_t &v, uint64_t *snaps, int64_t &next_b) {
+  constexpr int G = SPB >= 8 ? SPB : 8;  // stripes per group, a multiple of SPB
+  uint64_t wn[G];
+#pragma unroll
+  for (int u = 0; u < G; ++u) wn[u] = u < kt ? buf[4 * u + j] : 0;
+  for (int i = 0; i < kt; i += G) {
+    uint64_t xp[G];
+#pragma unroll
+    for (int u = 0; u < G; ++u) xp[u] = wn[u] * P2;
+#pragma unroll
+    for (int u = 0; u < G; ++u) {
+      const int ii = i + G + u;
+      wn[u] = ii < kt ? buf[4 * ii + j] : 0;
+    }
+#pragma unroll
+    for (int b = 0; b < G / SPB; ++b) {
+      if (i + b * SPB >= kt) break;
+#pragma unroll
+      for (int t = 0; t < SPB; ++t) v = rotl64(v + xp[b * SPB + t], 31) * P1;
+      if (snaps != nullptr && lane < 4) snaps[next_b * 4 + j] = v;
+      ++next_b;
+    }
+  }
+}
+
+// Same for any stripes-per-block count, with a per-stripe block counter.
+__device__ __forceinline__ void chain_tile_generic(const uint64_t *buf, int kt, int j, int lane,
+                                                   uint64_t &v, uint64_t *snaps, int64_t &next_b,
+                                                   int64_t spb) {
+  int64_t in_block = 0;
+  for (int i = 0; i < kt; ++i) {
+    v = rotl64(v + buf[4 * i + j] * P2, 31) * P1;
+    if (++in_block == spb) {
+      if (snaps != nullptr && lane < 4) snaps[next_b * 4 + j] = v;
+      ++next_b;
+      in_block = 0;
+    }
+  }
+}
+
 // Sequential lane chain over stream stripes [0, K) where the stream is
 // mem ++ data[0, len); writes lane snapshots for nb block boundaries (block
 // b ends at stream byte memsize + bb*(b+1)) and the successor state.
@@ -189,8 +238,38 @@ __global__ void __launch_bounds__(32) xxh_chain_kernel(const XxhState *in, XxhSt
     if (lane < 4) snaps[next_b * 4 + j] = v;
     ++next_b;
   }
-  const bool fast = (s.memsize % 8 == 0) && ((reinterpret_cast<uintptr_t>(data) & 7) == 0);
-  if (fast) {
+  const bool data_aligned = (reinterpret_cast<uintptr_t>(data) & 7) == 0;
+  // Common case: nothing buffered and blocks made of whole stripes (tpb a
+  // multiple of 4 tokens).  The words of the next 8 stripes are read from
+  // shared memory and multiplied by P2 before the current 8 rounds run, so
+  // the dependent chain per stripe is only add -> rotate -> multiply.
+  const bool aligned_blocks = s.memsize == 0 && data_aligned && (snaps == nullptr || bb % 32 == 0);
+  const bool fast = (s.memsize % 8 == 0) && data_aligned;
+  if (aligned_blocks) {
+    const uint64_t *data64 = reinterpret_cast<const uint64_t *>(data);
+    const int64_t n_words = 4 * K;
+    const int64_t spb = snaps ? bb / 32 : 1;  // stripes per block (1 when no snapshots)
+    int cur = 0;
+    if (K > 0) stage_tile(tiles[0], s, data64, 0, n_words, lane);
+    for (int64_t t0 = 0; t0 < n_words; t0 += kTileWords) {
+      if (t0 + kTileWords < n_words) stage_tile(tiles[cur ^ 1], s, data64, t0 + kTileWords, n_words, lane);
+      else cp_async_commit();
+      cp_async_wait_1();
+      __syncwarp();
+      const uint64_t *buf = tiles[cur];
+      const int64_t k_tile_end = (t0 + kTileWords) / 4;
+      const int kt = (int)((K < k_tile_end ? K : k_tile_end) - t0 / 4);
+      switch (spb) {
+        case 1: chain_tile_blocks<1>(buf, kt, j, lane, v, snaps, next_b); break;
+        case 2: chain_tile_blocks<2>(buf, kt, j, lane, v, snaps, next_b); break;
+        case 4: chain_tile_blocks<4>(buf, kt, j, lane, v, snaps, next_b); break;
+        case 8: chain_tile_blocks<8>(buf, kt, j, lane, v, snaps, next_b); break;
+        default: chain_tile_generic(buf, kt, j, lane, v, snaps, next_b, spb); break;
+      }
+      __syncwarp();
+      cur ^= 1;
+    }
+  } else if (fast) {
     const uint64_t *data64 = reinterpret_cast<const uint64_t *>(data);
     const int64_t n_words = 4 * K;  // only whole stripes are read here
     int cur = 0;
@@ -289,6 +368,14 @@ __global__ void __launch_bounds__(256) xxh_batched_kernel(const int64_t *tokens,
   for (int64_t b = 0; b < nblk; ++b) {
     const int64_t Lb = bb * (b + 1);
     const int64_t sb = Lb / 32;
+    for (; k + 4 <= sb; k += 4) {  // four independent loads in flight, then four rounds
+      const uint64_t x0 = w[4 * k + j] * P2, x1 = w[4 * k + 4 + j] * P2;
+      const uint64_t x2 = w[4 * k + 8 + j] * P2, x3 = w[4 * k + 12 + j] * P2;
+      v = rotl64(v + x0, 31) * P1;
+      v = rotl64(v + x1, 31) * P1;
+      v = rotl64(v + x2, 31) * P1;
+      v = rotl64(v + x3, 31) * P1;
+    }
     for (; k < sb; ++k) v = xround(v, w[4 * k + j]);
     const uint64_t v0 = __shfl_sync(quad_mask, v, 0, 4);
     const uint64_t v1 = __shfl_sync(quad_mask, v, 1, 4);
@@ -320,7 +407,7 @@ struct DevBuf {
   void *p = nullptr;
   cudaStream_t s = nullptr;
   ~DevBuf() {
-    if (p) cudaFreeAsync(p, s);
+    if (p) scratch_free(p, s);
   }
 };
 
@@ -368,7 +455,7 @@ int device_view(const void *p, int64_t bytes, int device, cudaStream_t s, DevBuf
     return FKV_OK;
   }
   tmp.s = s;
-  FKV_CUDA(cudaMallocAsync(&tmp.p, (size_t)std::max<int64_t>(bytes, 16), s));
+  if (int rc = scratch_alloc(device, (size_t)std::max<int64_t>(bytes, 16), s, &tmp.p)) return rc;
   if (bytes > 0) FKV_CUDA(cudaMemcpyAsync(tmp.p, p, (size_t)bytes, cudaMemcpyHostToDevice, s));
   *out = tmp.p;
   return FKV_OK;
@@ -498,11 +585,11 @@ int fkv_gen_hashes(fkv_hasher *h, const int64_t *token_ids, int64_t num_tokens,
   uint64_t *out_dev_ptr = block_hashes;
   if (!out_is_dev) {
     out_tmp.s = s;
-    FKV_CUDA(cudaMallocAsync(&out_tmp.p, (size_t)num_blocks * 8, s));
+    if (int rc = scratch_alloc(h->device, (size_t)num_blocks * 8, s, &out_tmp.p)) return rc;
     out_dev_ptr = (uint64_t *)out_tmp.p;
   }
   snaps.s = s;
-  FKV_CUDA(cudaMallocAsync(&snaps.p, (size_t)num_blocks * 32, s));
+  if (int rc = scratch_alloc(h->device, (size_t)num_blocks * 32, s, &snaps.p)) return rc;
   XxhState *in = h->states + h->cur;
   if (int rc = run_chain(h, (const uint8_t *)tok_dev, len, bb, num_blocks, (uint64_t *)snaps.p, s)) return rc;
   const int threads = 256;
@@ -551,7 +638,7 @@ int fkv_gen_hashes_batched(const int64_t *token_ids, const int64_t *seq_offsets,
   uint64_t *out_dev_ptr = block_hashes;
   if (!out_is_dev) {
     out_tmp.s = s;
-    FKV_CUDA(cudaMallocAsync(&out_tmp.p, (size_t)total_blocks * 8, s));
+    if (int rc = scratch_alloc(device, (size_t)total_blocks * 8, s, &out_tmp.p)) return rc;
     out_dev_ptr = (uint64_t *)out_tmp.p;
   }
   ThreadDeviceCtx *ctx = nullptr;
@@ -561,7 +648,7 @@ int fkv_gen_hashes_batched(const int64_t *token_ids, const int64_t *seq_offsets,
   if (int rc = acquire_staging(ctx, tb, &stage)) return rc;
   std::memcpy(stage, table.data(), tb);
   tab.s = s;
-  FKV_CUDA(cudaMallocAsync(&tab.p, tb, s));
+  if (int rc = scratch_alloc(device, tb, s, &tab.p)) return rc;
   FKV_CUDA(cudaMemcpyAsync(tab.p, stage, tb, cudaMemcpyHostToDevice, s));
   if (int rc = release_staging(ctx, s)) return rc;
   const int64_t *d_tok_off = (const int64_t *)tab.p;

@@ -1,7 +1,7 @@
 """CPU, world_size 2 over gloo: the data-parallel and tensor-parallel
 sharding of the path, with no collective on the data path.
 
-* DP: each rank derives its own batches (bench.rank_batches) and moves them
+* DP: each rank derives its own batches (bench.rank_steps) and moves them
   with the oracle on its own pools; only the timing reductions cross ranks.
 * TP: both ranks write their own byte slice (offset rank*gpu_chunk) of every
   CPU chunk of one shared host pool (a file-backed mapping standing in for
@@ -35,7 +35,8 @@ def _dp_worker(rank, world, port, out_dir):
     try:
         cfg = dict(layers=3, heads=2, head_dim=64, tpb=16, gpu_blocks=64, cpu_blocks=128, batch=24,
                    run_frac=0.5, max_run=8)
-        batches = bench.rank_batches(cfg, cfg["cpu_blocks"], rank, nbatches=2)
+        steps = bench.rank_steps(dict(cfg, kind="batch"), cfg["cpu_blocks"], rank, nsteps=1)
+        batches = [(g, c) for g, c, h in steps[0]]
         case = Case("dp", 3, 2, 64, 16, 64, 128)
         st = case.strides()
         gpu = [fill_bytes(st["gpu_layer_bytes"], 10 * rank + l) for l in range(3)]
