@@ -234,7 +234,8 @@ def mem_available_bytes() -> int:
 class Setup:
     """Pools, layouts and per-step ops of one rank."""
 
-    def __init__(self, cfg: dict, layout: str, ws: int, local: int, cpu_blocks_override: int = 0):
+    def __init__(self, cfg: dict, layout: str, ws: int, local: int, cpu_blocks_override: int = 0,
+                 gpu_alloc: str = "per-layer"):
         from flexkv_b200 import c_ext
         from flexkv_b200.layout import KVCacheLayout, KVCacheLayoutType
         self.cfg = cfg
@@ -264,10 +265,17 @@ class Setup:
         dev = torch.device(f"cuda:{local}")
         t0 = time.time()
         self.layers = []
-        for _ in range(L):
-            t = torch.empty(per.kv_shape, dtype=torch.bfloat16, device=dev)
-            t.normal_()
-            self.layers.append(t)
+        self.gpu_alloc = gpu_alloc
+        if gpu_alloc == "contiguous":
+            # One allocation viewed as per-layer [kv, N, tpb, H, D] tensors.
+            self._gpu_base = torch.empty((L,) + tuple(per.kv_shape), dtype=torch.bfloat16, device=dev)
+            self._gpu_base.normal_()
+            self.layers = [self._gpu_base[l] for l in range(L)]
+        else:
+            for _ in range(L):
+                t = torch.empty(per.kv_shape, dtype=torch.bfloat16, device=dev)
+                t.normal_()
+                self.layers.append(t)
         self.ptrs = torch.tensor([t.data_ptr() for t in self.layers], dtype=torch.int64)
         t1 = time.time()
         cpu_bytes = self.cpu_layout.get_total_elements() * e
@@ -409,7 +417,7 @@ def measure_hash():
 
 def run_ours(args, ws, rank, local, cfg, layout, with_hash):
     from flexkv_b200 import c_ext
-    S = Setup(cfg, layout, ws, local, args.cpu_blocks)
+    S = Setup(cfg, layout, ws, local, args.cpu_blocks, args.gpu_alloc)
     kw, use_ce = mode_kwargs(args)
     conc = cfg["concurrent"]
     plans = [[c_ext.TransferPlan(torch.from_numpy(g), S.ptrs, S.g_kv, S.g_blk, torch.from_numpy(c),
@@ -598,7 +606,7 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
             "warmup": W, "ms_per_step": round(max_elapsed / K, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (byte copy)", "data": "synthetic",
             "config": {"workload": args.config + (" (reduced: profiling case)" if (args.batch or args.gpu_blocks) else ""),
-                       "layout": layout, "mode": args.mode,
+                       "layout": layout, "mode": args.mode, "gpu_alloc": args.gpu_alloc,
                        "directions": "concurrent" if conc else "sequential",
                        "layers": cfg["layers"], "kv_heads": cfg["heads"], "head_dim": cfg["head_dim"],
                        "tokens_per_block": cfg["tpb"], "mla": S.mla, "chunk_bytes": S.chunk,
@@ -656,7 +664,7 @@ def run_reference(args, ws, rank, local, cfg, layout):
     if not O.reference_available():
         return {"impl": "reference", "unavailable": "oracle/_ref/libref_transfer.so not built "
                 "(needs the reference tree at build time)"}, None
-    S = Setup(cfg, layout, 1, local, args.cpu_blocks)
+    S = Setup(cfg, layout, 1, local, args.cpu_blocks, args.gpu_alloc)
     ref = O.ref_lib()
     ptrs = S.ptrs.pin_memory()
     host_ops = [[(torch.from_numpy(g).pin_memory(), torch.from_numpy(c).pin_memory(), h)
@@ -700,6 +708,7 @@ def run_reference(args, ws, rank, local, cfg, layout):
         "steps": K, "warmup": W, "ms_per_step": round(dt / K * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (byte copy)", "data": "synthetic",
         "config": {"workload": args.config, "layout": layout, "transfer_sms": sms,
+                   "gpu_alloc": args.gpu_alloc,
                    "directions": "sequential (one op at a time, as the reference worker)",
                    "ops_per_step": len(S.steps[0]), "step_bytes": sb, "cpu_pool_blocks": S.cpu_blocks,
                    "parallelism": "rank 0 only"},
@@ -728,6 +737,8 @@ def main():
     ap.add_argument("--mode", choices=["auto", "sm", "ce", "hybrid"], default="auto")
     ap.add_argument("--ce-min-run-bytes", type=int, default=1 << 20)
     ap.add_argument("--transfer-sms", type=int, default=-1)
+    ap.add_argument("--gpu-alloc", choices=["per-layer", "contiguous"], default="per-layer",
+                    help="GPU KV pool as one tensor per layer, or one allocation viewed per layer")
     ap.add_argument("--cpu-blocks", type=int, default=0, help="override the CPU pool size")
     ap.add_argument("--cpu-baseline-seconds", type=float, default=8.0)
     ap.add_argument("--batch", type=int, default=0, help="override blocks per batch (profiling case)")

@@ -34,10 +34,15 @@ namespace {
 constexpr int kThreads = 256;          // 8 warps per CTA
 constexpr int kDefaultSms = 16;        // SM budget when transfer_sms == -1
 // Defaults from interleaved A/B runs on B200 (Llama-3-8B shape, 2048-block
-// batches): runs of >= 1 MiB per (layer,kv) on the copy engines, concurrent
-// with the SM kernel, beat SM-only by 1-3% in both directions; 512 KiB and
-// 2 MiB thresholds and serial schedules do not.
+// batches): runs of >= 1 MiB per (layer,kv) row on the copy engines,
+// concurrent with the SM kernel, beat SM-only by 1-3% in both directions;
+// 512 KiB and 2 MiB thresholds and serial schedules do not.  When a run
+// folds into one descriptor across all layers (uniform layer stride), rows
+// from 128 KiB up go to the copy engines (H2D +2.7% over the unfolded
+// default); folding every block onto the copy engines is slower than the SM
+// kernel (2-D copies of 32 KiB rows) and is used only when asked for.
 constexpr int64_t kDefaultCeMinRunBytes = 1ll << 20;
+constexpr int64_t kDefaultCeMinRunBytesFolded = 128ll << 10;
 constexpr int kDefaultCeStreams = 2;
 constexpr int kDefaultCeSchedule = 0;  // copy engines concurrent with the SM kernel
 
@@ -194,6 +199,30 @@ int max_pitch(int device, int *out) {
   return FKV_OK;
 }
 
+// Whether [a, a+1) and [b, b+1) lie in one device allocation (driver
+// cuMemGetAddressRange, looked up through the runtime so the library has no
+// link-time dependency on libcuda).  A 2-D copy may not span allocations
+// even when they happen to be adjacent in the address space.
+bool same_allocation(const void *a, const void *b) {
+  using GetRange = int (*)(unsigned long long *, size_t *, unsigned long long);
+  static GetRange fn = [] {
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      return (GetRange) nullptr;
+    }
+    return reinterpret_cast<GetRange>(f);
+  }();
+  if (!fn) return false;
+  unsigned long long base_a = 0, base_b = 0;
+  size_t size_a = 0, size_b = 0;
+  if (fn(&base_a, &size_a, (unsigned long long)(uintptr_t)a) != 0) return false;
+  if (fn(&base_b, &size_b, (unsigned long long)(uintptr_t)b) != 0) return false;
+  return base_a == base_b;
+}
+
 }  // namespace
 }  // namespace fkv
 
@@ -229,6 +258,7 @@ struct HostPlan {
   int unroll_idx = 1;
   int num_ce_streams = 0;
   int ce_schedule = 0;
+  bool layer_folded = false;
 };
 
 inline int64_t trunc8(int64_t b) { return (b / 8) * 8; }  // transfer.cu:86-93
@@ -313,13 +343,48 @@ int build_host_plan(const fkv_transfer_desc &d, int device, HostPlan &hp) {
 
   // Split into copy-engine runs and SM chunks.
   const bool ce_all = d.use_ce_transfer != 0;
-  int64_t thr = d.ce_min_run_bytes;
-  if (thr < 0) thr = env_i64("FKV_CE_MIN_RUN_BYTES", kDefaultCeMinRunBytes);
+  const int64_t thr_user = d.ce_min_run_bytes >= 0 ? d.ce_min_run_bytes : env_i64("FKV_CE_MIN_RUN_BYTES", -1);
+  const int64_t thr = kDefaultCeMinRunBytes;
+  const int64_t thr_folded = kDefaultCeMinRunBytesFolded;
   int mp = 0;
   if (int rc = max_pitch(device, &mp)) return rc;
   const size_t cb = (size_t)hp.copy_bytes;
   const bool contig = (hp.gbs == hp.copy_bytes && hp.cbs == hp.copy_bytes);
   auto pitch_ok = [&](int64_t p) { return p >= hp.copy_bytes && p <= mp; };
+  // Layer folding.  When the GPU layer tensors sit at one uniform stride
+  // equal to kv_dim * gpu_kv_stride (one allocation viewed per layer) and the
+  // CPU layer stride equals kv_dim * cpu_kv_stride (true of both host
+  // layouts), the (layer, kv) chunks of a block are L*kv_dim rows of one
+  // pitch on each side, so a single 2-D copy moves a block -- or a run of
+  // blocks contiguous on both sides -- through every layer at once.
+  bool fold = false;
+  int64_t fold_gp = 0, fold_cp = 0;
+  const int64_t rows = L * KV;
+  if (L > 1) {
+    const char *p0 = (const char *)d.gpu_layer_ptrs[0];
+    const int64_t sg = (int64_t)((const char *)d.gpu_layer_ptrs[1] - p0);
+    bool uniform = sg > 0;
+    for (int64_t l = 2; uniform && l < L; ++l)
+      uniform = ((const char *)d.gpu_layer_ptrs[l] - p0) == l * sg;
+    // The whole folded extent must sit in one allocation.
+    if (uniform) uniform = same_allocation(d.gpu_layer_ptrs[0], (const char *)d.gpu_layer_ptrs[L - 1] + (KV - 1) * hp.gkv);
+    if (uniform) {
+      fold_gp = KV > 1 ? hp.gkv : sg;
+      fold_cp = KV > 1 ? hp.ckv : hp.cls;
+      fold = (KV == 1 || (sg == KV * hp.gkv && hp.cls == KV * hp.ckv)) && pitch_ok(fold_gp) &&
+             pitch_ok(fold_cp);
+    }
+  }
+  hp.layer_folded = fold;
+  auto emit = [&](char *g, char *c, size_t w, size_t h, size_t gp, size_t cp) {
+    CeCopy x;
+    x.width = w;
+    x.height = h;
+    if (hp.h2d) { x.dst = g; x.src = c; x.dpitch = gp; x.spitch = cp; }
+    else        { x.dst = c; x.src = g; x.dpitch = cp; x.spitch = gp; }
+    hp.ce.push_back(x);
+    hp.ce_bytes += (int64_t)(w * h);
+  };
   hp.sm_gpu.reserve(n);
   hp.sm_cpu.reserve(n);
   int64_t i = 0;
@@ -327,7 +392,25 @@ int build_host_plan(const fkv_transfer_desc &d, int device, HostPlan &hp) {
     int64_t r = 1;
     const int64_t g0 = d.gpu_block_ids[i], c0 = d.cpu_block_ids[i];
     while (i + r < n && d.gpu_block_ids[i + r] == g0 + r && d.cpu_block_ids[i + r] == c0 + r) ++r;
-    const bool to_ce = ce_all || (thr > 0 && r * hp.copy_bytes >= thr);
+    const int64_t span = r * hp.copy_bytes;
+    const bool fold_run = fold && contig && fold_gp >= span && fold_cp >= span;
+    // A run goes to the copy engines when its row (one layer and kv half)
+    // is wide enough; a run that folds across all layers becomes a single
+    // descriptor, so a narrower row already pays off.
+    const int64_t row_thr = thr_user >= 0 ? thr_user : (fold_run ? thr_folded : thr);
+    const bool to_ce = ce_all || (row_thr > 0 && span >= row_thr);
+    if (to_ce && (fold_run || (fold && ce_all))) {
+      char *g = (char *)d.gpu_layer_ptrs[0] + g0 * hp.gbs;
+      char *c = (char *)hp.cpu_host_base + c0 * hp.cbs;
+      if (fold_run) {
+        emit(g, c, (size_t)span, (size_t)rows, (size_t)fold_gp, (size_t)fold_cp);
+      } else {
+        for (int64_t k = 0; k < r; ++k)
+          emit(g + k * hp.gbs, c + k * hp.cbs, cb, (size_t)rows, (size_t)fold_gp, (size_t)fold_cp);
+      }
+      i += r;
+      continue;
+    }
     if (!to_ce) {
       for (int64_t k = 0; k < r; ++k) {
         hp.sm_gpu.push_back(g0 + k);
@@ -339,16 +422,6 @@ int build_host_plan(const fkv_transfer_desc &d, int device, HostPlan &hp) {
     for (int64_t l = 0; l < L; ++l) {
       char *gl = (char *)d.gpu_layer_ptrs[l] + g0 * hp.gbs;
       char *cl = (char *)hp.cpu_host_base + l * hp.cls + c0 * hp.cbs;
-      auto emit = [&](char *g, char *c, size_t w, size_t h, size_t gp, size_t cp) {
-        CeCopy x;
-        x.width = w;
-        x.height = h;
-        if (hp.h2d) { x.dst = g; x.src = c; x.dpitch = gp; x.spitch = cp; }
-        else        { x.dst = c; x.src = g; x.dpitch = cp; x.spitch = gp; }
-        hp.ce.push_back(x);
-        hp.ce_bytes += (int64_t)(w * h);
-      };
-      const int64_t span = r * hp.copy_bytes;
       if (contig && (KV == 1 || (hp.gkv >= span && hp.ckv >= span && hp.gkv <= mp && hp.ckv <= mp))) {
         // The run is contiguous on both sides: one row per kv half.
         emit(gl, cl, (size_t)span, (size_t)KV, (size_t)hp.gkv, (size_t)hp.ckv);

@@ -135,9 +135,15 @@ typedef struct fkv_transfer_desc {
   int64_t chunk_size_in_bytes;
   int64_t cpu_pool_bytes;    /* >0: bounds-check every CPU chunk           */
   int64_t gpu_layer_bytes;   /* >0: bounds-check every GPU chunk per layer */
-  int64_t ce_min_run_bytes;  /* <0 default; 0 = SM kernel only; else runs
-                                whose per-(layer,kv) span reaches this many
-                                bytes go to the copy engines              */
+  int64_t ce_min_run_bytes;  /* <0 default (1 MiB; 128 KiB for a run that
+                                folds into one descriptor across all
+                                layers); 0 = SM kernel only; else runs whose
+                                per-(layer,kv) row reaches this many bytes
+                                go to the copy engines.  Folding: when the
+                                GPU layers sit at one uniform stride (one
+                                allocation viewed per layer), a run
+                                contiguous on both sides is one 2-D copy
+                                through every layer.                      */
   int num_ce_streams;        /* <=0 default                               */
   int ce_schedule;           /* -1 default; 0 copy engines concurrent with
                                 the SM kernel; 1 copy engines first; 2 SM

@@ -17,10 +17,30 @@ class Pools:
     """Device layers + pinned host pool holding copies of host images."""
 
     def __init__(self, case: Case, gpu_imgs: List[np.ndarray], cpu_img: np.ndarray,
-                 device: str = "cuda:0"):
+                 device: str = "cuda:0", alloc: str = "separate"):
+        """alloc: "separate" (one tensor per layer, placement up to the
+        allocator), "contiguous" (one allocation viewed per layer: uniform
+        layer stride, which the planner folds), "irregular" (one allocation
+        with uneven gaps between layers: never folded)."""
         self.case = case
         self.st = case.strides()
-        self.layers = [torch.from_numpy(g.copy()).to(device) for g in gpu_imgs]
+        if alloc == "separate":
+            self.layers = [torch.from_numpy(g.copy()).to(device) for g in gpu_imgs]
+        else:
+            nb = self.st["gpu_layer_bytes"]
+            gaps = [0] * len(gpu_imgs) if alloc == "contiguous" else \
+                [256 * ((7 * l) % 5 + 1) for l in range(len(gpu_imgs))]
+            offs, o = [], 0
+            for gp in gaps:
+                o += gp
+                offs.append(o)
+                o += nb
+            self._base = torch.empty(o, dtype=torch.uint8, device=device)
+            self.layers = []
+            for g, off in zip(gpu_imgs, offs):
+                v = self._base[off:off + nb]
+                v.copy_(torch.from_numpy(g))
+                self.layers.append(v)
         self.cpu = torch.from_numpy(cpu_img.copy()).pin_memory()
         self.ptrs = torch.tensor([t.data_ptr() for t in self.layers], dtype=torch.int64)
 

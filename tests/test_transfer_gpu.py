@@ -25,13 +25,14 @@ def golden_inputs(g):
     return case, gids, cids, gpu, cpu
 
 
+@pytest.mark.parametrize("alloc", ["separate", "contiguous"])
 @pytest.mark.parametrize("mode", MODES)
 @pytest.mark.parametrize("idx", range(len(GOLD)), ids=[g["name"] for g in GOLD])
-def test_golden_round_trip(idx, mode):
+def test_golden_round_trip(idx, mode, alloc):
     """D2H then H2D into zeroed layers; both pools match the golden digests."""
     g = GOLD[idx]
     case, gids, cids, gpu, cpu = golden_inputs(g)
-    p = Pools(case, gpu, cpu)
+    p = Pools(case, gpu, cpu, alloc=alloc)
     p.transfer(gids, cids, h2d=False, mode=mode, rank=g["rank"])
     assert sha(p.cpu_image()) == g["d2h_cpu_sha256"]
     for t in p.layers:
@@ -69,10 +70,11 @@ RANDOM_CASES = [
 ]
 
 
+@pytest.mark.parametrize("alloc", ["separate", "contiguous", "irregular"])
 @pytest.mark.parametrize("mode", MODES)
 @pytest.mark.parametrize("ci", range(len(RANDOM_CASES)), ids=[c[0].name for c in RANDOM_CASES])
 @pytest.mark.parametrize("h2d", [False, True], ids=["d2h", "h2d"])
-def test_random_vs_oracle(ci, mode, h2d):
+def test_random_vs_oracle(ci, mode, h2d, alloc):
     case, n, frac, distinct = RANDOM_CASES[ci]
     gids, cids = make_ids(n, case.gpu_blocks, case.cpu_blocks, 1000 + ci, frac, max_run=16,
                           distinct=distinct)
@@ -85,7 +87,7 @@ def test_random_vs_oracle(ci, mode, h2d):
             cids = np.random.default_rng(ci).permutation(case.cpu_blocks)[:n].astype(np.int64)
     gpu, cpu = initial_images(case, 300 + ci, 299)
     rank = case.tp - 1
-    p = Pools(case, gpu, cpu)
+    p = Pools(case, gpu, cpu, alloc=alloc)
     p.transfer(gids, cids, h2d=h2d, mode=mode, rank=rank)
     oracle_transfer(case, gpu, cpu, gids, cids, h2d, rank=rank)
     if h2d:
@@ -194,3 +196,29 @@ def test_async_on_side_stream():
     s.synchronize()
     oracle_transfer(case, gpu, cpu, gids, cids, False)
     assert np.array_equal(p.cpu_image(), cpu)
+
+
+def test_layer_folding_engages_only_for_uniform_layers():
+    """One 2-D copy-engine descriptor per run across all layers when the GPU
+    layers share one allocation; per-layer descriptors otherwise."""
+    from flexkv_b200 import c_ext
+    case = Case("fold", 8, 2, 64, 16, 128, 256)
+    st = case.strides()
+    gids, cids = make_ids(64, 128, 256, 12, 0.5, max_run=8)
+    gpu, cpu = initial_images(case, 1200, 1201)
+    counts = {}
+    for alloc in ("contiguous", "irregular"):
+        p = Pools(case, gpu, cpu, alloc=alloc)
+        plan = c_ext.TransferPlan(torch.from_numpy(gids), p.ptrs, st["gpu_kv"], st["gpu_block"],
+                                  torch.from_numpy(cids), p.cpu, st["cpu_kv"], st["cpu_layer"],
+                                  st["cpu_block"], st["gpu_chunk"], 0, -1, True, True, False)
+        counts[alloc] = plan.stats()["ce_copies"]
+        plan.execute()
+        torch.cuda.synchronize()
+        want = [np.array(x) for x in gpu]
+        oracle_transfer(case, want, cpu.copy(), gids, cids, True)
+        for a, b in zip(p.gpu_images(), want):
+            assert np.array_equal(a, b)
+        plan.close()
+    # per-layer plan: one (kv-row pair) descriptor per layer per run; folded: one per run
+    assert counts["irregular"] == 8 * counts["contiguous"]
