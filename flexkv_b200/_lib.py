@@ -59,6 +59,53 @@ class TransferDesc(ctypes.Structure):
     ]
 
 
+class EngineConfig(ctypes.Structure):
+    """Mirror of ``fkv_engine_config``."""
+
+    _fields_ = [
+        ("num_ranks", c_int),
+        ("num_layers", c_int),
+        ("device_ids", c_vp),
+        ("gpu_layer_ptrs", c_vp),
+        ("cpu_ptr", c_vp),
+        ("cpu_pool_bytes", c_i64),
+        ("gpu_layer_bytes", c_i64),
+        ("gpu_kv_stride_in_bytes", c_i64),
+        ("gpu_block_stride_in_bytes", c_i64),
+        ("gpu_chunk_size_in_bytes", c_i64),
+        ("cpu_kv_stride_in_bytes", c_i64),
+        ("cpu_layer_stride_in_bytes", c_i64),
+        ("cpu_block_stride_in_bytes", c_i64),
+        ("cpu_chunk_size_in_bytes", c_i64),
+        ("is_mla", c_int),
+        ("transfer_sms_h2d", c_int),
+        ("transfer_sms_d2h", c_int),
+        ("use_ce_h2d", c_int),
+        ("use_ce_d2h", c_int),
+        ("reserved", c_int),
+        ("staging_bytes", c_i64),
+    ]
+
+
+class EngineOp(ctypes.Structure):
+    """Mirror of ``fkv_engine_op``."""
+
+    _fields_ = [
+        ("op_id", c_i64),
+        ("type", c_int),
+        ("num_blocks", c_int),
+        ("gpu_block_ids", c_vp),
+        ("cpu_block_ids", c_vp),
+        ("layer_id", c_int),
+        ("layer_granularity", c_int),
+        ("num_predecessors", c_int),
+        ("reserved", c_int),
+        ("predecessors", c_vp),
+    ]
+
+
+FKV_OP_H2D, FKV_OP_D2H, FKV_OP_VIRTUAL = 0, 1, 2
+
 # name -> (restype, argtypes)
 _SIGNATURES = {
     "fkv_last_error": (c_char_p, []),
@@ -96,6 +143,12 @@ _SIGNATURES = {
     "fkv_hasher_digest": (c_int, [c_vp, P_u64, c_vp]),
     "fkv_gen_hashes": (c_int, [c_vp, c_vp, c_i64, c_int, c_vp, c_i64, c_vp]),
     "fkv_gen_hashes_batched": (c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp]),
+    "fkv_engine_config_init": (None, [ctypes.POINTER(EngineConfig)]),
+    "fkv_engine_create": (c_int, [ctypes.POINTER(EngineConfig), ctypes.POINTER(c_vp)]),
+    "fkv_engine_submit_graph": (c_int, [c_vp, c_i64, ctypes.POINTER(EngineOp), c_int]),
+    "fkv_engine_poll": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, ctypes.POINTER(c_int)]),
+    "fkv_engine_pending_ops": (c_i64, [c_vp]),
+    "fkv_engine_destroy": (None, [c_vp]),
     "fkv_transfer_kv_blocks_noalloc": (
         c_int,
         [c_int, c_int, c_int, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64,

@@ -1,0 +1,545 @@
+// In-process transfer engine for one data-parallel group (one GPU, or the
+// GPUs of one tensor-parallel group) — the data-plane half of FlexKV's
+// TransferEngine (flexkv/transfer/transfer_engine.py:197-307) and its GPU
+// workers (flexkv/transfer/worker.py:144-177, 259-342, 402-480).
+//
+// The reference runs a Python scheduler thread that resolves op
+// dependencies on the host, pipes every op to a worker process, pins the
+// block ids on every call and copies synchronously, one op at a time.
+// Here one dispatcher thread owns all CUDA work of the group:
+//   * a submitted graph is ordered topologically and every op is enqueued
+//     at once; a dependency is a cudaStreamWaitEvent on the predecessor's
+//     completion event, resolved on the GPU without a host round trip;
+//   * H2D ops run on one stream and D2H ops on another per GPU, so the two
+//     directions share the full-duplex host link;
+//   * the block-id tables are staged in a page-locked ring owned by the
+//     engine (no per-op pinning), each slice released when its op is done;
+//   * completion is detected by polling the ops' events and reported as
+//     (graph_id, op_id) pairs, op_id = -1 once a whole graph is done — the
+//     shape of TransferEngine.get_completed_graphs_and_ops.
+// A failed op (invalid ids, CUDA error) is reported with its status; its
+// completion event is still recorded so successors are not held back.
+#include <cuda_runtime.h>
+
+#include <chrono>
+#include <condition_variable>
+#include <cstring>
+#include <deque>
+#include <list>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <unordered_map>
+#include <vector>
+
+#include "fkv_common.h"
+
+namespace {
+
+struct Op {
+  int64_t graph_id = 0;
+  int64_t op_id = 0;
+  int type = FKV_OP_H2D;
+  std::vector<int64_t> gpu_ids, cpu_ids;
+  int layer_id = 0;
+  int layer_gran = 0;
+  std::vector<int64_t> preds;
+  std::vector<cudaEvent_t> done;  // per rank
+  std::vector<std::pair<size_t, size_t>> slices;  // ring slices (offset, length)
+  int status = FKV_OK;
+  std::string error;
+  bool completed = false;
+};
+
+struct Graph {
+  int64_t id = 0;
+  std::vector<std::unique_ptr<Op>> ops;
+  int remaining = 0;
+  int status = FKV_OK;
+  std::string error;
+};
+
+struct Completion {
+  int64_t graph_id, op_id;
+  int status;
+};
+
+// Page-locked ring for id tables; slices are released in any order and
+// reclaimed in allocation order.
+class PinnedRing {
+ public:
+  int init(size_t cap) {
+    cap_ = cap;
+    cudaError_t e = cudaHostAlloc((void **)&buf_, cap, cudaHostAllocPortable);
+    if (e != cudaSuccess) return fkv::fail_cuda(e, "cudaHostAlloc(engine ring)");
+    return FKV_OK;
+  }
+  ~PinnedRing() {
+    if (buf_) cudaFreeHost(buf_);
+  }
+  char *base() const { return buf_; }
+  size_t capacity() const { return cap_; }
+  // Reserve len bytes (16-byte granular); false when the ring is full.
+  bool reserve(size_t len, size_t *off) {
+    len = (len + 15) & ~size_t(15);
+    if (len > cap_) return false;
+    if (head_ + len > cap_) {  // skip the tail end
+      if (used_ + (cap_ - head_) + len > cap_) return false;
+      slices_.push_back({head_, cap_ - head_, true});
+      used_ += cap_ - head_;
+      head_ = 0;
+    }
+    if (used_ + len > cap_) return false;
+    *off = head_;
+    slices_.push_back({head_, len, false});
+    head_ = (head_ + len) % cap_;
+    used_ += len;
+    return true;
+  }
+  void release(size_t off) {
+    for (auto &s : slices_)
+      if (!s.free && s.off == off) {
+        s.free = true;
+        break;
+      }
+    while (!slices_.empty() && slices_.front().free) {
+      used_ -= slices_.front().len;
+      slices_.pop_front();
+    }
+    if (slices_.empty()) head_ = 0;
+  }
+
+ private:
+  struct Slice {
+    size_t off, len;
+    bool free;
+  };
+  char *buf_ = nullptr;
+  size_t cap_ = 0, head_ = 0, used_ = 0;
+  std::deque<Slice> slices_;
+};
+
+struct Rank {
+  int device = 0;
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  std::vector<void *> layer_ptrs;
+  std::vector<cudaEvent_t> free_events;
+};
+
+}  // namespace
+
+struct fkv_engine {
+  fkv_engine_config cfg{};
+  std::vector<Rank> ranks;
+  PinnedRing ring;
+
+  std::mutex mu;
+  std::condition_variable cv_work, cv_done;
+  std::deque<std::unique_ptr<Graph>> submitted;
+  std::deque<Completion> completions;
+  bool stop = false;
+  int64_t inflight_ops = 0;
+  std::thread worker;
+  std::string init_error;
+  int init_rc = FKV_OK;
+  bool ready = false;
+
+  // Dispatcher-thread state.
+  std::unordered_map<int64_t, std::unique_ptr<Graph>> live;
+  std::list<Op *> inflight;
+};
+
+namespace {
+
+int make_event(Rank &r, cudaEvent_t *out) {
+  if (!r.free_events.empty()) {
+    *out = r.free_events.back();
+    r.free_events.pop_back();
+    return FKV_OK;
+  }
+  FKV_CUDA(cudaEventCreateWithFlags(out, cudaEventDisableTiming));
+  return FKV_OK;
+}
+
+void push_completion(fkv_engine *e, int64_t g, int64_t op, int status) {
+  {
+    std::lock_guard<std::mutex> lk(e->mu);
+    e->completions.push_back({g, op, status});
+  }
+  e->cv_done.notify_all();
+}
+
+// Enqueue one op on every rank (dispatcher thread).
+void dispatch(fkv_engine *e, Graph &g, Op &op, const std::unordered_map<int64_t, Op *> &by_id) {
+  const fkv_engine_config &c = e->cfg;
+  const int nr = (int)e->ranks.size();
+  op.done.assign(nr, nullptr);
+  const int L = c.num_layers;
+  const int lid = op.layer_id < 0 ? 0 : op.layer_id;
+  const int gran = op.layer_gran < 0 ? L - lid : op.layer_gran;
+  if (op.status == FKV_OK && (lid + gran > L || gran < 0)) {
+    op.status = FKV_ERR_INVALID_ARG;
+    op.error = "layer range exceeds the engine's layers";
+  }
+  for (int r = 0; r < nr; ++r) {
+    Rank &rk = e->ranks[r];
+    cudaSetDevice(rk.device);
+    cudaStream_t s = op.type == FKV_OP_D2H ? rk.d2h : rk.h2d;
+    for (int64_t p : op.preds) {
+      auto it = by_id.find(p);
+      if (it != by_id.end() && it->second->done[r]) cudaStreamWaitEvent(s, it->second->done[r], 0);
+    }
+    if (op.status == FKV_OK && op.type != FKV_OP_VIRTUAL && !op.gpu_ids.empty() && gran > 0) {
+      fkv_transfer_desc d;
+      fkv_transfer_desc_init(&d);
+      d.num_blocks = (int)op.gpu_ids.size();
+      d.start_layer_id = lid;
+      d.num_layers = gran;
+      d.is_host_to_device = op.type == FKV_OP_H2D;
+      d.is_mla = c.is_mla;
+      d.transfer_sms = op.type == FKV_OP_H2D ? c.transfer_sms_h2d : c.transfer_sms_d2h;
+      d.use_ce_transfer = op.type == FKV_OP_H2D ? c.use_ce_h2d : c.use_ce_d2h;
+      d.synchronous = 0;
+      d.gpu_block_ids = op.gpu_ids.data();
+      d.cpu_block_ids = op.cpu_ids.data();
+      d.gpu_layer_ptrs = rk.layer_ptrs.data() + lid;
+      d.cpu_ptr = c.cpu_ptr;
+      d.gpu_kv_stride_in_bytes = c.gpu_kv_stride_in_bytes;
+      d.gpu_block_stride_in_bytes = c.gpu_block_stride_in_bytes;
+      d.cpu_kv_stride_in_bytes = c.cpu_kv_stride_in_bytes;
+      d.cpu_layer_stride_in_bytes = c.cpu_layer_stride_in_bytes;
+      d.cpu_block_stride_in_bytes = c.cpu_block_stride_in_bytes;
+      d.cpu_startoff_inside_chunks = c.is_mla ? 0 : (int64_t)r * c.gpu_chunk_size_in_bytes;
+      d.chunk_size_in_bytes = c.gpu_chunk_size_in_bytes;
+      d.cpu_pool_bytes = c.cpu_pool_bytes;
+      d.gpu_layer_bytes = c.gpu_layer_bytes;
+      const size_t need = fkv::transfer_stage_bytes(d);
+      size_t off = 0;
+      // Wait for ring space by retiring finished ops (bounded by the ring).
+      while (!e->ring.reserve(need, &off)) {
+        if (e->inflight.empty()) {
+          op.status = FKV_ERR_INVALID_ARG;
+          op.error = "id table larger than the engine's staging ring";
+          break;
+        }
+        Op *oldest = e->inflight.front();
+        for (cudaEvent_t ev : oldest->done)
+          if (ev) cudaEventSynchronize(ev);
+        // The poll loop retires it (and frees its slices) on its next pass;
+        // free the slices right away so this op can proceed.
+        for (auto &sl : oldest->slices) e->ring.release(sl.first);
+        oldest->slices.clear();
+      }
+      if (op.status == FKV_OK) {
+        op.slices.push_back({off, need});
+        int rc = fkv::transfer_enqueue(d, s, e->ring.base() + off, need);
+        if (rc != FKV_OK) {
+          op.status = rc;
+          op.error = std::string("rank ") + std::to_string(r) + ": " + fkv_last_error();
+        }
+      }
+    }
+    cudaEvent_t ev = nullptr;
+    if (make_event(rk, &ev) == FKV_OK && cudaEventRecord(ev, s) == cudaSuccess) {
+      op.done[r] = ev;
+    } else {
+      if (ev) rk.free_events.push_back(ev);
+      op.status = FKV_ERR_CUDA;
+      op.error = "could not record the op's completion event";
+    }
+  }
+  e->inflight.push_back(&op);
+  (void)g;
+}
+
+// Retire every in-flight op whose events have all fired (dispatcher thread).
+bool retire(fkv_engine *e) {
+  bool any = false;
+  for (auto it = e->inflight.begin(); it != e->inflight.end();) {
+    Op *op = *it;
+    bool done = true;
+    for (size_t r = 0; r < op->done.size() && done; ++r) {
+      if (!op->done[r]) continue;
+      cudaSetDevice(e->ranks[r].device);
+      cudaError_t q = cudaEventQuery(op->done[r]);
+      if (q == cudaErrorNotReady) {
+        done = false;
+      } else if (q != cudaSuccess) {
+        cudaGetLastError();
+        if (op->status == FKV_OK) {
+          op->status = FKV_ERR_CUDA;
+          op->error = cudaGetErrorString(q);
+        }
+      }
+    }
+    if (!done) {
+      ++it;
+      continue;
+    }
+    any = true;
+    for (auto &sl : op->slices) e->ring.release(sl.first);
+    op->slices.clear();
+    op->completed = true;
+    auto git = e->live.find(op->graph_id);
+    push_completion(e, op->graph_id, op->op_id, op->status);
+    it = e->inflight.erase(it);
+    {
+      std::lock_guard<std::mutex> lk(e->mu);
+      --e->inflight_ops;
+    }
+    if (git != e->live.end()) {
+      Graph &g = *git->second;
+      if (op->status != FKV_OK && g.status == FKV_OK) g.status = op->status;
+      if (--g.remaining == 0) {
+        for (auto &o : g.ops)
+          for (size_t r = 0; r < o->done.size(); ++r)
+            if (o->done[r]) e->ranks[r].free_events.push_back(o->done[r]);
+        push_completion(e, g.id, -1, g.status);
+        e->live.erase(git);
+      }
+    }
+  }
+  return any;
+}
+
+// Order a graph's ops so every op follows its predecessors (Kahn).
+bool topo_order(Graph &g, std::vector<Op *> &order, std::string &err) {
+  std::unordered_map<int64_t, Op *> by_id;
+  for (auto &o : g.ops) {
+    if (!by_id.emplace(o->op_id, o.get()).second) {
+      err = "duplicate op id " + std::to_string(o->op_id);
+      return false;
+    }
+  }
+  std::unordered_map<int64_t, int> indeg;
+  std::unordered_map<int64_t, std::vector<Op *>> succ;
+  for (auto &o : g.ops) {
+    indeg[o->op_id] += 0;
+    for (int64_t p : o->preds) {
+      if (!by_id.count(p)) {
+        err = "op " + std::to_string(o->op_id) + " depends on op " + std::to_string(p) +
+              " outside its graph";
+        return false;
+      }
+      indeg[o->op_id]++;
+      succ[p].push_back(o.get());
+    }
+  }
+  std::deque<Op *> q;
+  for (auto &o : g.ops)
+    if (indeg[o->op_id] == 0) q.push_back(o.get());
+  while (!q.empty()) {
+    Op *o = q.front();
+    q.pop_front();
+    order.push_back(o);
+    for (Op *s : succ[o->op_id])
+      if (--indeg[s->op_id] == 0) q.push_back(s);
+  }
+  if (order.size() != g.ops.size()) {
+    err = "dependency cycle in graph " + std::to_string(g.id);
+    return false;
+  }
+  return true;
+}
+
+void engine_main(fkv_engine *e) {
+  // Per-rank streams are created on this thread (it owns all CUDA work).
+  int rc = FKV_OK;
+  std::string msg;
+  for (auto &r : e->ranks) {
+    cudaError_t ce = cudaSetDevice(r.device);
+    if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&r.h2d, cudaStreamNonBlocking);
+    if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&r.d2h, cudaStreamNonBlocking);
+    if (ce != cudaSuccess) {
+      rc = FKV_ERR_CUDA;
+      msg = std::string("engine stream creation: ") + cudaGetErrorString(ce);
+      break;
+    }
+  }
+  if (rc == FKV_OK) rc = e->ring.init(e->cfg.staging_bytes > 0 ? (size_t)e->cfg.staging_bytes : (32u << 20));
+  if (rc != FKV_OK && msg.empty()) msg = fkv_last_error();
+  {
+    std::lock_guard<std::mutex> lk(e->mu);
+    e->init_rc = rc;
+    e->init_error = msg;
+    e->ready = true;
+  }
+  e->cv_done.notify_all();
+  if (rc != FKV_OK) return;
+
+  for (;;) {
+    std::deque<std::unique_ptr<Graph>> batch;
+    {
+      std::unique_lock<std::mutex> lk(e->mu);
+      if (e->submitted.empty() && e->inflight.empty())
+        e->cv_work.wait(lk, [&] { return e->stop || !e->submitted.empty(); });
+      if (e->stop && e->submitted.empty() && e->inflight.empty()) break;
+      batch.swap(e->submitted);
+    }
+    for (auto &gp : batch) {
+      Graph &g = *gp;
+      std::vector<Op *> order;
+      std::string err;
+      const bool ok = topo_order(g, order, err);
+      g.remaining = (int)g.ops.size();
+      const int64_t gid = g.id;
+      if (!ok) {
+        for (auto &o : g.ops) push_completion(e, gid, o->op_id, FKV_ERR_INVALID_ARG);
+        push_completion(e, gid, -1, FKV_ERR_INVALID_ARG);
+        std::lock_guard<std::mutex> lk(e->mu);
+        e->inflight_ops -= (int64_t)g.ops.size();
+        continue;
+      }
+      std::unordered_map<int64_t, Op *> by_id;
+      for (auto &o : g.ops) by_id[o->op_id] = o.get();
+      e->live[gid] = std::move(gp);
+      Graph &lg = *e->live[gid];
+      if (lg.ops.empty()) {
+        push_completion(e, gid, -1, FKV_OK);
+        e->live.erase(gid);
+        continue;
+      }
+      for (Op *o : order) dispatch(e, lg, *o, by_id);
+    }
+    if (!retire(e)) {
+      // Nothing finished: give the GPU a moment before polling again.
+      std::unique_lock<std::mutex> lk(e->mu);
+      e->cv_work.wait_for(lk, std::chrono::microseconds(50),
+                          [&] { return e->stop || !e->submitted.empty(); });
+    }
+  }
+  for (auto &r : e->ranks) {
+    cudaSetDevice(r.device);
+    for (cudaEvent_t ev : r.free_events) cudaEventDestroy(ev);
+    if (r.h2d) cudaStreamDestroy(r.h2d);
+    if (r.d2h) cudaStreamDestroy(r.d2h);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+void fkv_engine_config_init(fkv_engine_config *c) {
+  std::memset(c, 0, sizeof(*c));
+  c->num_ranks = 1;
+  c->transfer_sms_h2d = -1;
+  c->transfer_sms_d2h = -1;
+}
+
+int fkv_engine_create(const fkv_engine_config *c, fkv_engine **out) {
+  fkv::clear_error();
+  if (!c || !out) return fkv::fail(FKV_ERR_INVALID_ARG, "null config or output");
+  *out = nullptr;
+  if (c->num_ranks <= 0 || c->num_layers <= 0 || !c->gpu_layer_ptrs || !c->cpu_ptr)
+    return fkv::fail(FKV_ERR_INVALID_ARG, "engine needs ranks, layers, layer pointers and a cpu pool");
+  if (!c->is_mla && (int64_t)c->num_ranks * c->gpu_chunk_size_in_bytes > c->cpu_chunk_size_in_bytes &&
+      c->cpu_chunk_size_in_bytes > 0)
+    return fkv::fail(FKV_ERR_INVALID_ARG, "num_ranks * gpu_chunk exceeds cpu_chunk");
+  int ndev = 0;
+  FKV_CUDA(cudaGetDeviceCount(&ndev));
+  auto e = std::make_unique<fkv_engine>();
+  e->cfg = *c;
+  e->ranks.resize(c->num_ranks);
+  for (int r = 0; r < c->num_ranks; ++r) {
+    int dev = c->device_ids ? c->device_ids[r] : r;
+    if (dev < 0 || dev >= ndev)
+      return fkv::fail(FKV_ERR_INVALID_ARG, "engine rank " + std::to_string(r) + " maps to missing device");
+    e->ranks[r].device = dev;
+    e->ranks[r].layer_ptrs.assign(c->gpu_layer_ptrs + (size_t)r * c->num_layers,
+                                  c->gpu_layer_ptrs + (size_t)(r + 1) * c->num_layers);
+  }
+  e->cfg.gpu_layer_ptrs = nullptr;  // copied per rank
+  e->cfg.device_ids = nullptr;
+  fkv_engine *raw = e.get();
+  e->worker = std::thread(engine_main, raw);
+  {
+    std::unique_lock<std::mutex> lk(e->mu);
+    e->cv_done.wait(lk, [&] { return e->ready; });
+  }
+  if (e->init_rc != FKV_OK) {
+    e->worker.join();
+    return fkv::fail(e->init_rc, "engine init failed: " + e->init_error);
+  }
+  *out = e.release();
+  return FKV_OK;
+}
+
+int fkv_engine_submit_graph(fkv_engine *e, int64_t graph_id, const fkv_engine_op *ops, int n_ops) {
+  fkv::clear_error();
+  if (!e) return fkv::fail(FKV_ERR_INVALID_ARG, "null engine");
+  if (n_ops < 0 || (n_ops > 0 && !ops)) return fkv::fail(FKV_ERR_INVALID_ARG, "bad op array");
+  auto g = std::make_unique<Graph>();
+  g->id = graph_id;
+  for (int i = 0; i < n_ops; ++i) {
+    const fkv_engine_op &s = ops[i];
+    if (s.type != FKV_OP_H2D && s.type != FKV_OP_D2H && s.type != FKV_OP_VIRTUAL)
+      return fkv::fail(FKV_ERR_INVALID_ARG, "unknown op type " + std::to_string(s.type));
+    if (s.num_blocks < 0 || (s.num_blocks > 0 && (!s.gpu_block_ids || !s.cpu_block_ids)))
+      return fkv::fail(FKV_ERR_INVALID_ARG, "bad block id arrays for op " + std::to_string(s.op_id));
+    if (s.num_predecessors < 0 || (s.num_predecessors > 0 && !s.predecessors))
+      return fkv::fail(FKV_ERR_INVALID_ARG, "bad predecessor array for op " + std::to_string(s.op_id));
+    auto o = std::make_unique<Op>();
+    o->graph_id = graph_id;
+    o->op_id = s.op_id;
+    o->type = s.type;
+    if (s.type != FKV_OP_VIRTUAL && s.num_blocks > 0) {
+      o->gpu_ids.assign(s.gpu_block_ids, s.gpu_block_ids + s.num_blocks);
+      o->cpu_ids.assign(s.cpu_block_ids, s.cpu_block_ids + s.num_blocks);
+    }
+    o->layer_id = s.layer_id;
+    o->layer_gran = s.layer_granularity;
+    if (s.num_predecessors > 0) o->preds.assign(s.predecessors, s.predecessors + s.num_predecessors);
+    g->ops.push_back(std::move(o));
+  }
+  {
+    std::lock_guard<std::mutex> lk(e->mu);
+    if (e->stop) return fkv::fail(FKV_ERR_INVALID_ARG, "engine is shutting down");
+    e->inflight_ops += n_ops;
+    e->submitted.push_back(std::move(g));
+  }
+  e->cv_work.notify_all();
+  return FKV_OK;
+}
+
+int fkv_engine_poll(fkv_engine *e, int64_t *graph_ids, int64_t *op_ids, int *statuses, int max,
+                    int timeout_ms, int *n_out) {
+  fkv::clear_error();
+  if (!e || !n_out || max < 0) return fkv::fail(FKV_ERR_INVALID_ARG, "bad poll arguments");
+  *n_out = 0;
+  std::unique_lock<std::mutex> lk(e->mu);
+  if (e->completions.empty() && timeout_ms > 0)
+    e->cv_done.wait_for(lk, std::chrono::milliseconds(timeout_ms),
+                        [&] { return !e->completions.empty(); });
+  int n = 0;
+  while (n < max && !e->completions.empty()) {
+    const Completion &c = e->completions.front();
+    if (graph_ids) graph_ids[n] = c.graph_id;
+    if (op_ids) op_ids[n] = c.op_id;
+    if (statuses) statuses[n] = c.status;
+    e->completions.pop_front();
+    ++n;
+  }
+  *n_out = n;
+  return FKV_OK;
+}
+
+int64_t fkv_engine_pending_ops(fkv_engine *e) {
+  if (!e) return 0;
+  std::lock_guard<std::mutex> lk(e->mu);
+  return e->inflight_ops;
+}
+
+void fkv_engine_destroy(fkv_engine *e) {
+  if (!e) return;
+  {
+    std::lock_guard<std::mutex> lk(e->mu);
+    e->stop = true;
+  }
+  e->cv_work.notify_all();
+  if (e->worker.joinable()) e->worker.join();
+  delete e;
+}
+
+}  // extern "C"

@@ -44,6 +44,7 @@ constexpr int kDefaultSms = 16;        // SM budget when transfer_sms == -1
 constexpr int64_t kDefaultCeMinRunBytes = 1ll << 20;
 constexpr int64_t kDefaultCeMinRunBytesFolded = 128ll << 10;
 constexpr int kDefaultCeStreams = 2;
+constexpr int kMaxCeStreams = 8;
 constexpr int kDefaultCeSchedule = 0;  // copy engines concurrent with the SM kernel
 
 struct CopyParams {
@@ -460,7 +461,7 @@ int build_host_plan(const fkv_transfer_desc &d, int device, HostPlan &hp) {
     hp.grid = (int)std::max<int64_t>(grid, 1);
   }
   hp.num_ce_streams = d.num_ce_streams > 0 ? d.num_ce_streams : env_int("FKV_CE_STREAMS", kDefaultCeStreams);
-  hp.num_ce_streams = std::max(1, std::min(hp.num_ce_streams, 8));
+  hp.num_ce_streams = std::max(1, std::min(hp.num_ce_streams, kMaxCeStreams));
   hp.ce_schedule = d.ce_schedule >= 0 ? d.ce_schedule : env_int("FKV_CE_SCHEDULE", kDefaultCeSchedule);
   if (hp.ce_schedule < 0 || hp.ce_schedule > 2)
     return fail(FKV_ERR_INVALID_ARG, "ce_schedule must be -1 (default), 0, 1 or 2");
@@ -510,16 +511,21 @@ int launch_copy(bool h2d, int variant, int grid, const CopyParams &p, cudaStream
 // Fork the side streams from `s`, enqueue the copy-engine descriptors on
 // them (contiguous slices per stream keep each engine's accesses
 // sequential) and, when `join`, make `s` wait for all of them.
+// Each direction has its own side streams (lane 0 = H2D, lane 1 = D2H, up
+// to kMaxCeStreams each), so an H2D transfer and a D2H transfer in flight
+// together never queue their copy-engine work behind each other.
 int fork_ce(ThreadDeviceCtx *ctx, const std::vector<CeCopy> &ce, int nstreams, bool h2d,
             cudaStream_t s) {
-  if (int rc = ensure_side_streams(ctx, nstreams)) return rc;
+  const int base = h2d ? 0 : kMaxCeStreams;
+  if (int rc = ensure_side_streams(ctx, base + nstreams)) return rc;
   FKV_CUDA(cudaEventRecord(ctx->fork_event, s));
-  for (int k = 0; k < nstreams; ++k) FKV_CUDA(cudaStreamWaitEvent(ctx->side_streams[k], ctx->fork_event, 0));
+  for (int k = 0; k < nstreams; ++k)
+    FKV_CUDA(cudaStreamWaitEvent(ctx->side_streams[base + k], ctx->fork_event, 0));
   const cudaMemcpyKind kind = h2d ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost;
   const size_t per = (ce.size() + nstreams - 1) / nstreams;
   for (size_t j = 0; j < ce.size(); ++j) {
     const CeCopy &x = ce[j];
-    cudaStream_t ss = ctx->side_streams[std::min<size_t>(j / per, nstreams - 1)];
+    cudaStream_t ss = ctx->side_streams[base + std::min<size_t>(j / per, nstreams - 1)];
     if (x.height <= 1) {
       FKV_CUDA(cudaMemcpyAsync(x.dst, x.src, x.width, kind, ss));
     } else {
@@ -529,10 +535,11 @@ int fork_ce(ThreadDeviceCtx *ctx, const std::vector<CeCopy> &ce, int nstreams, b
   return FKV_OK;
 }
 
-int join_ce(ThreadDeviceCtx *ctx, int nstreams, cudaStream_t s) {
+int join_ce(ThreadDeviceCtx *ctx, int nstreams, bool h2d, cudaStream_t s) {
+  const int base = h2d ? 0 : kMaxCeStreams;
   for (int k = 0; k < nstreams; ++k) {
-    FKV_CUDA(cudaEventRecord(ctx->join_events[k], ctx->side_streams[k]));
-    FKV_CUDA(cudaStreamWaitEvent(s, ctx->join_events[k], 0));
+    FKV_CUDA(cudaEventRecord(ctx->join_events[base + k], ctx->side_streams[base + k]));
+    FKV_CUDA(cudaStreamWaitEvent(s, ctx->join_events[base + k], 0));
   }
   return FKV_OK;
 }
@@ -557,16 +564,16 @@ int enqueue_transfer(ThreadDeviceCtx *ctx, bool h2d, int variant, int grid, cons
   if (schedule == 0) {  // fork before the kernel so both run together
     if (int rc = fork_ce(ctx, ce, nstreams, h2d, s)) return rc;
     if (int rc = kernel()) return rc;
-    return join_ce(ctx, nstreams, s);
+    return join_ce(ctx, nstreams, h2d, s);
   }
   if (schedule == 1) {
     if (int rc = fork_ce(ctx, ce, nstreams, h2d, s)) return rc;
-    if (int rc = join_ce(ctx, nstreams, s)) return rc;
+    if (int rc = join_ce(ctx, nstreams, h2d, s)) return rc;
     return kernel();
   }
   if (int rc = kernel()) return rc;
   if (int rc = fork_ce(ctx, ce, nstreams, h2d, s)) return rc;
-  return join_ce(ctx, nstreams, s);
+  return join_ce(ctx, nstreams, h2d, s);
 }
 
 int current_device(int *dev) {
@@ -575,6 +582,53 @@ int current_device(int *dev) {
 }
 
 }  // namespace
+}  // namespace fkv
+
+namespace fkv {
+
+size_t transfer_stage_bytes(const fkv_transfer_desc &d) {
+  return 8 * ((size_t)std::max(d.num_layers, 0) + 2 * (size_t)std::max(d.num_blocks, 0));
+}
+
+int transfer_enqueue(const fkv_transfer_desc &d, cudaStream_t s, char *ext_stage, size_t ext_cap) {
+  if (int rc = validate_desc(d)) return rc;
+  if (d.num_blocks == 0 || d.num_layers == 0 || d.chunk_size_in_bytes < 16) return FKV_OK;
+  int device = 0;
+  if (int rc = current_device(&device)) return rc;
+  HostPlan hp;
+  if (int rc = build_host_plan(d, device, hp)) return rc;
+  ThreadDeviceCtx *ctx = nullptr;
+  if (int rc = get_ctx(device, &ctx)) return rc;
+  char *dev_table = nullptr;
+  CopyParams p{};
+  if (!hp.sm_gpu.empty()) {
+    const size_t tb = table_bytes(hp);
+    char *stage = ext_stage;
+    if (stage != nullptr) {
+      if (tb > ext_cap) return fail(FKV_ERR_INVALID_ARG, "staging slice too small for the id table");
+    } else if (int rc = acquire_staging(ctx, tb, &stage)) {
+      return rc;
+    }
+    fill_table(hp, d, reinterpret_cast<int64_t *>(stage));
+    if (int rc = scratch_alloc(device, tb, s, (void **)&dev_table)) return rc;
+    cudaError_t e = cudaMemcpyAsync(dev_table, stage, tb, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) {
+      scratch_free(dev_table, s);
+      return fail_cuda(e, "cudaMemcpyAsync(plan table)");
+    }
+    if (ext_stage == nullptr)
+      if (int rc = release_staging(ctx, s)) return rc;
+    p = make_params(hp, dev_table);
+  }
+  int rc = enqueue_transfer(ctx, hp.h2d, hp.unroll_idx, hp.grid, &p, !hp.sm_gpu.empty(), hp.ce,
+                            hp.num_ce_streams, hp.ce_schedule, s, nullptr, nullptr);
+  if (dev_table) {
+    int rf = scratch_free(dev_table, s);
+    if (rc == FKV_OK) rc = rf;
+  }
+  return rc;
+}
+
 }  // namespace fkv
 
 using namespace fkv;
@@ -610,51 +664,14 @@ int64_t fkv_coalesce_runs(const int64_t *g, const int64_t *c, int64_t n, int64_t
 int fkv_transfer_kv_blocks_ex(const fkv_transfer_desc *d, void *stream_) {
   clear_error();
   if (!d) return fail(FKV_ERR_INVALID_ARG, "null descriptor");
-  if (int rc = validate_desc(*d)) return rc;
-  if (d->num_blocks == 0 || d->num_layers == 0 || d->chunk_size_in_bytes < 16) return FKV_OK;
   cudaStream_t s = (cudaStream_t)stream_;
   const double tstart = profiling() ? now_us() : 0;
-  int device = 0;
-  if (int rc = current_device(&device)) return rc;
-  HostPlan hp;
-  if (int rc = build_host_plan(*d, device, hp)) return rc;
-  ThreadDeviceCtx *ctx = nullptr;
-  if (int rc = get_ctx(device, &ctx)) return rc;
-
-  const bool prof = profiling();
-  const double t0 = prof ? now_us() : 0;
-  char *dev_table = nullptr;
-  CopyParams p{};
-  if (!hp.sm_gpu.empty()) {
-    const size_t tb = table_bytes(hp);
-    char *stage = nullptr;
-    if (int rc = acquire_staging(ctx, tb, &stage)) return rc;
-    fill_table(hp, *d, reinterpret_cast<int64_t *>(stage));
-    if (int rc = scratch_alloc(device, tb, s, (void **)&dev_table)) return rc;
-    cudaError_t e = cudaMemcpyAsync(dev_table, stage, tb, cudaMemcpyHostToDevice, s);
-    if (e != cudaSuccess) {
-      scratch_free(dev_table, s);
-      return fail_cuda(e, "cudaMemcpyAsync(plan table)");
-    }
-    if (int rc = release_staging(ctx, s)) return rc;
-    p = make_params(hp, dev_table);
-  }
-  const double t1 = prof ? now_us() : 0;
-  int rc = enqueue_transfer(ctx, hp.h2d, hp.unroll_idx, hp.grid, &p, !hp.sm_gpu.empty(), hp.ce,
-                            hp.num_ce_streams, hp.ce_schedule, s, nullptr, nullptr);
-  if (dev_table) {
-    int rf = scratch_free(dev_table, s);
-    if (rc == FKV_OK) rc = rf;
-  }
-  if (rc != FKV_OK) return rc;
-  const double t2 = prof ? now_us() : 0;
+  if (int rc = transfer_enqueue(*d, s, nullptr, 0)) return rc;
+  const double t1 = profiling() ? now_us() : 0;
   if (d->synchronous) FKV_CUDA(cudaStreamSynchronize(s));  // transfer.cu:131
-  if (prof) {
-    const double t3 = now_us();
-    std::fprintf(stderr, "[fkv] transfer %s n=%d: plan %.1fus upload %.1fus enqueue %.1fus sync %.1fus (sm %zu blocks, ce %zu copies)\n",
-                 hp.h2d ? "h2d" : "d2h", d->num_blocks, t0 - tstart, t1 - t0, t2 - t1, t3 - t2,
-                 hp.sm_gpu.size(), hp.ce.size());
-  }
+  if (profiling())
+    std::fprintf(stderr, "[fkv] transfer %s n=%d: plan+enqueue %.1fus sync %.1fus\n",
+                 d->is_host_to_device ? "h2d" : "d2h", d->num_blocks, t1 - tstart, now_us() - t1);
   return FKV_OK;
 }
 

@@ -210,6 +210,72 @@ int fkv_tp_group_transfer(fkv_tp_group *g, const int64_t *gpu_block_ids,
 int fkv_tp_group_num_gpus(const fkv_tp_group *g);
 void fkv_tp_group_destroy(fkv_tp_group *g);
 
+/* ---- transfer engine (TransferEngine data plane) ------------------------
+ * Replaces the GPU<->CPU part of flexkv/transfer/transfer_engine.py:197-307
+ * and its worker processes (flexkv/transfer/worker.py:144-177, 259-480):
+ * one engine per data-parallel group (one GPU, or the GPUs of a TP group).
+ * A graph's ops are enqueued at once; a dependency is an event wait on the
+ * GPU; H2D and D2H ops use separate streams per GPU; id tables are staged
+ * in an engine-owned pinned ring; completions are polled as (graph_id,
+ * op_id) pairs with op_id = -1 for a finished graph. */
+#define FKV_OP_H2D 0
+#define FKV_OP_D2H 1
+#define FKV_OP_VIRTUAL 2 /* no data; completes when its predecessors do */
+
+typedef struct fkv_engine fkv_engine;
+
+typedef struct fkv_engine_config {
+  int num_ranks;                /* GPUs of the group (TP ranks)              */
+  int num_layers;
+  const int *device_ids;        /* [num_ranks]; NULL = 0..num_ranks-1        */
+  void *const *gpu_layer_ptrs;  /* rank-major [num_ranks][num_layers]        */
+  void *cpu_ptr;                /* page-locked host pool shared by the ranks */
+  int64_t cpu_pool_bytes;       /* >0: bounds-check CPU chunks               */
+  int64_t gpu_layer_bytes;      /* >0: bounds-check GPU chunks               */
+  int64_t gpu_kv_stride_in_bytes;
+  int64_t gpu_block_stride_in_bytes;
+  int64_t gpu_chunk_size_in_bytes;
+  int64_t cpu_kv_stride_in_bytes;
+  int64_t cpu_layer_stride_in_bytes;
+  int64_t cpu_block_stride_in_bytes;
+  int64_t cpu_chunk_size_in_bytes;
+  int is_mla;
+  int transfer_sms_h2d;         /* -1 = default                              */
+  int transfer_sms_d2h;
+  int use_ce_h2d;               /* copy engines only, per direction          */
+  int use_ce_d2h;
+  int reserved;
+  int64_t staging_bytes;        /* pinned id-table ring; <= 0 = 32 MiB       */
+} fkv_engine_config;
+
+typedef struct fkv_engine_op {
+  int64_t op_id;
+  int type;                     /* FKV_OP_*                                  */
+  int num_blocks;
+  const int64_t *gpu_block_ids; /* host arrays, copied at submission        */
+  const int64_t *cpu_block_ids;
+  int layer_id;                 /* first layer; -1 = 0 (worker.py:318-321)   */
+  int layer_granularity;        /* layers; -1 = all remaining                */
+  int num_predecessors;
+  int reserved;
+  const int64_t *predecessors;  /* op ids of the same graph                  */
+} fkv_engine_op;
+
+/* Zero-fill and set defaults (num_ranks=1, transfer_sms_*=-1). */
+void fkv_engine_config_init(fkv_engine_config *c);
+int fkv_engine_create(const fkv_engine_config *c, fkv_engine **out);
+/* Queue a graph; returns once its ops are copied (non-blocking). */
+int fkv_engine_submit_graph(fkv_engine *e, int64_t graph_id, const fkv_engine_op *ops,
+                            int n_ops);
+/* Up to max completions (graph_id, op_id, status); waits up to timeout_ms
+ * (0 = poll) for the first one. */
+int fkv_engine_poll(fkv_engine *e, int64_t *graph_ids, int64_t *op_ids, int *statuses,
+                    int max, int timeout_ms, int *n_out);
+/* Ops submitted and not yet reported complete. */
+int64_t fkv_engine_pending_ops(fkv_engine *e);
+/* Finish the ops already submitted, then release the engine. */
+void fkv_engine_destroy(fkv_engine *e);
+
 /* ---- XXH64 block hashing (hash.cpp) ------------------------------------ */
 typedef struct fkv_hasher fkv_hasher;
 
