@@ -228,8 +228,12 @@ class TransferEngine:
         self._registered = False
         if not cpu_blocks.is_pinned():
             from .c_ext import cudaHostRegister
-            cudaHostRegister(cpu_blocks)
-            self._registered = True
+            try:
+                cudaHostRegister(cpu_blocks)
+                self._registered = True
+            except RuntimeError as e:  # registered already by the caller
+                if "AlreadyRegistered" not in str(e):
+                    raise
         itemsize = cpu_blocks.element_size()
         self._groups = [
             _GroupEngine(gpu_blocks[d * tp_size:(d + 1) * tp_size], cpu_blocks, gpu_layout, cpu_layout,
