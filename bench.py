@@ -59,6 +59,9 @@ CONFIGS = {
     "cfg5_dsv3_mla": dict(layers=61, heads=1, head_dim=576, tpb=64, gpu_blocks=8192,
                           cpu_blocks=16384, batch=1024, run_frac=0.5, max_run=128, fixed_run=True,
                           mla=True, kind="batch", concurrent=True, layout="BLOCKWISE"),
+    "cfg3_llama3_70b_tp": dict(layers=80, heads=8, head_dim=128, tpb=64, gpu_blocks=4096,
+                               cpu_blocks=8192, batch=512, run_frac=0.0, max_run=1, kind="tp",
+                               concurrent=False, layout="BLOCKWISE"),
     "cfg4_qwen2_7b": dict(layers=28, heads=4, head_dim=128, tpb=16, gpu_blocks=8192,
                           cpu_blocks=16384, requests=256, max_req_blocks=32, run_frac=0.0,
                           max_run=1, kind="requests", concurrent=True, layout="LAYERWISE"),
@@ -691,6 +694,232 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
     return out, S
 
 
+class TPSetup:
+    """A tensor-parallel group of R GPUs in one process:
+    rank r holds heads/R of every layer on cuda:r, and moves its slice to
+    byte offset r*gpu_chunk of every chunk of one shared BLOCKWISE host pool
+    that holds all heads."""
+
+    def __init__(self, cfg: dict, R: int, cpu_blocks_override: int = 0):
+        from flexkv_b200 import c_ext
+        from flexkv_b200.layout import KVCacheLayout, KVCacheLayoutType
+        self.cfg, self.R = cfg, R
+        L, H, D, tpb = cfg["layers"], cfg["heads"], cfg["head_dim"], cfg["tpb"]
+        if H % R:
+            raise ValueError(f"{H} KV heads do not divide over {R} ranks")
+        full = KVCacheLayout(KVCacheLayoutType.LAYERWISE, L, cfg["gpu_blocks"], tpb, H, D)
+        self.gpu_layout = full.div_head(R)
+        per = self.gpu_layout.div_layer(L)
+        e = 2
+        self.g_kv, self.g_blk = per.get_kv_stride() * e, per.get_block_stride() * e
+        self.g_chunk = per.get_chunk_size() * e
+        self.gpu_layer_bytes = per.get_total_elements() * e
+        self.block_bytes = L * 2 * tpb * H * D * e  # all heads: the host chunk
+        fit = int(0.55 * mem_available_bytes() / self.block_bytes)
+        cpu_blocks = cpu_blocks_override or min(cfg["cpu_blocks"], max(fit, 2 * cfg["batch"]))
+        self.cpu_blocks = cpu_blocks
+        self.cpu_layout = KVCacheLayout(KVCacheLayoutType.BLOCKWISE, L, cpu_blocks, tpb, H, D)
+        self.c_kv = self.cpu_layout.get_kv_stride() * e
+        self.c_layer = self.cpu_layout.get_layer_stride() * e
+        self.c_blk = self.cpu_layout.get_block_stride() * e
+        self.c_chunk = self.cpu_layout.get_chunk_size() * e
+        self.layers = []
+        for r in range(R):
+            dev = torch.device(f"cuda:{r}")
+            base = torch.empty((L,) + tuple(per.kv_shape), dtype=torch.bfloat16, device=dev)
+            base.normal_()
+            self.layers.append([base[l] for l in range(L)])
+        self.cpu = torch.empty(self.cpu_layout.get_total_elements(), dtype=torch.bfloat16)
+        c_ext.cudaHostRegister(self.cpu, advise_hugepages=True)
+        log(f"[tp{R}] gpu pool {L} layers x {R} ranks, cpu pool {self.cpu.numel() * 2 / 2**30:.1f} GiB")
+        self.steps = []
+        for s_ in range(4):
+            ops = []
+            for j, h2d in enumerate((True, False)):
+                g, c = make_batch(cfg["batch"], cfg["gpu_blocks"], cpu_blocks, 10 * s_ + j, 0.0, 1)
+                ops.append((g, c, h2d))
+            self.steps.append(ops)
+        self.step_bytes = {"h2d": cfg["batch"] * self.block_bytes, "d2h": cfg["batch"] * self.block_bytes}
+
+    def close(self):
+        from flexkv_b200 import c_ext
+        c_ext.cudaHostUnregister(self.cpu)
+
+
+def run_tp(args, cfg, R):
+    """cfg3: one op = every rank moving its head slice of a 512-block batch;
+    value = device time (CUDA events on each rank's stream, max over ranks),
+    e2e = the same steps through the engine (one TP group of R GPUs)."""
+    from flexkv_b200 import c_ext
+    from flexkv_b200.engine import TransferDescriptor, TransferEngine, TransferOp, TransferOpGraph, TransferType
+    S = TPSetup(cfg, R, args.cpu_blocks)
+    K, W = args.steps, args.warmup
+    streams = [torch.cuda.Stream(device=r) for r in range(R)]
+    plans = [[[c_ext.TransferPlan(torch.from_numpy(g), torch.tensor([t.data_ptr() for t in S.layers[r]]),
+                                  S.g_kv, S.g_blk, torch.from_numpy(c), S.cpu, S.c_kv, S.c_layer, S.c_blk,
+                                  S.g_chunk, 0, args.transfer_sms, h2d, False, False,
+                                  cpu_startoff_inside_chunks=r * S.g_chunk, device=r)
+               for r in range(R)] for g, c, h2d in ops] for ops in S.steps]
+
+    def step(k, evs=None):
+        for oi, per_rank in enumerate(plans[k % 4]):
+            for r, p in enumerate(per_rank):
+                with torch.cuda.device(r):
+                    if evs is not None:
+                        evs[r][2 * oi].record(streams[r])
+                    p.execute(stream=streams[r])
+                    if evs is not None:
+                        evs[r][2 * oi + 1].record(streams[r])
+            for r in range(R):
+                streams[r].synchronize()  # the reference's group joins every op
+
+    for k in range(W):
+        step(k)
+    rec = []
+    for k in range(K):
+        evs = []
+        for r in range(R):
+            with torch.cuda.device(r):
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+                for e_ in ev:
+                    e_.record(streams[r])
+                evs.append(ev)
+        rec.append(evs)
+    for r in range(R):
+        torch.cuda.synchronize(r)
+    sampler = ClockSampler(0)
+    with sampler:
+        for k in range(K):
+            step(W + k, rec[k])
+        for r in range(R):
+            torch.cuda.synchronize(r)
+        eng = TransferEngine(S.layers, S.cpu, S.gpu_layout, S.cpu_layout, tp_size=R)
+        try:
+            def estep(k):
+                ids = []
+                for g, c, h2d in S.steps[k % 4]:
+                    gr = TransferOpGraph()
+                    src, dst = (c, g) if h2d else (g, c)
+                    gr.add_transfer_op(TransferOp(graph_id=gr.graph_id,
+                                                  transfer_type=TransferType.H2D if h2d else TransferType.D2H,
+                                                  src_descriptor=TransferDescriptor(torch.from_numpy(src)),
+                                                  dst_descriptor=TransferDescriptor(torch.from_numpy(dst))))
+                    eng.submit_transfer_graph(gr)
+                    ids.append(gr.graph_id)
+                left = set(ids)
+                while left:
+                    for gid, oid in eng.get_completed_graphs_and_ops(timeout=0.01):
+                        if oid == -1:
+                            left.discard(gid)
+            for k in range(W):
+                estep(k)
+            t0 = time.perf_counter()
+            for k in range(K):
+                estep(W + k)
+            e2e_s = time.perf_counter() - t0
+            failed = dict(eng.failed_ops)
+        finally:
+            eng.shutdown()
+    if failed:
+        raise RuntimeError(f"engine ops failed: {failed}")
+    per = {"h2d": [], "d2h": []}
+    for k in range(K):
+        for oi, d in enumerate(("h2d", "d2h")):
+            per[d].append(max(rec[k][r][2 * oi].elapsed_time(rec[k][r][2 * oi + 1]) for r in range(R)))
+    sb = S.step_bytes
+    rate = {d: sb[d] / (statistics.mean(per[d]) / 1e3) / 1e9 for d in per}
+    step_ms = statistics.mean([per["h2d"][k] + per["d2h"][k] for k in range(K)])
+    value = (sb["h2d"] + sb["d2h"]) / (step_ms / 1e3) / 1e9
+    e2e = K * (sb["h2d"] + sb["d2h"]) / e2e_s / 1e9
+    head = min(rate, key=rate.get)
+    out = {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": R, "steps": K, "warmup": W,
+        "ms_per_step": round(step_ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 (byte copy)", "data": "synthetic",
+        "config": {"workload": args.config, "tp": R, "layout": "BLOCKWISE", "layers": cfg["layers"],
+                   "kv_heads_total": cfg["heads"], "heads_per_rank": cfg["heads"] // R,
+                   "head_dim": cfg["head_dim"], "tokens_per_block": cfg["tpb"],
+                   "gpu_chunk_bytes": S.g_chunk, "cpu_chunk_bytes": S.c_chunk, "batch_blocks": cfg["batch"],
+                   "gpu_pool_blocks": cfg["gpu_blocks"], "cpu_pool_blocks": S.cpu_blocks,
+                   "cpu_pool_blocks_requested": cfg["cpu_blocks"], "parallelism": f"tp{R} (one process)",
+                   "directions": "sequential per op (each op joins all ranks, as the reference group)"},
+        "per_direction_gbs": {d: round(v, 2) for d, v in rate.items()},
+        "box_roofline_frac": round(value / (PCIE_GEN5_X16_GBS * R), 4),
+        "roofline": {"bound": "pcie", "kernel": f"tp transfer op {head.upper()} (all ranks)",
+                     "achieved": round(rate[head], 2), "peak": PCIE_GEN5_X16_GBS * R, "unit": "GB/s",
+                     "frac": round(rate[head] / (PCIE_GEN5_X16_GBS * R), 4), "traffic": None,
+                     "peak_source": "nominal PCIe Gen5 x16 per GPU x ranks"},
+        "e2e": {"value": round(e2e, 3), "unit": "GB/s", "h2d_bytes_per_step": int(sb["h2d"]),
+                "d2h_bytes_per_step": int(sb["d2h"]),
+                "how": "flexkv_b200.engine.TransferEngine over the TP group, one graph per op"},
+        "clocks": sampler.summary(),
+    }
+    for ops in plans:
+        for per_rank in ops:
+            for p in per_rank:
+                p.close()
+    return out, S
+
+
+def run_tp_reference(args, cfg, R):
+    """The reference's group transfer: one host thread per rank, each running
+    its transfer.cu on the rank's device and stream with the rank's byte
+    offset inside the host chunk, then a join (tp_transfer_thread_group.cpp
+    :48-109), driven one op at a time."""
+    from oracle import oracle as O
+    if not O.reference_available():
+        return {"impl": "reference", "unavailable": "oracle/_ref/libref_transfer.so not built"}, None
+    S = TPSetup(cfg, R, args.cpu_blocks)
+    ref = O.ref_lib()
+    ptrs = [torch.tensor([t.data_ptr() for t in S.layers[r]], dtype=torch.int64).pin_memory() for r in range(R)]
+    host_ops = [[(torch.from_numpy(g).pin_memory(), torch.from_numpy(c).pin_memory(), h)
+                 for g, c, h in ops] for ops in S.steps]
+    streams = [torch.cuda.Stream(device=r) for r in range(R)]
+    errors = []
+
+    def rank_call(r, g, c, h2d):
+        torch.cuda.set_device(r)
+        rc = ref.ref_transfer_kv_blocks(len(g), 0, cfg["layers"], g.data_ptr(), ptrs[r].data_ptr(), S.g_kv,
+                                        S.g_blk, c.data_ptr(), S.cpu.data_ptr(), S.c_kv, S.c_layer, S.c_blk,
+                                        r * S.g_chunk, S.g_chunk, streams[r].cuda_stream, 8, int(h2d), 0, 0)
+        if rc != 0:
+            errors.append(rc)
+
+    def group(g, c, h2d):
+        ths = [threading.Thread(target=rank_call, args=(r, g, c, h2d)) for r in range(R)]
+        for t in ths:
+            t.start()
+        for t in ths:
+            t.join()
+        if errors:
+            raise RuntimeError(f"reference transfer CUDA error {errors[0]}")
+
+    K, W = args.steps, args.warmup
+    for k in range(W):
+        for g, c, h in host_ops[k % 4]:
+            group(g, c, h)
+    per = {"h2d": 0.0, "d2h": 0.0}
+    t0 = time.perf_counter()
+    for k in range(K):
+        for g, c, h in host_ops[(W + k) % 4]:
+            a = time.perf_counter()
+            group(g, c, h)
+            per["h2d" if h else "d2h"] += time.perf_counter() - a
+    dt = time.perf_counter() - t0
+    sb = S.step_bytes
+    value = K * (sb["h2d"] + sb["d2h"]) / dt / 1e9
+    out = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": R,
+           "steps": K, "warmup": W, "ms_per_step": round(dt / K * 1e3, 3), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (byte copy)", "data": "synthetic",
+           "config": {"workload": args.config, "tp": R, "transfer_sms": 8, "cpu_pool_blocks": S.cpu_blocks},
+           "per_direction_gbs": {d: round(K * sb[d] / per[d] / 1e9, 2) for d in per},
+           "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": R, "kind": "reference",
+                            "sample": "the reference's transfer.cu per rank from one host thread per rank "
+                                      "(its TP thread group's structure), full steps"},
+           "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    return out, S
+
+
 def cpu_baseline(S, seconds: float = 8.0):
     """The oracle (oracle/oracle.c, the CPU restatement of the reference copy)
     gathering/scattering a 256-block sample of the same workload on host
@@ -802,12 +1031,20 @@ def main():
     ap.add_argument("--cpu-baseline-seconds", type=float, default=8.0)
     ap.add_argument("--batch", type=int, default=0, help="override blocks per batch (profiling case)")
     ap.add_argument("--gpu-blocks", type=int, default=0, help="override the GPU pool size")
+    ap.add_argument("--hash-only", action="store_true",
+                    help="only the XXH64 block-hash measurement (one JSON line)")
+    ap.add_argument("--tp", type=int, default=0,
+                    help="TP ranks for cfg3 (one process drives them; default: all visible GPUs)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the link-peak, duplex and hash measurements (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3 (timing rule)")
         args.warmup = 3
+    if args.hash_only:
+        torch.cuda.set_device(0)
+        print(json.dumps({"hash": measure_hash()}), flush=True)
+        return
     if args.impl == "reference" and int(os.environ.get("RANK", "0")) != 0:
         return  # the reference arm runs on rank 0 only
     if args.impl == "reference":
@@ -820,7 +1057,12 @@ def main():
         cfg["gpu_blocks"] = args.gpu_blocks
     layout = args.layout or cfg["layout"]
     with_hash = args.config == "cfg2_llama3_8b" and not (args.batch or args.gpu_blocks)
-    if args.impl == "reference":
+    if cfg["kind"] == "tp":
+        R = args.tp or torch.cuda.device_count()
+        out, S = (run_tp_reference if args.impl == "reference" else run_tp)(args, cfg, R)
+        if out is not None and args.impl != "reference":
+            out["cpu_baseline"] = None
+    elif args.impl == "reference":
         out, S = run_reference(args, ws, rank, local, cfg, layout)
     else:
         out, S = run_ours(args, ws, rank, local, cfg, layout, with_hash)
