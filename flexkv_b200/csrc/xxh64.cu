@@ -14,7 +14,8 @@
 // sequence, so one sequence is hashed by
 //   xxh_chain_kernel    — one warp; lanes 0..3 run the four XXH64 lanes
 //                         while the whole warp streams the next token tile
-//                         into shared memory with cp.async; the lane values
+//                         into shared memory with cp.async and forms each
+//                         tile's x*P2 products for them; the lane values
 //                         at every block boundary go to a scratch array;
 //   xxh_finalize_kernel — one thread per block: merge + tail + avalanche,
 //                         fully parallel across the grid.
@@ -168,38 +169,240 @@ __device__ __forceinline__ void stage_tile(uint64_t *buf, const XxhState &s, con
   cp_async_commit();
 }
 
-// One shared-memory tile of kt stripes (tile and block boundaries coincide:
-// SPB divides the 256 stripes of a tile and kt is a multiple of SPB).  The
-// raw words of the next group are loaded from shared memory before the
-// current group's rounds, and the current group's x*P2 products are formed
-// from registers, so nothing on the in-order issue path waits for a load;
-// the per-stripe work left on the dependent chain is add, rotate, multiply.
-// After every SPB stripes the lane values are the snapshot of one block.
-template <int SPB>
-__device__ __forceinline__ void chain_tile_blocks(const uint64_t *buf, int kt, int j, int lane,
-                                                  uint64_t &v, uint64_t *snaps, int64_t &next_b) {
-  constexpr int G = SPB >= 8 ? SPB : 8;  // stripes per group, a multiple of SPB
-  uint64_t wn[G];
+// Fused-round path: two warps.  The producer warp reads each tile of 256
+// stripes (8 KiB of tokens) with coalesced loads and writes its x*P2
+// products into a shared ring slot, transposed: row j holds lane j's
+// products, word j of stripe s at index s + 1, with index 0 and index kt + 1
+// zero.  With the one-slot offset the addends of a group of 8 stripes
+// (indices 8g+2 .. 8g+9) are four aligned 16-byte pairs.  The row stride
+// (268 words) keeps the four chain lanes' reads conflict-free and leaves
+// room for their reads one group past the tile end (index <= 8*32 + 9).
+// Lanes 0..3 of the chain warp run only the rounds and write block
+// snapshots into a shared slot; the producer copies those to global
+// memory once the chain has released the slot.  Two slots suffice: a
+// tile's loads and products take a fraction of its chain time.
+constexpr int kProdStride = 268;
+constexpr int kProdSlot = 4 * kProdStride;  // words per product slot
+constexpr int kSnapSlot = 4 * 256;          // words per snapshot slot (up to 256 blocks)
+constexpr int kRawWords = 2 * kTileWords;   // single-warp paths: two raw tiles
+constexpr int kFusedWords = 2 * kProdSlot + 2 * kSnapSlot;
+constexpr int kChainSmemWords = kFusedWords > kRawWords ? kFusedWords : kRawWords;
+constexpr uint32_t P1L = (uint32_t)P1;
+constexpr uint32_t P1H = (uint32_t)(P1 >> 32);
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // a hand-off wait gives up after 2 s
+
+__device__ __forceinline__ uint64_t mad_wide_u32(uint32_t a, uint32_t b, uint64_t c) {
+  uint64_t d;
+  asm("mad.wide.u32 %0, %1, %2, %3;" : "=l"(d) : "r"(a), "r"(b), "l"(c));
+  return d;
+}
+
+// One XXH64 round on a lane value that already holds its stripe input,
+// a = v + x*P2, kept as 32-bit halves:  a <- rotl(a, 31) * P1 + next,
+// where next is the following stripe's x*P2.  The rotation is two funnel
+// shifts; the low half of the 64-bit multiply and the following round's
+// add are one widening multiply-add; the high half adds the two 32-bit
+// cross products.  The dependent path is shift -> multiply-add -> add,
+// against add -> add-with-carry -> shift -> multiply -> ... for the plain
+// 64-bit form.
+__device__ __forceinline__ void fused_round(uint32_t &lo, uint32_t &hi, uint64_t next) {
+  const uint32_t rl = __funnelshift_l(hi, lo, 31);  // low half of rotl(a, 31)
+  const uint32_t rh = __funnelshift_l(lo, hi, 31);  // high half
+  const uint64_t w = mad_wide_u32(rl, P1L, next);
+  lo = (uint32_t)w;
+  hi = (uint32_t)(w >> 32) + rh * P1L + rl * P1H;
+}
+
+__device__ __forceinline__ uint64_t join64(uint32_t lo, uint32_t hi) {
+  return ((uint64_t)hi << 32) | lo;
+}
+
+__device__ __forceinline__ void load_group(const uint64_t *p, uint64_t (&x)[8]) {
+  const ulonglong2 *q = reinterpret_cast<const ulonglong2 *>(p);
 #pragma unroll
-  for (int u = 0; u < G; ++u) wn[u] = u < kt ? buf[4 * u + j] : 0;
-  for (int i = 0; i < kt; i += G) {
-    uint64_t xp[G];
+  for (int k = 0; k < 4; ++k) {
+    const ulonglong2 t = q[k];
+    x[2 * k] = t.x;
+    x[2 * k + 1] = t.y;
+  }
+}
+
+// Eight rounds; x[u] is the addend folded in by stripe u's round (the next
+// stripe's product).  A block's snapshot is the held value minus the
+// addend already folded in, computed off the chain, stored to sn (stride 4
+// words per block).
+template <int SPB, bool SNAP>
+__device__ __forceinline__ void group_rounds(const uint64_t (&x)[8], uint32_t &lo, uint32_t &hi,
+                                             uint64_t *sn) {
 #pragma unroll
-    for (int u = 0; u < G; ++u) xp[u] = wn[u] * P2;
+  for (int u = 0; u < 8; ++u) {
+    fused_round(lo, hi, x[u]);
+    if (SNAP && u % SPB == SPB - 1) sn[(u / SPB) * 4] = join64(lo, hi) - x[u];
+  }
+}
+
+// One chain lane over one tile of kt stripes (tile and block boundaries
+// coincide: SPB divides the 256 stripes of a tile and kt is a multiple of
+// SPB).  pj is the lane's product row; sn is the lane's column of the
+// tile's snapshot slot (block k of the tile at sn[4k]).  Groups of 8
+// stripes run from registers loaded one group ahead, in two alternating
+// buffers; the stripes of a last partial group run block by block.  The
+// tile's final round folds in the zero at index kt + 1, so v leaves exact.
+template <int SPB, bool SNAP>
+__device__ __forceinline__ void chain_tile_fused(const uint64_t *pj, int kt, uint64_t &v, uint64_t *sn) {
+  static_assert(SPB == 1 || SPB == 2 || SPB == 4 || SPB == 8, "blocks must tile a group of 8 stripes");
+  static_assert(8 * 32 + 9 < kProdStride, "product row too short for the pipeline");
+  const uint64_t a = v + pj[1];
+  uint32_t lo = (uint32_t)a, hi = (uint32_t)(a >> 32);
+  const int ng = kt / 8;
+  uint64_t A[8], B[8];
+  load_group(pj + 2, A);
+  int g = 0;
+  for (; g + 2 <= ng; g += 2) {
+    load_group(pj + 8 * g + 10, B);
+    group_rounds<SPB, SNAP>(A, lo, hi, sn + 4 * (8 * g / SPB));
+    load_group(pj + 8 * g + 18, A);
+    group_rounds<SPB, SNAP>(B, lo, hi, sn + 4 * (8 * (g + 1) / SPB));
+  }
+  if (g < ng) {
+    group_rounds<SPB, SNAP>(A, lo, hi, sn + 4 * (8 * g / SPB));
+    ++g;
+  }
+  for (int st = 8 * g; st < kt; st += SPB) {
 #pragma unroll
-    for (int u = 0; u < G; ++u) {
-      const int ii = i + G + u;
-      wn[u] = ii < kt ? buf[4 * ii + j] : 0;
+    for (int t = 0; t < SPB; ++t) fused_round(lo, hi, pj[st + t + 2]);
+    if (SNAP) sn[4 * (st / SPB)] = join64(lo, hi) - pj[st + SPB + 1];
+  }
+  v = join64(lo, hi);
+}
+
+// Producer warp: products of one tile of kt stripes whose words start at
+// src, into product slot pr.  16-byte loads when src is 16-byte aligned,
+// 8-byte loads otherwise; eight loads in flight per lane.
+__device__ __forceinline__ void produce_tile(const uint64_t *src, int kt, uint64_t *pr, int lane,
+                                             bool al16) {
+  const int nw = 4 * kt;
+  if (al16) {
+    const ulonglong2 *s2 = reinterpret_cast<const ulonglong2 *>(src);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      ulonglong2 x[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int q = lane + 32 * (8 * h + i);  // words 2q, 2q+1: stripe q/2, lanes 2(q&1), +1
+        if (2 * q < nw) x[i] = __ldg(s2 + q);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int q = lane + 32 * (8 * h + i);
+        if (2 * q < nw) {
+          const int at = 2 * (q & 1) * kProdStride + (q >> 1) + 1;
+          pr[at] = x[i].x * P2;
+          pr[at + kProdStride] = x[i].y * P2;
+        }
+      }
     }
+  } else {
+#pragma unroll 1
+    for (int h = 0; h < 4; ++h) {
+      uint64_t x[8];
 #pragma unroll
-    for (int b = 0; b < G / SPB; ++b) {
-      if (i + b * SPB >= kt) break;
+      for (int i = 0; i < 8; ++i) {
+        const int w = lane + 32 * (8 * h + i);
+        if (w < nw) x[i] = __ldg(src + w);
+      }
 #pragma unroll
-      for (int t = 0; t < SPB; ++t) v = rotl64(v + xp[b * SPB + t], 31) * P1;
-      if (snaps != nullptr && lane < 4) snaps[next_b * 4 + j] = v;
-      ++next_b;
+      for (int i = 0; i < 8; ++i) {
+        const int w = lane + 32 * (8 * h + i);
+        if (w < nw) pr[(w & 3) * kProdStride + (w >> 2) + 1] = x[i] * P2;
+      }
     }
   }
+  if (kt < 256 && lane < 4) pr[lane * kProdStride + kt + 1] = 0;
+}
+
+__device__ __forceinline__ unsigned smem_u32(const void *p) {
+  return (unsigned)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *b, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(b))
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Wait for the phase of the given parity to complete; false (and the
+// caller's error word set) if it does not within kWaitLimitNs.
+__device__ __noinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *err) {
+  if (mbar_try_wait(b, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(b, parity)) {
+    if (global_ns() - t0 > kWaitLimitNs) {
+      *err = FKV_ERR_TIMEOUT;
+      return false;
+    }
+  }
+  return true;
+}
+
+// The two-warp chain over K stripes of aligned data.  Returns false on a
+// timed-out hand-off (error word set).
+template <int SPB, bool SNAP>
+__device__ bool chain_fused(const uint64_t *data64, bool al16, int64_t K, uint64_t *smem, uint64_t *bars,
+                            int warp, int lane, uint64_t &v, uint64_t *snaps, volatile int *err) {
+  uint64_t *prod = smem;                   // [2][kProdSlot]
+  uint64_t *snap = smem + 2 * kProdSlot;   // [2][kSnapSlot]
+  uint64_t *full = bars, *empty = bars + 2;
+  const int64_t T = (K + 255) / 256;
+  constexpr int kBlocksPerTile = 256 / SPB;
+  auto tile_stripes = [&](int64_t t) { return (int)(K - 256 * t < 256 ? K - 256 * t : 256); };
+  if (warp == 1) {
+    for (int64_t t = 0; t < T; ++t) {
+      const int sl = (int)(t & 1);
+      if (t >= 2) {  // slot sl held tile t-2 (a full tile): wait for the chain, drain its snapshots
+        if (!mbar_wait(&empty[sl], (uint32_t)(((t >> 1) - 1) & 1), err)) return false;
+        if (SNAP) {
+          uint64_t *dst = snaps + 4 * (t - 2) * kBlocksPerTile;
+          for (int k = lane; k < 4 * kBlocksPerTile; k += 32) dst[k] = snap[sl * kSnapSlot + k];
+        }
+      }
+      produce_tile(data64 + 1024 * t, tile_stripes(t), prod + sl * kProdSlot, lane, al16);
+      mbar_arrive(&full[sl]);
+    }
+    for (int64_t t = T >= 2 ? T - 2 : 0; t < T; ++t) {  // the last one or two tiles
+      const int sl = (int)(t & 1);
+      if (!mbar_wait(&empty[sl], (uint32_t)((t >> 1) & 1), err)) return false;
+      if (SNAP) {
+        uint64_t *dst = snaps + 4 * t * kBlocksPerTile;
+        const int n = 4 * (tile_stripes(t) / SPB);
+        for (int k = lane; k < n; k += 32) dst[k] = snap[sl * kSnapSlot + k];
+      }
+    }
+  } else if (lane < 4) {
+    for (int64_t t = 0; t < T; ++t) {
+      const int sl = (int)(t & 1);
+      if (!mbar_wait(&full[sl], (uint32_t)((t >> 1) & 1), err)) return false;
+      chain_tile_fused<SPB, SNAP>(prod + sl * kProdSlot + lane * kProdStride, tile_stripes(t), v,
+                                  snap + sl * kSnapSlot + lane);
+      mbar_arrive(&empty[sl]);
+    }
+  }
+  return true;
 }
 
 // Same for any stripes-per-block count, with a per-stripe block counter.
@@ -220,12 +423,19 @@ __device__ __forceinline__ void chain_tile_generic(const uint64_t *buf, int kt, 
 // Sequential lane chain over stream stripes [0, K) where the stream is
 // mem ++ data[0, len); writes lane snapshots for nb block boundaries (block
 // b ends at stream byte memsize + bb*(b+1)) and the successor state.
-// Launch: 1 block of 32 threads.
-__global__ void __launch_bounds__(32) xxh_chain_kernel(const XxhState *in, XxhState *out,
+// Launch: 1 block of 64 threads.  With nothing buffered, 8-byte aligned
+// data and blocks of 1, 2, 4 or 8 whole stripes (every gen_hashes call
+// with tpb a multiple of 4 tokens, and every update of aligned data) the
+// two warps run the fused path; otherwise warp 0 runs alone.  err is a
+// host-visible word set to FKV_ERR_TIMEOUT if a hand-off wait ran out.
+__global__ void __launch_bounds__(64) xxh_chain_kernel(const XxhState *in, XxhState *out,
                                                        const uint8_t *data, int64_t len,
-                                                       int64_t bb, int64_t nb, uint64_t *snaps) {
-  __shared__ __align__(16) uint64_t tiles[2][kTileWords];
-  const int lane = threadIdx.x;
+                                                       int64_t bb, int64_t nb, uint64_t *snaps,
+                                                       int *err) {
+  __shared__ __align__(16) uint64_t smem[kChainSmemWords];
+  __shared__ __align__(8) uint64_t bars[4];  // full[2], empty[2]
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
   const XxhState s = *in;
   const int j = lane & 3;
   uint64_t v = s.v[j];
@@ -233,60 +443,87 @@ __global__ void __launch_bounds__(32) xxh_chain_kernel(const XxhState *in, XxhSt
   const int64_t K = stream_len / 32;  // stripes consumed by this call
   int64_t next_b = 0;
   auto boundary_stripes = [&](int64_t b) -> int64_t { return ((int64_t)s.memsize + bb * (b + 1)) / 32; };
-  // Boundaries reached before any stripe of this call.
-  while (snaps && next_b < nb && boundary_stripes(next_b) == 0) {
-    if (lane < 4) snaps[next_b * 4 + j] = v;
-    ++next_b;
-  }
   const bool data_aligned = (reinterpret_cast<uintptr_t>(data) & 7) == 0;
-  // Common case: nothing buffered and blocks made of whole stripes (tpb a
-  // multiple of 4 tokens).  The words of the next 8 stripes are read from
-  // shared memory and multiplied by P2 before the current 8 rounds run, so
-  // the dependent chain per stripe is only add -> rotate -> multiply.
   const bool aligned_blocks = s.memsize == 0 && data_aligned && (snaps == nullptr || bb % 32 == 0);
-  const bool fast = (s.memsize % 8 == 0) && data_aligned;
-  if (aligned_blocks) {
-    const uint64_t *data64 = reinterpret_cast<const uint64_t *>(data);
-    const int64_t n_words = 4 * K;
-    const int64_t spb = snaps ? bb / 32 : 1;  // stripes per block (1 when no snapshots)
-    int cur = 0;
-    if (K > 0) stage_tile(tiles[0], s, data64, 0, n_words, lane);
-    for (int64_t t0 = 0; t0 < n_words; t0 += kTileWords) {
-      if (t0 + kTileWords < n_words) stage_tile(tiles[cur ^ 1], s, data64, t0 + kTileWords, n_words, lane);
-      else cp_async_commit();
-      cp_async_wait_1();
-      __syncwarp();
-      const uint64_t *buf = tiles[cur];
-      const int64_t k_tile_end = (t0 + kTileWords) / 4;
-      const int kt = (int)((K < k_tile_end ? K : k_tile_end) - t0 / 4);
-      switch (spb) {
-        case 1: chain_tile_blocks<1>(buf, kt, j, lane, v, snaps, next_b); break;
-        case 2: chain_tile_blocks<2>(buf, kt, j, lane, v, snaps, next_b); break;
-        case 4: chain_tile_blocks<4>(buf, kt, j, lane, v, snaps, next_b); break;
-        case 8: chain_tile_blocks<8>(buf, kt, j, lane, v, snaps, next_b); break;
-        default: chain_tile_generic(buf, kt, j, lane, v, snaps, next_b, spb); break;
-      }
-      __syncwarp();
-      cur ^= 1;
+  const int64_t spb = snaps ? bb / 32 : 1;  // stripes per block (1 when no snapshots)
+  const bool fused = aligned_blocks && (spb == 1 || spb == 2 || spb == 4 || spb == 8);
+  if (fused) {
+    for (int i = threadIdx.x; i < 2 * kProdSlot; i += blockDim.x) smem[i] = 0;  // index 0 and the pad stay zero
+    if (threadIdx.x == 0) {
+      mbar_init(&bars[0], 32);
+      mbar_init(&bars[1], 32);
+      mbar_init(&bars[2], 4);
+      mbar_init(&bars[3], 4);
     }
-  } else if (fast) {
+    __syncthreads();
     const uint64_t *data64 = reinterpret_cast<const uint64_t *>(data);
-    const int64_t n_words = 4 * K;  // only whole stripes are read here
-    int cur = 0;
-    if (K > 0) stage_tile(tiles[0], s, data64, 0, n_words, lane);
-    for (int64_t t0 = 0; t0 < n_words; t0 += kTileWords) {
-      // Prefetch the next tile, then wait for the current one.
-      if (t0 + kTileWords < n_words) stage_tile(tiles[cur ^ 1], s, data64, t0 + kTileWords, n_words, lane);
-      else cp_async_commit();
-      cp_async_wait_1();
-      __syncwarp();
-      const uint64_t *buf = tiles[cur];
-      const int64_t k_begin = t0 / 4;
-      const int64_t k_tile_end = (t0 + kTileWords) / 4;
-      const int64_t k_end = K < k_tile_end ? K : k_tile_end;
+    const bool al16 = (reinterpret_cast<uintptr_t>(data) & 15) == 0;
+    volatile int *e = err;
+    bool ok;
+    if (snaps == nullptr) ok = chain_fused<1, false>(data64, al16, K, smem, bars, warp, lane, v, snaps, e);
+    else if (spb == 1) ok = chain_fused<1, true>(data64, al16, K, smem, bars, warp, lane, v, snaps, e);
+    else if (spb == 2) ok = chain_fused<2, true>(data64, al16, K, smem, bars, warp, lane, v, snaps, e);
+    else if (spb == 4) ok = chain_fused<4, true>(data64, al16, K, smem, bars, warp, lane, v, snaps, e);
+    else ok = chain_fused<8, true>(data64, al16, K, smem, bars, warp, lane, v, snaps, e);
+    if (!ok || warp != 0) return;
+  } else {
+    if (warp != 0) return;
+    uint64_t(*tiles)[kTileWords] = reinterpret_cast<uint64_t(*)[kTileWords]>(smem);
+    // Boundaries reached before any stripe of this call.
+    while (snaps && next_b < nb && boundary_stripes(next_b) == 0) {
+      if (lane < 4) snaps[next_b * 4 + j] = v;
+      ++next_b;
+    }
+    const bool fast = (s.memsize % 8 == 0) && data_aligned;
+    if (aligned_blocks) {  // blocks of whole stripes, other than 1, 2, 4 or 8 of them
+      const uint64_t *data64 = reinterpret_cast<const uint64_t *>(data);
+      const int64_t n_words = 4 * K;
+      int cur = 0;
+      if (K > 0) stage_tile(tiles[0], s, data64, 0, n_words, lane);
+      for (int64_t t0 = 0; t0 < n_words; t0 += kTileWords) {
+        if (t0 + kTileWords < n_words) stage_tile(tiles[cur ^ 1], s, data64, t0 + kTileWords, n_words, lane);
+        else cp_async_commit();
+        cp_async_wait_1();
+        __syncwarp();
+        const int64_t k_tile_end = (t0 + kTileWords) / 4;
+        const int kt = (int)((K < k_tile_end ? K : k_tile_end) - t0 / 4);
+        chain_tile_generic(tiles[cur], kt, j, lane, v, snaps, next_b, spb);
+        __syncwarp();
+        cur ^= 1;
+      }
+    } else if (fast) {
+      const uint64_t *data64 = reinterpret_cast<const uint64_t *>(data);
+      const int64_t n_words = 4 * K;  // only whole stripes are read here
+      int cur = 0;
+      if (K > 0) stage_tile(tiles[0], s, data64, 0, n_words, lane);
+      for (int64_t t0 = 0; t0 < n_words; t0 += kTileWords) {
+        // Prefetch the next tile, then wait for the current one.
+        if (t0 + kTileWords < n_words) stage_tile(tiles[cur ^ 1], s, data64, t0 + kTileWords, n_words, lane);
+        else cp_async_commit();
+        cp_async_wait_1();
+        __syncwarp();
+        const uint64_t *buf = tiles[cur];
+        const int64_t k_begin = t0 / 4;
+        const int64_t k_tile_end = (t0 + kTileWords) / 4;
+        const int64_t k_end = K < k_tile_end ? K : k_tile_end;
+        int64_t nbk = (snaps && next_b < nb) ? boundary_stripes(next_b) : INT64_MAX;
+        for (int64_t k = k_begin; k < k_end; ++k) {
+          v = xround(v, buf[4 * (k - k_begin) + j]);
+          if (k + 1 == nbk) {
+            do {
+              if (lane < 4) snaps[next_b * 4 + j] = v;
+              ++next_b;
+              nbk = (next_b < nb) ? boundary_stripes(next_b) : INT64_MAX;
+            } while (k + 1 == nbk);
+          }
+        }
+        __syncwarp();
+        cur ^= 1;
+      }
+    } else {
       int64_t nbk = (snaps && next_b < nb) ? boundary_stripes(next_b) : INT64_MAX;
-      for (int64_t k = k_begin; k < k_end; ++k) {
-        v = xround(v, buf[4 * (k - k_begin) + j]);
+      for (int64_t k = 0; k < K; ++k) {
+        v = xround(v, stream_word(s, data, 32 * k + 8 * j, 8));
         if (k + 1 == nbk) {
           do {
             if (lane < 4) snaps[next_b * 4 + j] = v;
@@ -294,20 +531,6 @@ __global__ void __launch_bounds__(32) xxh_chain_kernel(const XxhState *in, XxhSt
             nbk = (next_b < nb) ? boundary_stripes(next_b) : INT64_MAX;
           } while (k + 1 == nbk);
         }
-      }
-      __syncwarp();
-      cur ^= 1;
-    }
-  } else {
-    int64_t nbk = (snaps && next_b < nb) ? boundary_stripes(next_b) : INT64_MAX;
-    for (int64_t k = 0; k < K; ++k) {
-      v = xround(v, stream_word(s, data, 32 * k + 8 * j, 8));
-      if (k + 1 == nbk) {
-        do {
-          if (lane < 4) snaps[next_b * 4 + j] = v;
-          ++next_b;
-          nbk = (next_b < nb) ? boundary_stripes(next_b) : INT64_MAX;
-        } while (k + 1 == nbk);
       }
     }
   }
@@ -420,6 +643,8 @@ struct fkv_hasher {
   int cur = 0;
   uint64_t *digest_dev = nullptr;
   uint64_t *digest_host = nullptr;  // pinned
+  int *err_host = nullptr;          // pinned, mapped: written by the chain kernel on a timed-out wait
+  int *err_dev = nullptr;           // device address of err_host
 };
 
 using namespace fkv;
@@ -465,10 +690,18 @@ int run_chain(fkv_hasher *h, const uint8_t *data_dev, int64_t len, int64_t bb, i
               uint64_t *snaps, cudaStream_t s) {
   XxhState *in = h->states + h->cur;
   XxhState *out = h->states + (h->cur ^ 1);
-  xxh_chain_kernel<<<1, 32, 0, s>>>(in, out, data_dev, len, bb, nb, snaps);
+  xxh_chain_kernel<<<1, 64, 0, s>>>(in, out, data_dev, len, bb, nb, snaps, h->err_dev);
   FKV_CUDA(cudaGetLastError());
   note_launch();
   return FKV_OK;
+}
+
+// After a synchronize: report (once) a chain hand-off wait that ran out.
+int check_chain(fkv_hasher *h) {
+  if (*h->err_host == 0) return FKV_OK;
+  const int code = *h->err_host;
+  *h->err_host = 0;
+  return fail(code, "hash chain kernel: a producer/consumer hand-off wait timed out; the hasher state is invalid");
 }
 
 }  // namespace
@@ -489,6 +722,11 @@ int fkv_hasher_create(int device, fkv_hasher **out) {
   cudaError_t e = cudaMalloc((void **)&h->states, 2 * sizeof(XxhState));
   if (e == cudaSuccess) e = cudaMalloc((void **)&h->digest_dev, 8);
   if (e == cudaSuccess) e = cudaHostAlloc((void **)&h->digest_host, 8, cudaHostAllocPortable);
+  if (e == cudaSuccess) e = cudaHostAlloc((void **)&h->err_host, 4, cudaHostAllocPortable | cudaHostAllocMapped);
+  if (e == cudaSuccess) {
+    *h->err_host = 0;
+    e = cudaHostGetDevicePointer((void **)&h->err_dev, h->err_host, 0);
+  }
   if (e != cudaSuccess) {
     fkv_hasher_destroy(h);
     return fail_cuda(e, "hasher allocation");
@@ -510,6 +748,7 @@ void fkv_hasher_destroy(fkv_hasher *h) {
   if (h->states) cudaFree(h->states);
   if (h->digest_dev) cudaFree(h->digest_dev);
   if (h->digest_host) cudaFreeHost(h->digest_host);
+  if (h->err_host) cudaFreeHost(h->err_host);
   delete h;
 }
 
@@ -539,7 +778,10 @@ int fkv_hasher_update(fkv_hasher *h, const void *data, int64_t size, void *strea
   if (int rc = device_view(data, size, h->device, s, tmp, &dv, &was_host)) return rc;
   if (int rc = run_chain(h, (const uint8_t *)dv, size, 0, 0, nullptr, s)) return rc;
   h->cur ^= 1;
-  if (was_host) FKV_CUDA(cudaStreamSynchronize(s));
+  if (was_host) {
+    FKV_CUDA(cudaStreamSynchronize(s));
+    return check_chain(h);
+  }
   return FKV_OK;
 }
 
@@ -554,6 +796,7 @@ int fkv_hasher_digest(fkv_hasher *h, uint64_t *out, void *stream) {
   note_launch();
   FKV_CUDA(cudaMemcpyAsync(h->digest_host, h->digest_dev, 8, cudaMemcpyDeviceToHost, s));
   FKV_CUDA(cudaStreamSynchronize(s));
+  if (int rc = check_chain(h)) return rc;
   *out = *h->digest_host;
   return FKV_OK;
 }
@@ -601,7 +844,10 @@ int fkv_gen_hashes(fkv_hasher *h, const int64_t *token_ids, int64_t num_tokens,
   h->cur ^= 1;
   if (!out_is_dev)
     FKV_CUDA(cudaMemcpyAsync(block_hashes, out_dev_ptr, (size_t)num_blocks * 8, cudaMemcpyDeviceToHost, s));
-  if (!out_is_dev || tok_host) FKV_CUDA(cudaStreamSynchronize(s));
+  if (!out_is_dev || tok_host) {
+    FKV_CUDA(cudaStreamSynchronize(s));
+    return check_chain(h);
+  }
   return FKV_OK;
 }
 
