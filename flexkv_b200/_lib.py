@@ -26,6 +26,7 @@ FKV_ERR_MISALIGNED = 3
 FKV_ERR_CUDA = 4
 FKV_ERR_UNSUPPORTED = 5
 FKV_ERR_TIMEOUT = 6
+FKV_ERR_IO = 7
 
 
 class TransferDesc(ctypes.Structure):
@@ -106,6 +107,20 @@ class EngineOp(ctypes.Structure):
 
 FKV_OP_H2D, FKV_OP_D2H, FKV_OP_VIRTUAL = 0, 1, 2
 
+
+class IpcHandle(ctypes.Structure):
+    """Mirror of ``fkv_ipc_handle``."""
+
+    _fields_ = [
+        ("cuda_handle", ctypes.c_ubyte * 64),
+        ("base_addr", c_u64),
+        ("alloc_bytes", c_u64),
+        ("offset", c_i64),
+        ("bytes", c_i64),
+        ("device", ctypes.c_int32),
+        ("pid", ctypes.c_int32),
+    ]
+
 # name -> (restype, argtypes)
 _SIGNATURES = {
     "fkv_last_error": (c_char_p, []),
@@ -149,6 +164,18 @@ _SIGNATURES = {
     "fkv_engine_poll": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, ctypes.POINTER(c_int)]),
     "fkv_engine_pending_ops": (c_i64, [c_vp]),
     "fkv_engine_destroy": (None, [c_vp]),
+    "fkv_ipc_export": (c_int, [c_vp, c_i64, ctypes.POINTER(IpcHandle)]),
+    "fkv_ipc_open": (c_int, [ctypes.POINTER(IpcHandle), c_int, ctypes.POINTER(c_vp)]),
+    "fkv_ipc_close": (c_int, [c_vp]),
+    "fkv_ipc_open_count": (c_int, []),
+    "fkv_ssd_ctx_create": (c_int, [ctypes.POINTER(c_char_p), c_int, c_int, c_int, c_int, ctypes.POINTER(c_vp)]),
+    "fkv_ssd_ctx_destroy": (None, [c_vp]),
+    "fkv_transfer_kv_blocks_ssd": (
+        c_int,
+        [c_vp, c_int, c_int, c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
+         c_int, c_int, c_int, c_int, c_int],
+    ),
+    "fkv_ssd_last_stats": (c_int, [c_vp, P_i64, P_i64]),
     "fkv_transfer_kv_blocks_noalloc": (
         c_int,
         [c_int, c_int, c_int, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64,

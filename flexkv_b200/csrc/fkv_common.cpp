@@ -163,6 +163,27 @@ int pointer_is_device(const void *p, int *is_device, int *device) {
   return FKV_OK;
 }
 
+bool alloc_range(const void *p, uint64_t *base, size_t *size) {
+  using GetRange = int (*)(unsigned long long *, size_t *, unsigned long long);
+  static GetRange fn = [] {
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      return (GetRange) nullptr;
+    }
+    return reinterpret_cast<GetRange>(f);
+  }();
+  if (!fn) return false;
+  unsigned long long b = 0;
+  size_t n = 0;
+  if (fn(&b, &n, (unsigned long long)(uintptr_t)p) != 0) return false;
+  *base = b;
+  *size = n;
+  return true;
+}
+
 }  // namespace fkv
 
 extern "C" {

@@ -76,5 +76,9 @@ size_t transfer_stage_bytes(const fkv_transfer_desc &d);
 
 // Classify a pointer: 1 = device memory (or managed), 0 = host.
 int pointer_is_device(const void *p, int *is_device, int *device);
+// Base and size of the device allocation that contains p (driver
+// cuMemGetAddressRange, looked up through the runtime so the library needs
+// no -lcuda).  False if p is not inside a device allocation.
+bool alloc_range(const void *p, uint64_t *base, size_t *size);
 
 }  // namespace fkv

@@ -200,27 +200,12 @@ int max_pitch(int device, int *out) {
   return FKV_OK;
 }
 
-// Whether [a, a+1) and [b, b+1) lie in one device allocation (driver
-// cuMemGetAddressRange, looked up through the runtime so the library has no
-// link-time dependency on libcuda).  A 2-D copy may not span allocations
-// even when they happen to be adjacent in the address space.
+// Whether a and b lie in one device allocation.  A 2-D copy may not span
+// allocations even when they happen to be adjacent in the address space.
 bool same_allocation(const void *a, const void *b) {
-  using GetRange = int (*)(unsigned long long *, size_t *, unsigned long long);
-  static GetRange fn = [] {
-    void *f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess) {
-      cudaGetLastError();
-      return (GetRange) nullptr;
-    }
-    return reinterpret_cast<GetRange>(f);
-  }();
-  if (!fn) return false;
-  unsigned long long base_a = 0, base_b = 0;
+  uint64_t base_a = 0, base_b = 0;
   size_t size_a = 0, size_b = 0;
-  if (fn(&base_a, &size_a, (unsigned long long)(uintptr_t)a) != 0) return false;
-  if (fn(&base_b, &size_b, (unsigned long long)(uintptr_t)b) != 0) return false;
+  if (!alloc_range(a, &base_a, &size_a) || !alloc_range(b, &base_b, &size_b)) return false;
   return base_a == base_b;
 }
 

@@ -44,6 +44,7 @@ extern "C" {
 #define FKV_ERR_CUDA 4         /* a CUDA runtime call failed                */
 #define FKV_ERR_UNSUPPORTED 5  /* feature not provided by this build        */
 #define FKV_ERR_TIMEOUT 6      /* a bounded wait ran out                    */
+#define FKV_ERR_IO 7           /* a file operation failed or came up short  */
 
 /* Message of the last failure on this thread ("" if none). */
 const char *fkv_last_error(void);
@@ -311,6 +312,89 @@ int fkv_gen_hashes_batched(const int64_t *token_ids,
                            const int64_t *seq_offsets, int num_seqs,
                            int tokens_per_block, uint64_t *block_hashes,
                            void *stream);
+
+/* ------------------------------------------------------------------------
+ * CUDA-IPC registration boundary.  The inference engine's process owns the
+ * paged GPU KV cache; the process running the transfers maps it.  Replaces
+ * TensorSharedHandle (flexkv/common/memory_handle.py:17-56, used by
+ * KVTPClient.register_to_server, flexkv/server/client.py:199-215), which
+ * goes through torch.multiprocessing.reductions; this handle is a plain
+ * struct that a process with or without torch can produce and consume.
+ *
+ * Only memory from cudaMalloc-style allocations can be exported (torch's
+ * default caching allocator); virtual-memory allocations (torch
+ * expandable segments) fail with FKV_ERR_CUDA and a message saying so.
+ * ---------------------------------------------------------------------- */
+typedef struct fkv_ipc_handle {
+  unsigned char cuda_handle[64]; /* cudaIpcMemHandle_t of the allocation     */
+  uint64_t base_addr;            /* allocation base in the exporting process  */
+  uint64_t alloc_bytes;          /* allocation size                            */
+  int64_t offset;                /* range start - allocation base              */
+  int64_t bytes;                 /* range length                               */
+  int32_t device;                /* exporting device ordinal                   */
+  int32_t pid;                   /* exporting process id                       */
+} fkv_ipc_handle;
+
+/* Describe [dev_ptr, dev_ptr + bytes) for another process.  Does not
+ * allocate or copy; the exporter keeps the memory alive while any importer
+ * uses it. */
+int fkv_ipc_export(const void *dev_ptr, int64_t bytes, fkv_ipc_handle *out);
+
+/* Map the range described by h into this process and return its address.
+ * Opens of ranges of one allocation share one mapping (reference counted).
+ * device = -1 maps on h->device; another ordinal maps through peer access.
+ * In the exporting process itself the original address is returned. */
+int fkv_ipc_open(const fkv_ipc_handle *h, int device, void **out_ptr);
+
+/* Release one open of the mapping containing ptr; the last release unmaps.
+ * FKV_ERR_INVALID_ARG if ptr lies in no range opened here. */
+int fkv_ipc_close(void *ptr);
+
+/* Number of allocations currently mapped through fkv_ipc_open. */
+int fkv_ipc_open_count(void);
+
+/* ------------------------------------------------------------------------
+ * SSD tier: CPU pool <-> SSD files.  Replaces SSDIOCTX and
+ * transfer_kv_blocks_ssd (csrc/transfer_ssd.h:170-264,
+ * csrc/transfer_ssd.cpp:17-287, bound at csrc/bindings.cpp:57-77,110-119,
+ * 141-142) with the same on-disk format: SSD block s is on device
+ * d = (s/rr) % D at in-device index i = ((s/rr)/D)*rr + s%rr, in file i % F
+ * at file block i / F; chunk (layer l, kv k) at file byte
+ * (i/F)*block_stride + l*ssd_layer_stride + k*ssd_kv_stride.
+ * ---------------------------------------------------------------------- */
+typedef struct fkv_ssd_ctx fkv_ssd_ctx;
+
+/* paths[d * files_per_device + f] is file f of device d; every file is
+ * opened read-write (buffered, plus O_DIRECT where the filesystem allows).
+ * iouring_entries / iouring_flags are accepted for the reference's
+ * constructor and unused: requests are issued by a thread pool. */
+int fkv_ssd_ctx_create(const char *const *paths, int num_devices,
+                       int files_per_device, int iouring_entries,
+                       int iouring_flags, fkv_ssd_ctx **out);
+void fkv_ssd_ctx_destroy(fkv_ssd_ctx *ctx);
+
+/* Move layers [start_layer, start_layer + num_layers) of each block pair
+ * (is_read: SSD -> CPU, else CPU -> SSD).  Synchronous: returns when every
+ * byte is in place.  cpu_pool_bytes > 0 bounds-checks the CPU side (the
+ * reference does no check; 0 keeps that).  num_threads_per_device requests
+ * run in parallel per device.  num_blocks_per_file is accepted and, as in
+ * the reference, not used.  Ids must lie in [0, 2^31). */
+int fkv_transfer_kv_blocks_ssd(fkv_ssd_ctx *ctx, int start_layer, int num_layers,
+                               void *cpu_ptr, int64_t cpu_pool_bytes,
+                               const int64_t *ssd_block_ids,
+                               const int64_t *cpu_block_ids, int64_t num_blocks,
+                               int64_t cpu_layer_stride_in_bytes,
+                               int64_t cpu_kv_stride_in_bytes,
+                               int64_t ssd_layer_stride_in_bytes,
+                               int64_t ssd_kv_stride_in_bytes,
+                               int64_t chunk_size_in_bytes,
+                               int64_t block_stride_in_bytes, int is_read,
+                               int num_blocks_per_file, int round_robin,
+                               int num_threads_per_device, int is_mla);
+
+/* File requests and bytes of the context's most recent transfer (chunks
+ * adjacent in both the file and the pool are merged into one request). */
+int fkv_ssd_last_stats(const fkv_ssd_ctx *ctx, int64_t *num_ios, int64_t *bytes);
 
 #ifdef __cplusplus
 }

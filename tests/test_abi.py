@@ -5,6 +5,7 @@ import os
 import re
 
 import numpy as np
+import pytest
 
 from flexkv_b200 import _lib
 from kvcase import make_ids
@@ -94,3 +95,23 @@ def test_tp_group_rejects_bad_arguments():
     assert lib.fkv_tp_group_create(0, 0, None, None, 0, None, 0, ctypes.byref(h)) == _lib.FKV_ERR_INVALID_ARG
     assert lib.fkv_tp_group_transfer(None, None, None, 0, 0, 0, 0, 0, 0, 0, 0, 0, 1, 0, 0, 0, 0) \
         == _lib.FKV_ERR_INVALID_ARG
+
+
+def test_ipc_argument_checks_without_gpu():
+    """IPC entry points reject bad arguments before touching CUDA, and the
+    Python handle refuses host tensors like the reference's."""
+    import ctypes
+    import torch
+    from flexkv_b200 import _lib
+    from flexkv_b200.memory_handle import TensorSharedHandle
+    L = _lib.load()
+    h = _lib.IpcHandle()
+    assert ctypes.sizeof(h) == 104
+    assert L.fkv_ipc_export(None, 16, ctypes.byref(h)) == _lib.FKV_ERR_INVALID_ARG
+    h.alloc_bytes, h.offset, h.bytes = 100, 96, 8  # range past the allocation
+    out = ctypes.c_void_p()
+    assert L.fkv_ipc_open(ctypes.byref(h), 0, ctypes.byref(out)) == _lib.FKV_ERR_INVALID_ARG
+    assert L.fkv_ipc_close(ctypes.c_void_p(0x1000)) == _lib.FKV_ERR_INVALID_ARG
+    assert L.fkv_ipc_open_count() == 0
+    with pytest.raises(ValueError):
+        TensorSharedHandle(torch.zeros(4))
