@@ -25,7 +25,7 @@ gpu_layer_bytes) default to the reference behaviour.
 from __future__ import annotations
 
 import ctypes
-from typing import List, Optional, Sequence
+from typing import Dict, List, Optional, Sequence, Tuple
 
 import numpy as np
 import torch
@@ -359,13 +359,77 @@ def gen_hashes_batched(token_ids: torch.Tensor, seq_offsets: Sequence[int], toke
 
 
 class SSDIOCTX:
-    """Name kept for ``from flexkv.c_ext import ... SSDIOCTX`` (worker.py:19);
-    the SSD tier is not part of this library."""
+    """Mirror of flexkv::SSDIOCTX (csrc/transfer_ssd.h:170-242, bound at
+    bindings.cpp:141-142): ``SSDIOCTX(ssd_files, num_devices,
+    iouring_entries, iouring_flags)`` with ``ssd_files[d]`` the file paths of
+    SSD device d (all devices hold as many files as device 0, as the
+    reference assumes).  Opens every file read-write; the io_uring settings
+    are accepted and unused (a thread pool issues the requests)."""
 
-    def __init__(self, *args, **kwargs):
-        raise NotImplementedError("the SSD tier (csrc/transfer_ssd.cpp) is not provided by flexkv_b200")
+    def __init__(self, ssd_files: Dict[int, List[str]], num_devices: int, iouring_entries: int = 0,
+                 iouring_flags: int = 0):
+        self._handle = None
+        nf = len(ssd_files[0])
+        paths = [str(ssd_files[d][f]) for d in range(num_devices) for f in range(nf)]
+        arr = (ctypes.c_char_p * len(paths))(*[p.encode() for p in paths])
+        h = ctypes.c_void_p()
+        check(_lib.load().fkv_ssd_ctx_create(arr, int(num_devices), nf, int(iouring_entries),
+                                             int(iouring_flags), ctypes.byref(h)), "SSDIOCTX")
+        self._handle = h
+        self.num_devices, self.num_files_per_device = int(num_devices), nf
+
+    def last_stats(self) -> Tuple[int, int]:
+        """(file requests, bytes) of the most recent transfer on this context."""
+        n, b = ctypes.c_int64(), ctypes.c_int64()
+        check(_lib.load().fkv_ssd_last_stats(self._handle, ctypes.byref(n), ctypes.byref(b)), "last_stats")
+        return n.value, b.value
+
+    def close(self) -> None:
+        if self._handle:
+            _lib.load().fkv_ssd_ctx_destroy(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
-def transfer_kv_blocks_ssd(*args, **kwargs):
-    """Name kept for worker.py:19; the SSD tier is not provided."""
-    raise NotImplementedError("the SSD tier (csrc/transfer_ssd.cpp) is not provided by flexkv_b200")
+def _ssd_ids(t, name: str):
+    if isinstance(t, np.ndarray):
+        if t.dtype != np.int64:
+            raise RuntimeError(f"{name} must be int64")
+        return np.ascontiguousarray(t)
+    if not isinstance(t, torch.Tensor) or t.dtype != torch.int64:
+        raise RuntimeError(f"{name} must be int64")  # TORCH_CHECK, bindings.cpp:66-69
+    return t.detach().cpu().contiguous()
+
+
+def transfer_kv_blocks_ssd(ioctx: SSDIOCTX, cpu_layer_id_list, cpu_tensor_ptr: int, ssd_block_ids,
+                           cpu_block_ids, cpu_layer_stride_in_bytes: int, cpu_kv_stride_in_bytes: int,
+                           ssd_layer_stride_in_bytes: int, ssd_kv_stride_in_bytes: int,
+                           chunk_size_in_bytes: int, block_stride_in_bytes: int, is_read: bool,
+                           num_blocks_per_file: int, round_robin: int = 1,
+                           num_threads_per_device: int = 16, is_mla: bool = False,
+                           cpu_pool_bytes: int = 0) -> None:
+    """Drop-in for flexkv.c_ext.transfer_kv_blocks_ssd (bindings.cpp:57-77,
+    110-119; same keyword names and defaults).  Layers
+    [cpu_layer_id_list[0], cpu_layer_id_list[0] + len(cpu_layer_id_list))
+    move between the CPU pool at cpu_tensor_ptr and the SSD files, SSD ->
+    CPU when is_read.  Synchronous.  cpu_pool_bytes (not in the reference)
+    enables a bounds check of the CPU side."""
+    s_ids = _ssd_ids(ssd_block_ids, "ssd_block_ids")
+    c_ids = _ssd_ids(cpu_block_ids, "cpu_block_ids")
+    if len(s_ids) != len(c_ids):
+        raise RuntimeError("ssd_block_ids and cpu_block_ids differ in length")
+    layers = cpu_layer_id_list.tolist() if hasattr(cpu_layer_id_list, "tolist") else list(cpu_layer_id_list)
+    start = int(layers[0]) if layers else 0
+    sp = s_ids.ctypes.data if isinstance(s_ids, np.ndarray) else s_ids.data_ptr()
+    cp = c_ids.ctypes.data if isinstance(c_ids, np.ndarray) else c_ids.data_ptr()
+    check(_lib.load().fkv_transfer_kv_blocks_ssd(
+        ioctx._handle, start, len(layers), ctypes.c_void_p(int(cpu_tensor_ptr)), int(cpu_pool_bytes), sp, cp,
+        len(s_ids), int(cpu_layer_stride_in_bytes), int(cpu_kv_stride_in_bytes),
+        int(ssd_layer_stride_in_bytes), int(ssd_kv_stride_in_bytes), int(chunk_size_in_bytes),
+        int(block_stride_in_bytes), int(bool(is_read)), int(num_blocks_per_file), int(round_robin),
+        int(num_threads_per_device), int(bool(is_mla))), "transfer_kv_blocks_ssd")

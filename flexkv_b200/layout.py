@@ -52,6 +52,21 @@ class KVCacheLayout:
         return KVCacheLayout(self.type, self.num_layer // n, self.num_block, self.tokens_per_block,
                              self.num_head, self.head_size, self.is_mla)
 
+    def div_block(self, num_chunks: int, padding: bool = False) -> "KVCacheLayout":
+        """Per-file layout of a pool split over num_chunks files
+        (storage.py:78-94): ceil when padding, else exact."""
+        if padding:
+            nb = (self.num_block + num_chunks - 1) // num_chunks
+        else:
+            assert self.num_block % num_chunks == 0, \
+                f"num_block {self.num_block} must be divisible by num_chunks {num_chunks}"
+            nb = self.num_block // num_chunks
+        return KVCacheLayout(self.type, self.num_layer, nb, self.tokens_per_block, self.num_head,
+                             self.head_size, self.is_mla)
+
+    def get_elements_per_block(self) -> int:
+        return self.num_layer * self.kv_dim * self.get_chunk_size()
+
     def get_chunk_size(self) -> int:
         return self.tokens_per_block * self.num_head * self.head_size
 

@@ -141,3 +141,33 @@ def ref_lib() -> ctypes.CDLL:
             _c_i64, _c_i64, _vp, _c_int, _c_int, _c_int, _c_int]
         _ref = L
     return _ref
+
+
+def ssd_transfer(files: List[List[np.ndarray]], start_layer: int, num_layers: int, cpu: np.ndarray,
+                 ssd_block_ids: np.ndarray, cpu_block_ids: np.ndarray, cpu_layer_stride: int,
+                 cpu_kv_stride: int, ssd_layer_stride: int, ssd_kv_stride: int, chunk: int,
+                 block_stride: int, is_read: bool, round_robin: int = 1, is_mla: bool = False) -> None:
+    """Restatement of flexkv::transfer_kv_blocks_ssd on in-memory file
+    images: files[d][f] is the byte image of file f of SSD device d.
+    Device/file mapping: transfer_ssd.cpp:17-32 (partition_and_remap);
+    per-chunk offsets and the K-then-V order: transfer_ssd.cpp:133-176
+    (_transfer_single_thread_impl).  Block ids are cast to int there
+    (std::vector<int>), so ids must fit in 31 bits."""
+    D, F = len(files), len(files[0])
+    kv = 1 if is_mla else 2
+    for s_id, c_id in zip(ssd_block_ids.tolist(), cpu_block_ids.tolist()):
+        assert 0 <= s_id < 2 ** 31 and 0 <= c_id < 2 ** 31
+        d = (s_id // round_robin) % D
+        in_dev = ((s_id // round_robin) // D) * round_robin + s_id % round_robin
+        img = files[d][in_dev % F]
+        b = in_dev // F
+        for l in range(start_layer, start_layer + num_layers):
+            for k in range(kv):
+                so = b * block_stride + l * ssd_layer_stride + k * ssd_kv_stride
+                co = c_id * block_stride + l * cpu_layer_stride + k * cpu_kv_stride
+                if is_read:
+                    if so + chunk > img.size:
+                        raise IOError("short read past the end of the file")
+                    cpu[co:co + chunk] = img[so:so + chunk]
+                else:
+                    img[so:so + chunk] = cpu[co:co + chunk]
