@@ -85,6 +85,13 @@ class EngineConfig(ctypes.Structure):
         ("use_ce_d2h", c_int),
         ("reserved", c_int),
         ("staging_bytes", c_i64),
+        ("ssd_ctx", c_vp),
+        ("ssd_layer_stride_in_bytes", c_i64),
+        ("ssd_kv_stride_in_bytes", c_i64),
+        ("ssd_num_blocks_per_file", c_int),
+        ("ssd_round_robin", c_int),
+        ("ssd_threads_per_device", c_int),
+        ("ssd_reserved", c_int),
     ]
 
 
@@ -105,7 +112,7 @@ class EngineOp(ctypes.Structure):
     ]
 
 
-FKV_OP_H2D, FKV_OP_D2H, FKV_OP_VIRTUAL = 0, 1, 2
+FKV_OP_H2D, FKV_OP_D2H, FKV_OP_VIRTUAL, FKV_OP_DISK2H, FKV_OP_H2DISK = 0, 1, 2, 3, 4
 
 
 class IpcHandle(ctypes.Structure):

@@ -19,8 +19,16 @@
 //     shape of TransferEngine.get_completed_graphs_and_ops.
 // A failed op (invalid ids, CUDA error) is reported with its status; its
 // completion event is still recorded so successors are not held back.
+//
+// SSD ops (DISK2H / H2DISK, CPUSSDDiskTransferWorker, worker.py:482-590)
+// are host work: two engine I/O threads (reads, writes) run them through
+// the SSD tier.  An SSD op is handed to its thread once every predecessor
+// has completed; a GPU op is enqueued once each predecessor has either
+// completed or been enqueued on the GPU itself (then an event wait orders
+// them), so a GPU op after an SSD op waits on the host for it.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <chrono>
 #include <condition_variable>
 #include <cstring>
@@ -50,11 +58,15 @@ struct Op {
   int status = FKV_OK;
   std::string error;
   bool completed = false;
+  bool host = false;        // DISK2H / H2DISK: runs on an I/O thread
+  bool dispatched = false;  // enqueued (GPU) or handed to an I/O thread
+  std::atomic<bool> host_done{false};
 };
 
 struct Graph {
   int64_t id = 0;
   std::vector<std::unique_ptr<Op>> ops;
+  std::unordered_map<int64_t, Op *> by_id;
   int remaining = 0;
   int status = FKV_OK;
   std::string error;
@@ -148,6 +160,14 @@ struct fkv_engine {
   // Dispatcher-thread state.
   std::unordered_map<int64_t, std::unique_ptr<Graph>> live;
   std::list<Op *> inflight;
+  std::list<Op *> waiting;  // held until their predecessors allow dispatch
+
+  // SSD I/O threads: queue 0 runs DISK2H ops, queue 1 H2DISK ops.
+  std::mutex io_mu;
+  std::condition_variable io_cv;
+  std::deque<Op *> io_q[2];
+  bool io_stop = false;
+  std::thread io_th[2];
 };
 
 namespace {
@@ -188,7 +208,9 @@ void dispatch(fkv_engine *e, Graph &g, Op &op, const std::unordered_map<int64_t,
     cudaStream_t s = op.type == FKV_OP_D2H ? rk.d2h : rk.h2d;
     for (int64_t p : op.preds) {
       auto it = by_id.find(p);
-      if (it != by_id.end() && it->second->done[r]) cudaStreamWaitEvent(s, it->second->done[r], 0);
+      if (it == by_id.end() || it->second->host) continue;  // SSD predecessors completed before dispatch
+      if ((size_t)r < it->second->done.size() && it->second->done[r])
+        cudaStreamWaitEvent(s, it->second->done[r], 0);
     }
     if (op.status == FKV_OK && op.type != FKV_OP_VIRTUAL && !op.gpu_ids.empty() && gran > 0) {
       fkv_transfer_desc d;
@@ -249,8 +271,96 @@ void dispatch(fkv_engine *e, Graph &g, Op &op, const std::unordered_map<int64_t,
       op.error = "could not record the op's completion event";
     }
   }
+  op.dispatched = true;
   e->inflight.push_back(&op);
   (void)g;
+}
+
+// Whether op may be dispatched now (dispatcher thread).
+bool ready(const Op &op, const std::unordered_map<int64_t, Op *> &by_id) {
+  for (int64_t p : op.preds) {
+    auto it = by_id.find(p);
+    if (it == by_id.end()) continue;
+    const Op *q = it->second;
+    if (q->completed) continue;
+    if (op.host || q->host || !q->dispatched) return false;
+  }
+  return true;
+}
+
+// Hand an SSD op to its I/O thread (dispatcher thread).
+void dispatch_host(fkv_engine *e, Op &op) {
+  op.dispatched = true;
+  e->inflight.push_back(&op);
+  {
+    std::lock_guard<std::mutex> lk(e->io_mu);
+    e->io_q[op.type == FKV_OP_DISK2H ? 0 : 1].push_back(&op);
+  }
+  e->io_cv.notify_all();
+}
+
+void dispatch_any(fkv_engine *e, Graph &g, Op &op) {
+  if (op.host) dispatch_host(e, op);
+  else dispatch(e, g, op, g.by_id);
+}
+
+// Dispatch every held op whose predecessors now allow it; the list keeps
+// each graph's topological order, so chains advance in one pass.
+void pump_waiting(fkv_engine *e) {
+  for (auto it = e->waiting.begin(); it != e->waiting.end();) {
+    Op *op = *it;
+    auto git = e->live.find(op->graph_id);
+    if (git != e->live.end() && ready(*op, git->second->by_id)) {
+      dispatch_any(e, *git->second, *op);
+      it = e->waiting.erase(it);
+    } else {
+      ++it;
+    }
+  }
+}
+
+// One SSD op through the SSD tier (I/O thread).
+void run_ssd_op(fkv_engine *e, Op &op) {
+  if (op.status != FKV_OK || op.gpu_ids.empty()) return;
+  const fkv_engine_config &c = e->cfg;
+  const int L = c.num_layers;
+  const int lid = op.layer_id < 0 ? 0 : op.layer_id;
+  const int gran = op.layer_gran < 0 ? L - lid : op.layer_gran;
+  if (lid + gran > L || gran < 0) {
+    op.status = FKV_ERR_INVALID_ARG;
+    op.error = "layer range exceeds the engine's layers";
+    return;
+  }
+  const int rc = fkv_transfer_kv_blocks_ssd(
+      c.ssd_ctx, lid, gran, c.cpu_ptr, c.cpu_pool_bytes, op.gpu_ids.data(), op.cpu_ids.data(),
+      (int64_t)op.gpu_ids.size(), c.cpu_layer_stride_in_bytes, c.cpu_kv_stride_in_bytes,
+      c.ssd_layer_stride_in_bytes, c.ssd_kv_stride_in_bytes, c.cpu_chunk_size_in_bytes,
+      c.cpu_block_stride_in_bytes, op.type == FKV_OP_DISK2H, c.ssd_num_blocks_per_file,
+      c.ssd_round_robin > 0 ? c.ssd_round_robin : 1, c.ssd_threads_per_device > 0 ? c.ssd_threads_per_device : 32,
+      c.is_mla);
+  if (rc != FKV_OK) {
+    op.status = rc;
+    op.error = fkv_last_error();
+  }
+}
+
+void io_main(fkv_engine *e, int q) {
+  for (;;) {
+    Op *op = nullptr;
+    {
+      std::unique_lock<std::mutex> lk(e->io_mu);
+      e->io_cv.wait(lk, [&] { return e->io_stop || !e->io_q[q].empty(); });
+      if (e->io_q[q].empty()) return;
+      op = e->io_q[q].front();
+      e->io_q[q].pop_front();
+    }
+    run_ssd_op(e, *op);
+    op->host_done.store(true, std::memory_order_release);
+    {
+      std::lock_guard<std::mutex> lk(e->mu);  // pairs with the dispatcher's wait on cv_work
+    }
+    e->cv_work.notify_all();
+  }
 }
 
 // Retire every in-flight op whose events have all fired (dispatcher thread).
@@ -258,7 +368,7 @@ bool retire(fkv_engine *e) {
   bool any = false;
   for (auto it = e->inflight.begin(); it != e->inflight.end();) {
     Op *op = *it;
-    bool done = true;
+    bool done = !op->host || op->host_done.load(std::memory_order_acquire);
     for (size_t r = 0; r < op->done.size() && done; ++r) {
       if (!op->done[r]) continue;
       cudaSetDevice(e->ranks[r].device);
@@ -372,9 +482,9 @@ void engine_main(fkv_engine *e) {
     std::deque<std::unique_ptr<Graph>> batch;
     {
       std::unique_lock<std::mutex> lk(e->mu);
-      if (e->submitted.empty() && e->inflight.empty())
+      if (e->submitted.empty() && e->inflight.empty() && e->waiting.empty())
         e->cv_work.wait(lk, [&] { return e->stop || !e->submitted.empty(); });
-      if (e->stop && e->submitted.empty() && e->inflight.empty()) break;
+      if (e->stop && e->submitted.empty() && e->inflight.empty() && e->waiting.empty()) break;
       batch.swap(e->submitted);
     }
     for (auto &gp : batch) {
@@ -391,8 +501,7 @@ void engine_main(fkv_engine *e) {
         e->inflight_ops -= (int64_t)g.ops.size();
         continue;
       }
-      std::unordered_map<int64_t, Op *> by_id;
-      for (auto &o : g.ops) by_id[o->op_id] = o.get();
+      for (auto &o : g.ops) g.by_id[o->op_id] = o.get();
       e->live[gid] = std::move(gp);
       Graph &lg = *e->live[gid];
       if (lg.ops.empty()) {
@@ -400,9 +509,14 @@ void engine_main(fkv_engine *e) {
         e->live.erase(gid);
         continue;
       }
-      for (Op *o : order) dispatch(e, lg, *o, by_id);
+      for (Op *o : order) {
+        if (ready(*o, lg.by_id)) dispatch_any(e, lg, *o);
+        else e->waiting.push_back(o);
+      }
     }
-    if (!retire(e)) {
+    const bool progressed = retire(e);
+    if (!e->waiting.empty()) pump_waiting(e);
+    if (!progressed) {
       // Nothing finished: give the GPU a moment before polling again.
       std::unique_lock<std::mutex> lk(e->mu);
       e->cv_work.wait_for(lk, std::chrono::microseconds(50),
@@ -415,6 +529,17 @@ void engine_main(fkv_engine *e) {
     if (r.h2d) cudaStreamDestroy(r.h2d);
     if (r.d2h) cudaStreamDestroy(r.d2h);
   }
+}
+
+// Stop the I/O threads (after the dispatcher drained every op).
+void stop_io(fkv_engine *e) {
+  {
+    std::lock_guard<std::mutex> lk(e->io_mu);
+    e->io_stop = true;
+  }
+  e->io_cv.notify_all();
+  for (auto &t : e->io_th)
+    if (t.joinable()) t.join();
 }
 
 }  // namespace
@@ -453,6 +578,10 @@ int fkv_engine_create(const fkv_engine_config *c, fkv_engine **out) {
   e->cfg.gpu_layer_ptrs = nullptr;  // copied per rank
   e->cfg.device_ids = nullptr;
   fkv_engine *raw = e.get();
+  if (c->ssd_ctx) {
+    e->io_th[0] = std::thread(io_main, raw, 0);
+    e->io_th[1] = std::thread(io_main, raw, 1);
+  }
   e->worker = std::thread(engine_main, raw);
   {
     std::unique_lock<std::mutex> lk(e->mu);
@@ -460,6 +589,7 @@ int fkv_engine_create(const fkv_engine_config *c, fkv_engine **out) {
   }
   if (e->init_rc != FKV_OK) {
     e->worker.join();
+    stop_io(raw);
     return fkv::fail(e->init_rc, "engine init failed: " + e->init_error);
   }
   *out = e.release();
@@ -474,8 +604,11 @@ int fkv_engine_submit_graph(fkv_engine *e, int64_t graph_id, const fkv_engine_op
   g->id = graph_id;
   for (int i = 0; i < n_ops; ++i) {
     const fkv_engine_op &s = ops[i];
-    if (s.type != FKV_OP_H2D && s.type != FKV_OP_D2H && s.type != FKV_OP_VIRTUAL)
+    if (s.type != FKV_OP_H2D && s.type != FKV_OP_D2H && s.type != FKV_OP_VIRTUAL && s.type != FKV_OP_DISK2H &&
+        s.type != FKV_OP_H2DISK)
       return fkv::fail(FKV_ERR_INVALID_ARG, "unknown op type " + std::to_string(s.type));
+    if ((s.type == FKV_OP_DISK2H || s.type == FKV_OP_H2DISK) && !e->cfg.ssd_ctx)
+      return fkv::fail(FKV_ERR_INVALID_ARG, "DISK2H / H2DISK ops need an engine created with an SSD context");
     if (s.num_blocks < 0 || (s.num_blocks > 0 && (!s.gpu_block_ids || !s.cpu_block_ids)))
       return fkv::fail(FKV_ERR_INVALID_ARG, "bad block id arrays for op " + std::to_string(s.op_id));
     if (s.num_predecessors < 0 || (s.num_predecessors > 0 && !s.predecessors))
@@ -484,6 +617,7 @@ int fkv_engine_submit_graph(fkv_engine *e, int64_t graph_id, const fkv_engine_op
     o->graph_id = graph_id;
     o->op_id = s.op_id;
     o->type = s.type;
+    o->host = s.type == FKV_OP_DISK2H || s.type == FKV_OP_H2DISK;
     if (s.type != FKV_OP_VIRTUAL && s.num_blocks > 0) {
       o->gpu_ids.assign(s.gpu_block_ids, s.gpu_block_ids + s.num_blocks);
       o->cpu_ids.assign(s.cpu_block_ids, s.cpu_block_ids + s.num_blocks);
@@ -539,6 +673,7 @@ void fkv_engine_destroy(fkv_engine *e) {
   }
   e->cv_work.notify_all();
   if (e->worker.joinable()) e->worker.join();
+  stop_io(e);
   delete e;
 }
 

@@ -32,7 +32,8 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import FKV_OP_D2H, FKV_OP_H2D, FKV_OP_VIRTUAL, EngineConfig, EngineOp, check
+from ._lib import FKV_OP_D2H, FKV_OP_DISK2H, FKV_OP_H2D, FKV_OP_H2DISK, FKV_OP_VIRTUAL, EngineConfig, \
+    EngineOp, check
 from .layout import KVCacheLayout
 
 
@@ -40,6 +41,8 @@ class TransferType(Enum):
     """Names as flexkv/common/transfer.py:15-28 (the tiers handled here)."""
     H2D = "H2D"
     D2H = "D2H"
+    DISK2H = "DISK2H"
+    H2DISK = "H2DISK"
     VIRTUAL = "Virtual"
 
 
@@ -114,7 +117,11 @@ def _type_code(t) -> int:
         return FKV_OP_D2H
     if name == "VIRTUAL":
         return FKV_OP_VIRTUAL
-    raise ValueError(f"transfer type {name} is not handled by the GPU<->CPU engine")
+    if name == "DISK2H":
+        return FKV_OP_DISK2H
+    if name == "H2DISK":
+        return FKV_OP_H2DISK
+    raise ValueError(f"transfer type {name} is not handled by this engine")
 
 
 def _ids(desc) -> np.ndarray:
@@ -130,7 +137,7 @@ class _GroupEngine:
     def __init__(self, gpu_blocks: Sequence[Sequence[torch.Tensor]], cpu_blocks: torch.Tensor,
                  gpu_layout: KVCacheLayout, cpu_layout: KVCacheLayout, itemsize: int,
                  transfer_sms_h2d: int, transfer_sms_d2h: int, use_ce_h2d: bool, use_ce_d2h: bool,
-                 staging_bytes: int):
+                 staging_bytes: int, ssd=None):
         self._lib = _lib.load()
         self._handle = None
         nr, nl = len(gpu_blocks), len(gpu_blocks[0])
@@ -157,6 +164,14 @@ class _GroupEngine:
         c.transfer_sms_h2d, c.transfer_sms_d2h = int(transfer_sms_h2d), int(transfer_sms_d2h)
         c.use_ce_h2d, c.use_ce_d2h = int(bool(use_ce_h2d)), int(bool(use_ce_d2h))
         c.staging_bytes = int(staging_bytes)
+        if ssd is not None:
+            ctx, st, per_file, rr, threads = ssd
+            c.ssd_ctx = ctx._handle
+            c.ssd_layer_stride_in_bytes = st.ssd_layer_stride_in_bytes
+            c.ssd_kv_stride_in_bytes = st.ssd_kv_stride_in_bytes
+            c.ssd_num_blocks_per_file = int(per_file)
+            c.ssd_round_robin = int(rr)
+            c.ssd_threads_per_device = int(threads)
         h = ctypes.c_void_p()
         check(self._lib.fkv_engine_create(ctypes.byref(c), ctypes.byref(h)), "TransferEngine")
         self._handle = h
@@ -175,8 +190,10 @@ class _GroupEngine:
                 src, dst = _ids(op.src_descriptor), _ids(op.dst_descriptor)
                 if src.size != dst.size:
                     raise ValueError(f"op {op.op_id}: source and destination block counts differ")
-                # H2D: src = CPU ids, dst = GPU ids; D2H the reverse (worker.py:272-281)
-                g, c = (dst, src) if code == FKV_OP_H2D else (src, dst)
+                # H2D: src = CPU ids, dst = GPU ids; D2H the reverse (worker.py:272-281).
+                # DISK2H: src = SSD ids, dst = CPU ids; H2DISK the reverse
+                # (worker.py:549-556); the SSD ids ride in the gpu-id slot.
+                g, c = (dst, src) if code in (FKV_OP_H2D, FKV_OP_H2DISK) else (src, dst)
                 keep += [g, c]
                 e.num_blocks = g.size
                 e.gpu_block_ids = g.ctypes.data
@@ -215,13 +232,22 @@ class TransferEngine:
     ``g = dp_id * tp_size + tp_rank`` (each [kv, num_blocks, tpb, heads/tp,
     head_dim]); ``cpu_blocks`` is the flat host pool with ``cpu_layout``
     (page-locked here if it is not already).  ``gpu_layout`` is the per-rank
-    GPU layout (heads already divided for TP)."""
+    GPU layout (heads already divided for TP).
+
+    SSD tier (optional): ``ssd_files`` (SSD device -> file paths, as
+    SSDAllocator makes them), ``ssd_layout`` and ``ssd_num_blocks_per_file``
+    enable DISK2H / H2DISK ops, run as CPUSSDDiskTransferWorker does
+    (worker.py:482-590) on two engine I/O threads, dependencies honoured
+    across the tiers."""
 
     def __init__(self, gpu_blocks: Sequence[Sequence[torch.Tensor]], cpu_blocks: torch.Tensor,
                  gpu_layout: KVCacheLayout, cpu_layout: KVCacheLayout, tp_size: int = 1,
                  dp_size: int = 1, transfer_sms_h2d: int = -1, transfer_sms_d2h: int = -1,
                  use_ce_transfer_h2d: bool = False, use_ce_transfer_d2h: bool = False,
-                 staging_bytes: int = 0):
+                 staging_bytes: int = 0, ssd_files: Optional[Dict[int, List[str]]] = None,
+                 ssd_layout: Optional[KVCacheLayout] = None, ssd_num_blocks_per_file: int = 0,
+                 ssd_iouring_entries: int = 0, ssd_iouring_flags: int = 0,
+                 ssd_threads_per_device: int = 32, ssd_round_robin: int = 1):
         if len(gpu_blocks) != tp_size * dp_size:
             raise ValueError("gpu_blocks needs one list of layer tensors per GPU (dp_size * tp_size)")
         self._cpu = cpu_blocks
@@ -235,10 +261,21 @@ class TransferEngine:
                 if "AlreadyRegistered" not in str(e):
                     raise
         itemsize = cpu_blocks.element_size()
+        self._ssd_ctx = None
+        ssd = None
+        if ssd_files is not None:
+            from .c_ext import SSDIOCTX
+            from .ssd import SsdStrides
+            if ssd_layout is None or ssd_num_blocks_per_file <= 0:
+                raise ValueError("the SSD tier needs ssd_layout and ssd_num_blocks_per_file")
+            self._ssd_ctx = SSDIOCTX(ssd_files, len(ssd_files), ssd_iouring_entries, ssd_iouring_flags)
+            nfiles = sum(len(v) for v in ssd_files.values())
+            st = SsdStrides.of(cpu_layout, ssd_layout, nfiles, itemsize)
+            ssd = (self._ssd_ctx, st, ssd_num_blocks_per_file, ssd_round_robin, ssd_threads_per_device)
         self._groups = [
             _GroupEngine(gpu_blocks[d * tp_size:(d + 1) * tp_size], cpu_blocks, gpu_layout, cpu_layout,
                          itemsize, transfer_sms_h2d, transfer_sms_d2h, use_ce_transfer_h2d,
-                         use_ce_transfer_d2h, staging_bytes)
+                         use_ce_transfer_d2h, staging_bytes, ssd)
             for d in range(dp_size)]
         self.failed_ops: Dict[int, int] = {}
         self._running = True
@@ -247,17 +284,24 @@ class TransferEngine:
     def from_handles(cls, gpu_handles, model_config, cache_config, cpu_handle, ssd_handle=None,
                      remote_handle=None) -> "TransferEngine":
         """Build from FlexKV StorageHandles and configs, the arguments of the
-        reference constructor (transfer_engine.py:43-49)."""
-        if ssd_handle is not None or remote_handle is not None:
-            raise NotImplementedError("the SSD and remote tiers are not part of flexkv_b200")
+        reference constructor (transfer_engine.py:43-49); the SSD handle's
+        file list, layout and blocks-per-file configure the SSD tier."""
+        if remote_handle is not None:
+            raise NotImplementedError("the remote tier is not part of flexkv_b200")
         gpu_blocks = [h.get_tensor_list() for h in gpu_handles]
         g, c = gpu_handles[0].kv_layout, cpu_handle.kv_layout
         from .layout import KVCacheLayoutType
         to = lambda x: KVCacheLayout(KVCacheLayoutType[x.type.name], x.num_layer, x.num_block,
                                      x.tokens_per_block, x.num_head, x.head_size, x.is_mla)
+        ssd = {}
+        if ssd_handle is not None:
+            ssd = dict(ssd_files=ssd_handle.get_file_list(), ssd_layout=to(ssd_handle.kv_layout),
+                       ssd_num_blocks_per_file=ssd_handle.num_blocks_per_file,
+                       ssd_iouring_entries=getattr(cache_config, "ssd_cache_iouring_entries", 0),
+                       ssd_iouring_flags=getattr(cache_config, "ssd_cache_iouring_flags", 0))
         return cls(gpu_blocks, cpu_handle.get_tensor(), to(g), to(c), model_config.tp_size,
                    model_config.dp_size, cache_config.transfer_sms_h2d, cache_config.transfer_sms_d2h,
-                   cache_config.use_ce_transfer_h2d, cache_config.use_ce_transfer_d2h)
+                   cache_config.use_ce_transfer_h2d, cache_config.use_ce_transfer_d2h, **ssd)
 
     def start(self) -> None:
         """The engine runs from construction; kept for the reference API."""
@@ -286,6 +330,9 @@ class TransferEngine:
         for g in self._groups:
             g.close()
         self._groups = []
+        if getattr(self, "_ssd_ctx", None) is not None:  # after the engines: their I/O threads use it
+            self._ssd_ctx.close()
+            self._ssd_ctx = None
         if self._registered:
             from .c_ext import cudaHostUnregister
             cudaHostUnregister(self._cpu)

@@ -218,12 +218,19 @@ void fkv_tp_group_destroy(fkv_tp_group *g);
  * A graph's ops are enqueued at once; a dependency is an event wait on the
  * GPU; H2D and D2H ops use separate streams per GPU; id tables are staged
  * in an engine-owned pinned ring; completions are polled as (graph_id,
- * op_id) pairs with op_id = -1 for a finished graph. */
+ * op_id) pairs with op_id = -1 for a finished graph.  With an SSD context
+ * the engine also runs DISK2H / H2DISK ops (CPUSSDDiskTransferWorker,
+ * worker.py:482-590) on two engine-owned I/O threads, one per direction:
+ * such an op starts once its predecessors have completed, and a GPU op
+ * that follows one is enqueued once it has completed. */
 #define FKV_OP_H2D 0
 #define FKV_OP_D2H 1
 #define FKV_OP_VIRTUAL 2 /* no data; completes when its predecessors do */
+#define FKV_OP_DISK2H 3  /* SSD -> cpu pool (needs the config's ssd_ctx)  */
+#define FKV_OP_H2DISK 4  /* cpu pool -> SSD                                */
 
 typedef struct fkv_engine fkv_engine;
+typedef struct fkv_ssd_ctx fkv_ssd_ctx; /* SSD tier context, declared below */
 
 typedef struct fkv_engine_config {
   int num_ranks;                /* GPUs of the group (TP ranks)              */
@@ -247,13 +254,24 @@ typedef struct fkv_engine_config {
   int use_ce_d2h;
   int reserved;
   int64_t staging_bytes;        /* pinned id-table ring; <= 0 = 32 MiB       */
+  /* SSD tier (optional; ssd_ctx NULL = no DISK2H / H2DISK ops).  Chunk and
+   * block stride are the cpu pool's, as CPUSSDDiskTransferWorker passes
+   * them (worker.py:514-520); the ctx stays owned by the caller. */
+  fkv_ssd_ctx *ssd_ctx;
+  int64_t ssd_layer_stride_in_bytes;
+  int64_t ssd_kv_stride_in_bytes;
+  int ssd_num_blocks_per_file;
+  int ssd_round_robin;          /* <= 0 = 1                                  */
+  int ssd_threads_per_device;   /* <= 0 = 32 (worker.py:573)                 */
+  int ssd_reserved;
 } fkv_engine_config;
 
 typedef struct fkv_engine_op {
   int64_t op_id;
   int type;                     /* FKV_OP_*                                  */
   int num_blocks;
-  const int64_t *gpu_block_ids; /* host arrays, copied at submission        */
+  const int64_t *gpu_block_ids; /* host arrays, copied at submission; the
+                                   SSD block ids for DISK2H / H2DISK         */
   const int64_t *cpu_block_ids;
   int layer_id;                 /* first layer; -1 = 0 (worker.py:318-321)   */
   int layer_granularity;        /* layers; -1 = all remaining                */
@@ -362,8 +380,6 @@ int fkv_ipc_open_count(void);
  * at file block i / F; chunk (layer l, kv k) at file byte
  * (i/F)*block_stride + l*ssd_layer_stride + k*ssd_kv_stride.
  * ---------------------------------------------------------------------- */
-typedef struct fkv_ssd_ctx fkv_ssd_ctx;
-
 /* paths[d * files_per_device + f] is file f of device d; every file is
  * opened read-write (buffered, plus O_DIRECT where the filesystem allows).
  * iouring_entries / iouring_flags are accepted for the reference's
