@@ -306,10 +306,11 @@ def mode_kwargs(args):
     return {}, False
 
 
-def measure_link_peaks(S, stream):
+def measure_link_peaks(S, stream, sync=None):
     """The host link's copy-engine rate on the same pinned pool: one large
     contiguous cudaMemcpyAsync each way, and both ways at once (the measured
-    roofline of the path)."""
+    roofline of the path).  sync, when given, runs before each timed phase
+    (a barrier: every rank copies at once)."""
     n = min(max(S.step_bytes.values()), 2 << 30)
     g1 = torch.empty(n, dtype=torch.uint8, device="cuda")
     g2 = torch.empty(n, dtype=torch.uint8, device="cuda")
@@ -321,6 +322,8 @@ def measure_link_peaks(S, stream):
     def timed(fn):
         fn()
         torch.cuda.synchronize()
+        if sync is not None:
+            sync()
         ts = []
         for _ in range(3):
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -349,6 +352,106 @@ def measure_link_peaks(S, stream):
     del g1, g2
     return dict(peak, unit="GB/s", bytes=n,
                 how="contiguous cudaMemcpyAsync from the pinned pool (each way, and both at once), median of 3")
+
+
+def _fs_type(path: str) -> str:
+    """Filesystem type of the mount holding path (longest mount prefix)."""
+    best, typ = "", "unknown"
+    path = os.path.realpath(path)
+    with open("/proc/mounts") as f:
+        for line in f:
+            parts = line.split()
+            if len(parts) >= 3 and path.startswith(parts[1]) and len(parts[1]) > len(best):
+                best, typ = parts[1], parts[2]
+    return typ
+
+
+def measure_ssd(steps: int = 3):
+    """SSD tier: cfg2's Llama-3-8B block (32 layers x K,V x 32 KiB = 2 MiB),
+    BLOCKWISE on both sides (the reference requires one layout type), one
+    SSD device (a directory on the box's own disk, FLEXKV_SSD_BENCH_DIR or
+    ./_ssd_bench), 512-block batches (1 GiB) of 50 % joint runs.  Writes
+    (H2DISK), then reads (DISK2H, O_DIRECT where the filesystem allows) after
+    a sync, for our SSD tier and for the C restatement of the reference's
+    per-chunk loop (32 threads per device, as CPUSSDDiskTransferWorker
+    passes).  Wall clock around each synchronous call, median of `steps`."""
+    import shutil
+    from flexkv_b200 import c_ext
+    from flexkv_b200.layout import KVCacheLayout, KVCacheLayoutType
+    from flexkv_b200.ssd import SsdStrides, allocate_ssd_files
+    from oracle import oracle as O
+    L, H, D, tpb, nblk, batch = 32, 8, 128, 16, 4096, 512
+    def pin(t):  # page-aligned (O_DIRECT) either way: pinned memory, or an aligned view
+        if torch.cuda.is_available():
+            return t.pin_memory()
+        raw = np.empty(t.numel() + 4096, np.uint8)
+        off = (-raw.ctypes.data) % 4096
+        a = torch.from_numpy(raw[off:off + t.numel()])
+        a.copy_(t)
+        return a
+    lay = KVCacheLayout(KVCacheLayoutType.BLOCKWISE, L, nblk, tpb, H, D)
+    root = os.environ.get("FLEXKV_SSD_BENCH_DIR") or os.path.join(os.path.dirname(os.path.abspath(__file__)),
+                                                                   "_ssd_bench")
+    os.makedirs(root, exist_ok=True)
+    try:
+        files, per_file = allocate_ssd_files(lay, 2, root, max_blocks_per_file=nblk)
+        st = SsdStrides.of(lay, lay, 1, 2)
+        nbytes_pool = lay.get_total_elements() * 2
+        pool = pin(torch.empty(nbytes_pool, dtype=torch.uint8))
+        pool.view(torch.int64).copy_(torch.arange(nbytes_pool // 8, dtype=torch.int64) * 0x9E3779B97F4A7C15)
+        back = pin(torch.zeros(nbytes_pool, dtype=torch.uint8))
+        batches = [make_batch(batch, nblk, nblk, 70 + j, 0.5, 64) for j in range(steps + 1)]
+        ours = c_ext.SSDIOCTX(files, 1)
+        ref = O.SsdRefContext(files, 1)
+        layers = torch.arange(0, L, dtype=torch.int32)
+
+        def run_ours(pool_t, s_ids, c_ids, is_read):
+            c_ext.transfer_kv_blocks_ssd(ours, layers, pool_t.data_ptr(), torch.from_numpy(s_ids),
+                                         torch.from_numpy(c_ids), st.cpu_layer_stride_in_bytes,
+                                         st.cpu_kv_stride_in_bytes, st.ssd_layer_stride_in_bytes,
+                                         st.ssd_kv_stride_in_bytes, st.chunk_size_in_bytes,
+                                         st.block_stride_in_bytes, is_read, per_file, 1, 32, False)
+
+        def run_ref(pool_t, s_ids, c_ids, is_read):
+            ref.transfer(0, L, pool_t.data_ptr(), s_ids, c_ids, st, is_read, 1, 32, False)
+
+        res = {}
+        for name, fn in (("reference_style", run_ref), ("ours", run_ours)):
+            tw, tr = [], []
+            for j, (g, c) in enumerate(batches):  # ssd ids = g, cpu ids = c
+                t0 = time.perf_counter()
+                fn(pool, g, c, False)
+                t1 = time.perf_counter()
+                os.sync()
+                t2 = time.perf_counter()
+                fn(back, g, c, True)
+                t3 = time.perf_counter()
+                if j:  # the first batch warms up
+                    tw.append(t1 - t0)
+                    tr.append(t3 - t2)
+            nbytes = batch * L * 2 * st.chunk_size_in_bytes
+            res[name] = {"write_gbs": round(nbytes / statistics.median(tw) / 1e9, 2),
+                         "read_gbs": round(nbytes / statistics.median(tr) / 1e9, 2)}
+        g, c = batches[-1]
+        run_ours(back, g, c, True)
+        n_ios, _ = ours.last_stats()
+        got = back.numpy()
+        want_t = pin(torch.zeros(nbytes_pool, dtype=torch.uint8))
+        ref.transfer(0, L, want_t.data_ptr(), g, c, st, True, 1, 32, False)
+        want = want_t.numpy()
+        if not np.array_equal(got.reshape(nblk, -1)[c], want.reshape(nblk, -1)[c]):
+            raise RuntimeError("SSD tier read different bytes than the reference-style loop")
+        ours.close()
+        ref.close()
+        return {"config": {"workload": "cfg2 Llama-3-8B blocks, BLOCKWISE CPU and SSD", "block_bytes": 2 << 20,
+                           "batch_blocks": batch, "batch_bytes": batch * (2 << 20), "ssd_devices": 1,
+                           "filesystem": _fs_type(root), "threads_per_device": 32,
+                           "reads": "after os.sync(); O_DIRECT where the filesystem allows it"},
+                "ours": res["ours"], "reference_style": res["reference_style"],
+                "requests_per_batch": {"ours": int(n_ios), "reference_style": batch * L * 2},
+                "how": "wall clock around each synchronous call, median of %d batches" % steps}
+    finally:
+        shutil.rmtree(root, ignore_errors=True)
 
 
 def measure_hash():
@@ -564,6 +667,11 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
             if r == rank:
                 extras["link_peak_measured"] = measure_link_peaks(S, stream)
             barrier(ws)
+        if ws > 1:  # every rank at once: the host side shared by all links
+            lpc = measure_link_peaks(S, stream, sync=lambda: barrier(ws))
+            lpc["how"] = ("contiguous cudaMemcpyAsync from each rank's pinned pool with every rank copying "
+                          "at once (rank 0's rates), median of 3")
+            extras["link_peak_concurrent"] = lpc
         if not conc and cfg["kind"] == "batch":
             ts = []  # the same steps with both directions in flight together
             for k in range(max(K, 3)):
@@ -619,7 +727,8 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
     e2e = e2e_engine
     out = None
     if rank == 0:
-        lp = extras.get("link_peak_measured")
+        lpc = extras.get("link_peak_concurrent")  # all ranks run at once in the timed region
+        lp = lpc or extras.get("link_peak_measured")
         if conc:
             ach = step_total / (elapsed_ms / K / 1e3) / 1e9
             peak = lp["duplex_total"] if lp else 2 * PCIE_GEN5_X16_GBS
@@ -628,9 +737,10 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
                     "unit": "GB/s", "frac": round(ach / peak, 4),
                     "traffic": int(sb["h2d"] * TRAFFIC_RATIO["h2d"] + sb["d2h"] * TRAFFIC_RATIO["d2h"]),
                     "traffic_unit": "DRAM bytes per step",
-                    "peak_source": ("measured live: contiguous cudaMemcpyAsync both ways at once on the "
-                                    "same pinned pool (MEASURED_PEAKS.json has no host-link figure)") if lp else
-                                   "nominal 2 x PCIe Gen5 x16",
+                    "peak_source": (("measured live: contiguous cudaMemcpyAsync both ways at once on the "
+                                     "same pinned pool" + (", every rank copying at once" if lpc else "") +
+                                     " (MEASURED_PEAKS.json has no host-link figure)") if lp else
+                                    "nominal 2 x PCIe Gen5 x16"),
                     "nominal_peak": 2 * PCIE_GEN5_X16_GBS,
                     "frac_of_nominal": round(ach / (2 * PCIE_GEN5_X16_GBS), 4)}
         else:
@@ -642,9 +752,10 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
                     "frac": round(rate[head] / peak, 4),
                     "traffic": int(sb[head] * TRAFFIC_RATIO[head] / max(nops_head, 1)),
                     "traffic_unit": "DRAM bytes per op",
-                    "peak_source": ("measured live: one contiguous cudaMemcpyAsync of up to 2 GiB on the "
-                                    "same pinned pool (MEASURED_PEAKS.json has no host-link figure)") if lp else
-                                   "nominal PCIe Gen5 x16 (no live measurement in this run)",
+                    "peak_source": (("measured live: one contiguous cudaMemcpyAsync of up to 2 GiB on the "
+                                     "same pinned pool" + (", every rank copying at once" if lpc else "") +
+                                     " (MEASURED_PEAKS.json has no host-link figure)") if lp else
+                                    "nominal PCIe Gen5 x16 (no live measurement in this run)"),
                     "nominal_peak": PCIE_GEN5_X16_GBS,
                     "frac_of_nominal": round(rate[head] / PCIE_GEN5_X16_GBS, 4),
                     "per_direction": {d: {"achieved": round(rate[d], 2),
@@ -1033,6 +1144,8 @@ def main():
     ap.add_argument("--gpu-blocks", type=int, default=0, help="override the GPU pool size")
     ap.add_argument("--hash-only", action="store_true",
                     help="only the XXH64 block-hash measurement (one JSON line)")
+    ap.add_argument("--ssd-only", action="store_true",
+                    help="only the SSD-tier measurement (one JSON line)")
     ap.add_argument("--tp", type=int, default=0,
                     help="TP ranks for cfg3 (one process drives them; default: all visible GPUs)")
     ap.add_argument("--no-extras", action="store_true",
@@ -1044,6 +1157,9 @@ def main():
     if args.hash_only:
         torch.cuda.set_device(0)
         print(json.dumps({"hash": measure_hash()}), flush=True)
+        return
+    if args.ssd_only:
+        print(json.dumps({"ssd": measure_ssd()}), flush=True)
         return
     if args.impl == "reference" and int(os.environ.get("RANK", "0")) != 0:
         return  # the reference arm runs on rank 0 only

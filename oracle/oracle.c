@@ -19,9 +19,21 @@
  *    (XXH64_reset/update/digest as used by csrc/hash.cpp:17-45) and the
  *    prefix-chained gen_hashes of csrc/hash.cpp:47-66.
  *
+ * 3. oracle_ssd_transfer: restatement of the reference's SSD tier without
+ *    io_uring (csrc/transfer_ssd.cpp:17-32 device/file remapping,
+ *    :133-176 one pread/pwrite per (block, layer) K chunk then V chunk,
+ *    :182-287 num_threads_per_device threads created per call per device
+ *    over contiguous block ranges, O_DIRECT descriptors for reads when the
+ *    chunk is a multiple of 4 KiB, transfer_ssd.h:196-242).  It is the
+ *    reference-style baseline the bench times beside the SSD tier, and a
+ *    second checker of its bytes.
+ *
  * Parity of (2) is pinned against the python `xxhash` package and the
  * system libxxhash.so.0 in tests/test_oracle.py and tests/golden/.
  */
+#define _GNU_SOURCE
+#include <fcntl.h>
+#include <unistd.h>
 #include <pthread.h>
 #include <stdint.h>
 #include <stdlib.h>
@@ -251,4 +263,108 @@ void oracle_gen_hashes_batched(const int64_t *token_ids, const int64_t *seq_offs
     oracle_gen_hashes(&s, token_ids + seq_offsets[q], tokens_per_block, block_hashes + o, nb);
     o += nb;
   }
+}
+
+
+/* ------------------------------------------------------------------ */
+/* 3. SSD tier (reference-style loop)                                  */
+/* ------------------------------------------------------------------ */
+
+typedef struct {
+  const int *fds; /* this device's files */
+  int files_per_device;
+  const int *cpu_ids, *ssd_in_dev;
+  int begin, end, start_layer, end_layer, is_read, is_mla;
+  char *cpu;
+  int64_t cls, sls, ckv, skv, chunk, bstride;
+  int rc;
+} oracle_ssd_job;
+
+static void *oracle_ssd_worker(void *arg) {
+  oracle_ssd_job *j = (oracle_ssd_job *)arg;
+  for (int i = j->begin; i < j->end; ++i) {
+    int s = j->ssd_in_dev[i];
+    const int fd = j->fds[s % j->files_per_device];
+    s /= j->files_per_device;
+    for (int l = j->start_layer; l < j->end_layer; ++l) {
+      for (int k = 0; k < (j->is_mla ? 1 : 2); ++k) {
+        const int64_t so = (int64_t)s * j->bstride + l * j->sls + k * j->skv;
+        char *cp = j->cpu + (int64_t)j->cpu_ids[i] * j->bstride + l * j->cls + k * j->ckv;
+        const ssize_t n = j->is_read ? pread(fd, cp, (size_t)j->chunk, so) : pwrite(fd, cp, (size_t)j->chunk, so);
+        if (n != j->chunk) {
+          j->rc = 1;
+          return NULL;
+        }
+      }
+    }
+  }
+  return NULL;
+}
+
+/* fds_buf / fds_direct: [num_devices * files_per_device] descriptors opened
+ * by the caller (buffered, and with O_DIRECT).  Returns 0, or 1 on a
+ * failed or short request. */
+int oracle_ssd_transfer(const int *fds_buf, const int *fds_direct, int num_devices, int files_per_device,
+                        int start_layer, int num_layers, char *cpu, const int64_t *ssd_ids,
+                        const int64_t *cpu_ids, int num_blocks, int64_t cpu_layer_stride,
+                        int64_t cpu_kv_stride, int64_t ssd_layer_stride, int64_t ssd_kv_stride,
+                        int64_t chunk, int64_t block_stride, int is_read, int round_robin,
+                        int threads_per_device, int is_mla) {
+  const int direct = is_read && chunk % 4096 == 0;
+  const int *fds = direct ? fds_direct : fds_buf;
+  int *cpu_part = (int *)malloc(sizeof(int) * (size_t)(num_blocks > 0 ? num_blocks : 1) * num_devices);
+  int *ssd_part = (int *)malloc(sizeof(int) * (size_t)(num_blocks > 0 ? num_blocks : 1) * num_devices);
+  int *count = (int *)calloc((size_t)num_devices, sizeof(int));
+  for (int i = 0; i < num_blocks; ++i) {
+    const int64_t sid = ssd_ids[i];
+    const int d = (int)((sid / round_robin) % num_devices);
+    const int in_dev = (int)(((sid / round_robin) / num_devices) * round_robin + sid % round_robin);
+    cpu_part[d * num_blocks + count[d]] = (int)cpu_ids[i];
+    ssd_part[d * num_blocks + count[d]] = in_dev;
+    ++count[d];
+  }
+  const int nt = num_devices * threads_per_device;
+  pthread_t *th = (pthread_t *)calloc((size_t)nt, sizeof(pthread_t));
+  oracle_ssd_job *jobs = (oracle_ssd_job *)calloc((size_t)nt, sizeof(oracle_ssd_job));
+  char *started = (char *)calloc((size_t)nt, 1);
+  for (int d = 0; d < num_devices; ++d) {
+    const int per = (count[d] + threads_per_device - 1) / threads_per_device;
+    for (int t = 0; t < threads_per_device; ++t) {
+      const int b = t * per, e = b + per < count[d] ? b + per : count[d];
+      if (b >= e) continue;
+      oracle_ssd_job *j = &jobs[d * threads_per_device + t];
+      j->fds = fds + d * files_per_device;
+      j->files_per_device = files_per_device;
+      j->cpu_ids = cpu_part + d * num_blocks;
+      j->ssd_in_dev = ssd_part + d * num_blocks;
+      j->begin = b;
+      j->end = e;
+      j->start_layer = start_layer;
+      j->end_layer = start_layer + num_layers;
+      j->is_read = is_read;
+      j->is_mla = is_mla;
+      j->cpu = cpu;
+      j->cls = cpu_layer_stride;
+      j->sls = ssd_layer_stride;
+      j->ckv = cpu_kv_stride;
+      j->skv = ssd_kv_stride;
+      j->chunk = chunk;
+      j->bstride = block_stride;
+      started[d * threads_per_device + t] = pthread_create(&th[d * threads_per_device + t], NULL,
+                                                           oracle_ssd_worker, j) == 0;
+      if (!started[d * threads_per_device + t]) oracle_ssd_worker(j);
+    }
+  }
+  int rc = 0;
+  for (int i = 0; i < nt; ++i) {
+    if (started[i]) pthread_join(th[i], NULL);
+    rc |= jobs[i].rc;
+  }
+  free(started);
+  free(jobs);
+  free(th);
+  free(count);
+  free(ssd_part);
+  free(cpu_part);
+  return rc;
 }

@@ -51,6 +51,10 @@ def lib() -> ctypes.CDLL:
         L.oracle_xxh64.argtypes = [_vp, ctypes.c_size_t, ctypes.c_uint64]
         L.oracle_gen_hashes.argtypes = [_vp, _vp, _c_int, _vp, _c_i64]
         L.oracle_gen_hashes_batched.argtypes = [_vp, _vp, _c_int, _c_int, _vp]
+        L.oracle_ssd_transfer.restype = _c_int
+        L.oracle_ssd_transfer.argtypes = [
+            _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int, _c_i64, _c_i64, _c_i64,
+            _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int]
         _lib = L
     return _lib
 
@@ -171,3 +175,40 @@ def ssd_transfer(files: List[List[np.ndarray]], start_layer: int, num_layers: in
                     cpu[co:co + chunk] = img[so:so + chunk]
                 else:
                     img[so:so + chunk] = cpu[co:co + chunk]
+
+
+class SsdRefContext:
+    """Files opened the way the reference's SSDIOCTX opens them (buffered
+    and O_DIRECT, transfer_ssd.h:196-220) for oracle_ssd_transfer, the C
+    restatement of its per-chunk loop."""
+
+    def __init__(self, ssd_files, num_devices: int):
+        self.nd = num_devices
+        self.nf = len(ssd_files[0])
+        paths = [ssd_files[d][f] for d in range(num_devices) for f in range(self.nf)]
+        self.buf = np.array([os.open(p, os.O_RDWR) for p in paths], dtype=np.int32)
+        direct = []
+        for p in paths:
+            try:
+                direct.append(os.open(p, os.O_RDWR | getattr(os, "O_DIRECT", 0)))
+            except OSError:  # a filesystem without O_DIRECT: the reference would throw here
+                direct.append(os.open(p, os.O_RDWR))
+        self.direct = np.array(direct, dtype=np.int32)
+
+    def transfer(self, start_layer, num_layers, cpu_ptr, ssd_ids, cpu_ids, st, is_read, round_robin=1,
+                 threads_per_device=32, is_mla=False) -> None:
+        s = np.ascontiguousarray(ssd_ids, dtype=np.int64)
+        c = np.ascontiguousarray(cpu_ids, dtype=np.int64)
+        rc = lib().oracle_ssd_transfer(
+            self.buf.ctypes.data, self.direct.ctypes.data, self.nd, self.nf, start_layer, num_layers,
+            cpu_ptr, s.ctypes.data, c.ctypes.data, len(s), st.cpu_layer_stride_in_bytes,
+            st.cpu_kv_stride_in_bytes, st.ssd_layer_stride_in_bytes, st.ssd_kv_stride_in_bytes,
+            st.chunk_size_in_bytes, st.block_stride_in_bytes, int(is_read), round_robin,
+            threads_per_device, int(is_mla))
+        if rc:
+            raise IOError("reference-style SSD transfer: a request failed or came up short")
+
+    def close(self) -> None:
+        for fd in list(self.buf) + list(self.direct):
+            os.close(int(fd))
+        self.buf = self.direct = np.zeros(0, np.int32)

@@ -154,3 +154,33 @@ def test_errors(tmp_path):
     with pytest.raises(FlexKVError) as ei:
         c_ext.SSDIOCTX({0: [str(tmp_path / "missing.bin")]}, 1)
     assert ei.value.code == FKV_ERR_IO
+
+
+@pytest.mark.parametrize("ci", [1, 3, 5], ids=[CASES[i][0] for i in (1, 3, 5)])
+def test_reference_style_loop_agrees(ci, tmp_path):
+    """The C restatement of the reference's per-chunk loop (the bench's
+    reference arm) writes the same files and reads the same pool."""
+    case = CASES[ci]
+    mla, rr, (l0, nl) = case[6], case[11], case[12]
+    cpu_layout, files, per_file, st, cids, sids = setup(case, tmp_path)
+    pool = aligned(cpu_layout.get_total_elements() * 2, 500 + ci)
+    ref = O.SsdRefContext(files, len(files))
+    ref.transfer(l0, nl, pool.ctypes.data, sids, cids, st, False, rr, 4, mla)
+    want = images(files)
+    back_ref = aligned(pool.size)
+    ref.transfer(l0, nl, back_ref.ctypes.data, sids, cids, st, True, rr, 4, mla)
+    ref.close()
+    for d in files.values():
+        for p in d:
+            with open(p, "r+b") as f:
+                f.truncate(0)
+                f.truncate(per_file * cpu_layout.get_elements_per_block() * 2)
+    ctx = c_ext.SSDIOCTX(files, len(files))
+    run(ctx, st, pool, sids, cids, l0, nl, False, per_file, rr, mla)
+    for gd, wd in zip(images(files), want):
+        for g, w in zip(gd, wd):
+            assert np.array_equal(g, w)
+    back = aligned(pool.size)
+    run(ctx, st, back, sids, cids, l0, nl, True, per_file, rr, mla)
+    assert np.array_equal(back, back_ref)
+    ctx.close()
