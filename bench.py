@@ -517,6 +517,23 @@ def measure_hash():
         "gpu_host_buffers_ms": round(t_bh * 1e3, 3), "cpu_port_1thread_ms": round(t_bc * 1e3, 3),
         "gpu_device_mtokens_s": round(sizes.sum() / t_bd / 1e6, 1),
         "cpu_port_mtokens_s": round(sizes.sum() / t_bc / 1e6, 1)}
+    # A scheduling step's worth of requests: 4096 of U[1,32] blocks (~1 M tokens).
+    sizes = rng.integers(1, 33, 4096) * tpb
+    offs = np.concatenate([[0], np.cumsum(sizes)]).tolist()
+    rt = rng.integers(0, 152064, int(sizes.sum())).astype(np.int64)
+    rt_dev = torch.from_numpy(rt).cuda()
+    rt_host = torch.from_numpy(rt).pin_memory()
+    t_bd = best(lambda: (c_ext.gen_hashes_batched(rt_dev, offs, tpb), torch.cuda.synchronize()))
+    t_bh = best(lambda: c_ext.gen_hashes_batched(rt_host, offs, tpb))
+    t_bc = best(lambda: O.gen_hashes_batched(rt, offs, tpb), 3)
+    if not np.array_equal(c_ext.gen_hashes_batched(rt_host, offs, tpb).numpy(), O.gen_hashes_batched(rt, offs, tpb)):
+        raise RuntimeError("batched GPU block hashes differ from the oracle")
+    out["batched_4096_requests"] = {
+        "tokens": int(sizes.sum()), "gpu_device_ms": round(t_bd * 1e3, 3),
+        "gpu_host_buffers_ms": round(t_bh * 1e3, 3), "cpu_port_1thread_ms": round(t_bc * 1e3, 3),
+        "gpu_device_mtokens_s": round(sizes.sum() / t_bd / 1e6, 1),
+        "gpu_host_buffers_mtokens_s": round(sizes.sum() / t_bh / 1e6, 1),
+        "cpu_port_mtokens_s": round(sizes.sum() / t_bc / 1e6, 1)}
     h.close()
     return out
 
@@ -574,6 +591,10 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
               for g, c, h2d in ops] for ops in S.steps]
     stream = torch.cuda.current_stream()
     side = torch.cuda.Stream()
+    # Concurrent workloads: each direction alternates over two streams (as
+    # the engine's per-direction stream pool does), so one small op's tail
+    # overlaps the next op's start.
+    pool_h, pool_d = [stream, torch.cuda.Stream()], [side, torch.cuda.Stream()]
     K, W = args.steps, args.warmup
     track_kernels = cfg["kind"] == "batch"
 
@@ -589,9 +610,16 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
         start = rec["start"] if rec is not None else torch.cuda.Event()
         start.record(stream)
         if conc:
-            side.wait_event(start)
+            for q in pool_h[1:] + pool_d:
+                q.wait_event(start)
+        nh = nd = 0
         for i, ((g, c, h2d), p) in enumerate(zip(ops, ps)):
-            st = stream if (h2d or not conc) else side
+            if not conc:
+                st = stream
+            elif h2d:
+                st, nh = pool_h[nh % 2], nh + 1
+            else:
+                st, nd = pool_d[nd % 2], nd + 1
             if rec is not None and not conc:
                 rec["op"][i][0].record(st)
             if rec is not None and track_kernels:
@@ -601,6 +629,10 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
             if rec is not None and not conc:
                 rec["op"][i][1].record(st)
         if conc:
+            for a, b in ((stream, pool_h[1]), (side, pool_d[1])):
+                j = torch.cuda.Event()
+                j.record(b)
+                a.wait_event(j)
             if rec is not None:
                 rec["end_side"].record(side)
                 rec["end_main"].record(stream)

@@ -83,7 +83,7 @@ class EngineConfig(ctypes.Structure):
         ("transfer_sms_d2h", c_int),
         ("use_ce_h2d", c_int),
         ("use_ce_d2h", c_int),
-        ("reserved", c_int),
+        ("streams_per_direction", c_int),
         ("staging_bytes", c_i64),
         ("ssd_ctx", c_vp),
         ("ssd_layer_stride_in_bytes", c_i64),

@@ -10,8 +10,10 @@
 //   * a submitted graph is ordered topologically and every op is enqueued
 //     at once; a dependency is a cudaStreamWaitEvent on the predecessor's
 //     completion event, resolved on the GPU without a host round trip;
-//   * H2D ops run on one stream and D2H ops on another per GPU, so the two
-//     directions share the full-duplex host link;
+//   * H2D ops and D2H ops run on separate streams per GPU, so the two
+//     directions share the full-duplex host link; each direction has a
+//     small pool of streams (2 by default) used round robin, so the tail
+//     of one small op overlaps the start of the next;
 //   * the block-id tables are staged in a page-locked ring owned by the
 //     engine (no per-op pinning), each slice released when its op is done;
 //   * completion is detected by polling the ops' events and reported as
@@ -134,7 +136,8 @@ class PinnedRing {
 
 struct Rank {
   int device = 0;
-  cudaStream_t h2d = nullptr, d2h = nullptr;
+  std::vector<cudaStream_t> h2d, d2h;  // per-direction stream pools
+  size_t next_h2d = 0, next_d2h = 0;
   std::vector<void *> layer_ptrs;
   std::vector<cudaEvent_t> free_events;
 };
@@ -205,7 +208,8 @@ void dispatch(fkv_engine *e, Graph &g, Op &op, const std::unordered_map<int64_t,
   for (int r = 0; r < nr; ++r) {
     Rank &rk = e->ranks[r];
     cudaSetDevice(rk.device);
-    cudaStream_t s = op.type == FKV_OP_D2H ? rk.d2h : rk.h2d;
+    cudaStream_t s = op.type == FKV_OP_D2H ? rk.d2h[rk.next_d2h++ % rk.d2h.size()]
+                                           : rk.h2d[rk.next_h2d++ % rk.h2d.size()];
     for (int64_t p : op.preds) {
       auto it = by_id.find(p);
       if (it == by_id.end() || it->second->host) continue;  // SSD predecessors completed before dispatch
@@ -238,18 +242,25 @@ void dispatch(fkv_engine *e, Graph &g, Op &op, const std::unordered_map<int64_t,
       d.gpu_layer_bytes = c.gpu_layer_bytes;
       const size_t need = fkv::transfer_stage_bytes(d);
       size_t off = 0;
-      // Wait for ring space by retiring finished ops (bounded by the ring).
+      // Wait for ring space: free the slices of the oldest in-flight op that
+      // still holds any.  Slices are allocated in dispatch order, so that
+      // op owns the ring's front slice and every pass frees space; an op
+      // whose slices an earlier pass already freed (it stays in flight until
+      // the poll loop retires it) is skipped.
       while (!e->ring.reserve(need, &off)) {
-        if (e->inflight.empty()) {
+        Op *oldest = nullptr;
+        for (Op *o : e->inflight)
+          if (!o->slices.empty()) {
+            oldest = o;
+            break;
+          }
+        if (!oldest) {
           op.status = FKV_ERR_INVALID_ARG;
           op.error = "id table larger than the engine's staging ring";
           break;
         }
-        Op *oldest = e->inflight.front();
         for (cudaEvent_t ev : oldest->done)
           if (ev) cudaEventSynchronize(ev);
-        // The poll loop retires it (and frees its slices) on its next pass;
-        // free the slices right away so this op can proceed.
         for (auto &sl : oldest->slices) e->ring.release(sl.first);
         oldest->slices.clear();
       }
@@ -457,10 +468,18 @@ void engine_main(fkv_engine *e) {
   // Per-rank streams are created on this thread (it owns all CUDA work).
   int rc = FKV_OK;
   std::string msg;
+  const int nstreams = e->cfg.streams_per_direction > 0 ? e->cfg.streams_per_direction : 2;
   for (auto &r : e->ranks) {
     cudaError_t ce = cudaSetDevice(r.device);
-    if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&r.h2d, cudaStreamNonBlocking);
-    if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&r.d2h, cudaStreamNonBlocking);
+    for (int i = 0; i < nstreams && ce == cudaSuccess; ++i) {
+      cudaStream_t a = nullptr, b = nullptr;
+      ce = cudaStreamCreateWithFlags(&a, cudaStreamNonBlocking);
+      if (ce == cudaSuccess) {
+        r.h2d.push_back(a);
+        ce = cudaStreamCreateWithFlags(&b, cudaStreamNonBlocking);
+      }
+      if (ce == cudaSuccess) r.d2h.push_back(b);
+    }
     if (ce != cudaSuccess) {
       rc = FKV_ERR_CUDA;
       msg = std::string("engine stream creation: ") + cudaGetErrorString(ce);
@@ -526,8 +545,8 @@ void engine_main(fkv_engine *e) {
   for (auto &r : e->ranks) {
     cudaSetDevice(r.device);
     for (cudaEvent_t ev : r.free_events) cudaEventDestroy(ev);
-    if (r.h2d) cudaStreamDestroy(r.h2d);
-    if (r.d2h) cudaStreamDestroy(r.d2h);
+    for (cudaStream_t st : r.h2d) cudaStreamDestroy(st);
+    for (cudaStream_t st : r.d2h) cudaStreamDestroy(st);
   }
 }
 

@@ -137,7 +137,7 @@ class _GroupEngine:
     def __init__(self, gpu_blocks: Sequence[Sequence[torch.Tensor]], cpu_blocks: torch.Tensor,
                  gpu_layout: KVCacheLayout, cpu_layout: KVCacheLayout, itemsize: int,
                  transfer_sms_h2d: int, transfer_sms_d2h: int, use_ce_h2d: bool, use_ce_d2h: bool,
-                 staging_bytes: int, ssd=None):
+                 staging_bytes: int, ssd=None, streams_per_direction: int = 0):
         self._lib = _lib.load()
         self._handle = None
         nr, nl = len(gpu_blocks), len(gpu_blocks[0])
@@ -164,6 +164,7 @@ class _GroupEngine:
         c.transfer_sms_h2d, c.transfer_sms_d2h = int(transfer_sms_h2d), int(transfer_sms_d2h)
         c.use_ce_h2d, c.use_ce_d2h = int(bool(use_ce_h2d)), int(bool(use_ce_d2h))
         c.staging_bytes = int(staging_bytes)
+        c.streams_per_direction = int(streams_per_direction)
         if ssd is not None:
             ctx, st, per_file, rr, threads = ssd
             c.ssd_ctx = ctx._handle
@@ -238,7 +239,8 @@ class TransferEngine:
     SSDAllocator makes them), ``ssd_layout`` and ``ssd_num_blocks_per_file``
     enable DISK2H / H2DISK ops, run as CPUSSDDiskTransferWorker does
     (worker.py:482-590) on two engine I/O threads, dependencies honoured
-    across the tiers."""
+    across the tiers.  ``streams_per_direction`` sizes the per-GPU stream
+    pool of each direction (0 = 2)."""
 
     def __init__(self, gpu_blocks: Sequence[Sequence[torch.Tensor]], cpu_blocks: torch.Tensor,
                  gpu_layout: KVCacheLayout, cpu_layout: KVCacheLayout, tp_size: int = 1,
@@ -247,7 +249,8 @@ class TransferEngine:
                  staging_bytes: int = 0, ssd_files: Optional[Dict[int, List[str]]] = None,
                  ssd_layout: Optional[KVCacheLayout] = None, ssd_num_blocks_per_file: int = 0,
                  ssd_iouring_entries: int = 0, ssd_iouring_flags: int = 0,
-                 ssd_threads_per_device: int = 32, ssd_round_robin: int = 1):
+                 ssd_threads_per_device: int = 32, ssd_round_robin: int = 1,
+                 streams_per_direction: int = 0):
         if len(gpu_blocks) != tp_size * dp_size:
             raise ValueError("gpu_blocks needs one list of layer tensors per GPU (dp_size * tp_size)")
         self._cpu = cpu_blocks
@@ -275,7 +278,7 @@ class TransferEngine:
         self._groups = [
             _GroupEngine(gpu_blocks[d * tp_size:(d + 1) * tp_size], cpu_blocks, gpu_layout, cpu_layout,
                          itemsize, transfer_sms_h2d, transfer_sms_d2h, use_ce_transfer_h2d,
-                         use_ce_transfer_d2h, staging_bytes, ssd)
+                         use_ce_transfer_d2h, staging_bytes, ssd, streams_per_direction)
             for d in range(dp_size)]
         self.failed_ops: Dict[int, int] = {}
         self._running = True

@@ -218,7 +218,9 @@ void fkv_tp_group_destroy(fkv_tp_group *g);
  * A graph's ops are enqueued at once; a dependency is an event wait on the
  * GPU; H2D and D2H ops use separate streams per GPU; id tables are staged
  * in an engine-owned pinned ring; completions are polled as (graph_id,
- * op_id) pairs with op_id = -1 for a finished graph.  With an SSD context
+ * op_id) pairs with op_id = -1 for a finished graph.  Independent ops of
+ * one direction alternate over a small stream pool, so consecutive small
+ * ops overlap their tails.  With an SSD context
  * the engine also runs DISK2H / H2DISK ops (CPUSSDDiskTransferWorker,
  * worker.py:482-590) on two engine-owned I/O threads, one per direction:
  * such an op starts once its predecessors have completed, and a GPU op
@@ -252,7 +254,7 @@ typedef struct fkv_engine_config {
   int transfer_sms_d2h;
   int use_ce_h2d;               /* copy engines only, per direction          */
   int use_ce_d2h;
-  int reserved;
+  int streams_per_direction;    /* stream pool per direction per GPU; <= 0 = 2 */
   int64_t staging_bytes;        /* pinned id-table ring; <= 0 = 32 MiB       */
   /* SSD tier (optional; ssd_ctx NULL = no DISK2H / H2DISK ops).  Chunk and
    * block stride are the cpu pool's, as CPUSSDDiskTransferWorker passes
