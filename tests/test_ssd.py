@@ -2,6 +2,8 @@
 oracle's restatement of csrc/transfer_ssd.cpp on in-memory file images.
 Every byte of every file and of the pool is compared.  No GPU needed: the
 tier moves bytes between the host pool and files."""
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -184,3 +186,27 @@ def test_reference_style_loop_agrees(ci, tmp_path):
     run(ctx, st, back, sids, cids, l0, nl, True, per_file, rr, mla)
     assert np.array_equal(back, back_ref)
     ctx.close()
+
+
+def test_allocation_and_stride_helpers(tmp_path):
+    """allocate_ssd_files follows SSDAllocator.allocate (allocator.py:132-200);
+    SsdStrides follows the SSD worker (worker.py:512-520)."""
+    lay = KVCacheLayout(LW, 4, 30, 16, 2, 64)
+    with pytest.raises(ValueError):  # blocks must split evenly over the devices
+        allocate_ssd_files(lay, 2, [str(tmp_path / "a"), str(tmp_path / "b"), str(tmp_path / "c"),
+                                    str(tmp_path / "d")], max_blocks_per_file=8)
+    files, per_file = allocate_ssd_files(lay, 2, [str(tmp_path / "a"), str(tmp_path / "b")],
+                                         max_blocks_per_file=4)
+    assert per_file == 4 and [len(v) for v in files.values()] == [4, 4]  # ceil(15 / 4) per device
+    block_bytes = lay.get_elements_per_block() * 2
+    for v in files.values():
+        for p in v:
+            assert os.path.getsize(p) == per_file * block_bytes
+    st = SsdStrides.of(lay, lay, 8, 2)
+    per = lay.div_block(8, padding=True)  # ceil(30 / 8) = 4 blocks per file
+    assert per.num_block == 4
+    assert st.ssd_layer_stride_in_bytes == per.get_layer_stride() * 2
+    assert st.ssd_kv_stride_in_bytes == per.get_kv_stride() * 2
+    assert st.block_stride_in_bytes == lay.get_block_stride() * 2
+    with pytest.raises(ValueError):  # one layout type on both sides, as the reference requires
+        SsdStrides.of(lay, KVCacheLayout(BW, 4, 30, 16, 2, 64), 8, 2)
