@@ -538,6 +538,47 @@ def measure_hash():
     return out
 
 
+def measure_op_latency(S, args, n: int = 200):
+    """Latency of one small op, each submitted after the previous finished:
+    a 1-block H2D (every layer: 64 chunks of the workload's chunk size)
+    through the TransferEngine (submit_transfer_graph, then
+    get_completed_graphs_and_ops until it reports the graph) and through
+    one synchronous c_ext.transfer_kv_blocks call.  Medians in microseconds."""
+    from flexkv_b200 import c_ext
+    from flexkv_b200.engine import TransferDescriptor, TransferEngine, TransferOp, TransferOpGraph, TransferType
+    rng = np.random.default_rng(5)
+    pairs = [(int(g), int(c)) for g, c in zip(rng.integers(0, S.gpu_layout.num_block, n),
+                                             rng.integers(0, S.cpu_layout.num_block, n))]
+    eng = TransferEngine([S.layers], S.cpu, S.gpu_layout, S.cpu_layout)
+    t_eng = []
+    try:
+        for k, (g, c) in enumerate(pairs):
+            gr = TransferOpGraph()
+            gr.add_transfer_op(TransferOp(graph_id=gr.graph_id, transfer_type=TransferType.H2D,
+                                          src_descriptor=TransferDescriptor(torch.tensor([c])),
+                                          dst_descriptor=TransferDescriptor(torch.tensor([g]))))
+            t0 = time.perf_counter()
+            eng.submit_transfer_graph(gr)
+            done = False
+            while not done:
+                done = any(gid == gr.graph_id and oid == -1
+                           for gid, oid in eng.get_completed_graphs_and_ops(timeout=0.001))
+            t_eng.append(time.perf_counter() - t0)
+    finally:
+        eng.shutdown()
+    t_call = []
+    for g, c in pairs:
+        gi, ci = torch.tensor([g]), torch.tensor([c])
+        t0 = time.perf_counter()
+        c_ext.transfer_kv_blocks(gi, S.ptrs, S.g_kv, S.g_blk, ci, S.cpu, S.c_kv, S.c_layer, S.c_blk, S.chunk, 0,
+                                 -1, True, False, S.mla)
+        t_call.append(time.perf_counter() - t0)
+    med = lambda v: round(statistics.median(v[10:]) * 1e6, 1)
+    return {"engine_us": med(t_eng), "direct_call_us": med(t_call), "unit": "us",
+            "op": f"1 block H2D ({S.chunk * S.gpu_layout.num_layer * (1 if S.mla else 2)} bytes)",
+            "how": "median of %d ops, each after the previous finished; wall clock" % (n - 10)}
+
+
 def measure_engine(S, args, K, W, ws):
     """Wall-clock seconds for K steps through flexkv_b200.engine.TransferEngine
     (public API: submit_transfer_graph / get_completed_graphs_and_ops) on the
@@ -725,6 +766,7 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
                                 "how": "the same steps with the H2D and the D2H batch in flight together on two streams"}
         if with_hash and rank == 0 and ws == 1:
             extras["hash"] = measure_hash()
+            extras["op_latency"] = measure_op_latency(S, args)
 
     # Per-direction rates.
     dir_ms = {"h2d": [], "d2h": []}

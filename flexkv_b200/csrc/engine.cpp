@@ -30,8 +30,10 @@
 // them), so a GPU op after an SSD op waits on the host for it.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <chrono>
+#include <cstdlib>
 #include <condition_variable>
 #include <cstring>
 #include <deque>
@@ -496,6 +498,10 @@ void engine_main(fkv_engine *e) {
   }
   e->cv_done.notify_all();
   if (rc != FKV_OK) return;
+  // Completion-poll interval while ops are in flight: the added latency of
+  // a finished op is at most this (FKV_ENGINE_POLL_US, default 10 us).
+  int poll_us = 10;
+  if (const char *v = std::getenv("FKV_ENGINE_POLL_US")) poll_us = std::max(1, std::atoi(v));
 
   for (;;) {
     std::deque<std::unique_ptr<Graph>> batch;
@@ -536,9 +542,10 @@ void engine_main(fkv_engine *e) {
     const bool progressed = retire(e);
     if (!e->waiting.empty()) pump_waiting(e);
     if (!progressed) {
-      // Nothing finished: give the GPU a moment before polling again.
+      // Nothing finished: give the GPU a moment before polling again (a
+      // submission or a finished SSD op wakes the loop at once).
       std::unique_lock<std::mutex> lk(e->mu);
-      e->cv_work.wait_for(lk, std::chrono::microseconds(50),
+      e->cv_work.wait_for(lk, std::chrono::microseconds(poll_us),
                           [&] { return e->stop || !e->submitted.empty(); });
     }
   }
