@@ -171,6 +171,7 @@ _SIGNATURES = {
     "fkv_engine_poll": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, ctypes.POINTER(c_int)]),
     "fkv_engine_pending_ops": (c_i64, [c_vp]),
     "fkv_engine_destroy": (None, [c_vp]),
+    "fkv_engine_shutdown": (c_int, [c_vp, c_int]),
     "fkv_ipc_export": (c_int, [c_vp, c_i64, ctypes.POINTER(IpcHandle)]),
     "fkv_ipc_open": (c_int, [ctypes.POINTER(IpcHandle), c_int, ctypes.POINTER(c_vp)]),
     "fkv_ipc_close": (c_int, [c_vp]),

@@ -161,6 +161,7 @@ struct fkv_engine {
   std::string init_error;
   int init_rc = FKV_OK;
   bool ready = false;
+  bool finished = false;  // the dispatcher has returned
 
   // Dispatcher-thread state.
   std::unordered_map<int64_t, std::unique_ptr<Graph>> live;
@@ -466,6 +467,14 @@ bool topo_order(Graph &g, std::vector<Op *> &order, std::string &err) {
   return true;
 }
 
+void mark_finished(fkv_engine *e) {
+  {
+    std::lock_guard<std::mutex> lk(e->mu);
+    e->finished = true;
+  }
+  e->cv_done.notify_all();
+}
+
 void engine_main(fkv_engine *e) {
   // Per-rank streams are created on this thread (it owns all CUDA work).
   int rc = FKV_OK;
@@ -497,7 +506,10 @@ void engine_main(fkv_engine *e) {
     e->ready = true;
   }
   e->cv_done.notify_all();
-  if (rc != FKV_OK) return;
+  if (rc != FKV_OK) {
+    mark_finished(e);
+    return;
+  }
   // Completion-poll interval while ops are in flight: the added latency of
   // a finished op is at most this (FKV_ENGINE_POLL_US, default 10 us).
   int poll_us = 10;
@@ -555,6 +567,7 @@ void engine_main(fkv_engine *e) {
     for (cudaStream_t st : r.h2d) cudaStreamDestroy(st);
     for (cudaStream_t st : r.d2h) cudaStreamDestroy(st);
   }
+  mark_finished(e);
 }
 
 // Stop the I/O threads (after the dispatcher drained every op).
@@ -691,16 +704,35 @@ int64_t fkv_engine_pending_ops(fkv_engine *e) {
   return e->inflight_ops;
 }
 
-void fkv_engine_destroy(fkv_engine *e) {
-  if (!e) return;
+int fkv_engine_shutdown(fkv_engine *e, int timeout_ms) {
+  fkv::clear_error();
+  if (!e) return FKV_OK;
   {
     std::lock_guard<std::mutex> lk(e->mu);
     e->stop = true;
   }
   e->cv_work.notify_all();
+  int64_t pending = 0;
+  bool drained = true;
+  if (timeout_ms >= 0) {
+    std::unique_lock<std::mutex> lk(e->mu);
+    drained = e->cv_done.wait_for(lk, std::chrono::milliseconds(timeout_ms), [&] { return e->finished; });
+    pending = e->inflight_ops;
+  }
+  if (!drained) {
+    // The dispatcher still owns e: leave it running (it exits once its ops
+    // are done) and keep e allocated; the caller must not use e again.
+    e->worker.detach();
+    return fkv::fail(FKV_ERR_TIMEOUT, "engine did not drain its " + std::to_string(pending) +
+                                          " pending ops within " + std::to_string(timeout_ms) +
+                                          " ms; it was left running detached and must not be used again");
+  }
   if (e->worker.joinable()) e->worker.join();
   stop_io(e);
   delete e;
+  return FKV_OK;
 }
+
+void fkv_engine_destroy(fkv_engine *e) { fkv_engine_shutdown(e, -1); }
 
 }  // extern "C"

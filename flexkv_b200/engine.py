@@ -131,6 +131,11 @@ def _ids(desc) -> np.ndarray:
     return np.ascontiguousarray(t, dtype=np.int64)
 
 
+# Engines whose bounded shutdown timed out keep running detached; what they
+# move (tensors held by the group, an SSD context) is kept alive here.
+_DETACHED: list = []
+
+
 class _GroupEngine:
     """One native engine: the GPUs of one data-parallel group."""
 
@@ -220,10 +225,14 @@ class _GroupEngine:
     def pending(self) -> int:
         return int(self._lib.fkv_engine_pending_ops(self._handle))
 
-    def close(self) -> None:
+    def close(self, timeout_s: Optional[float] = None) -> None:
         if self._handle is not None:
-            self._lib.fkv_engine_destroy(self._handle)
-            self._handle = None
+            h, self._handle = self._handle, None
+            ms = -1 if timeout_s is None else max(0, int(timeout_s * 1000))
+            rc = self._lib.fkv_engine_shutdown(h, ms)
+            if rc != 0:
+                _DETACHED.append(self)  # its tensors stay alive for the detached engine
+            check(rc, "shutdown")
 
 
 class TransferEngine:
@@ -329,10 +338,24 @@ class TransferEngine:
     def pending_ops(self) -> int:
         return sum(g.pending() for g in self._groups)
 
-    def shutdown(self) -> None:
-        for g in self._groups:
-            g.close()
-        self._groups = []
+    def shutdown(self, timeout: Optional[float] = 60.0) -> None:
+        """Drain the submitted ops and release the engine, waiting at most
+        ``timeout`` seconds per data-parallel group (None: no limit).  On a
+        timeout this raises RuntimeError; that group's engine keeps running
+        detached until its ops finish, so the tensors it moves must stay
+        alive, and the SSD context (if any) is left open for it."""
+        groups, self._groups = self._groups, []
+        err = None
+        for g in groups:
+            try:
+                g.close(timeout)
+            except RuntimeError as e:
+                err = err or e
+        if err is not None:
+            if getattr(self, "_ssd_ctx", None) is not None:  # still used by the detached engine
+                _DETACHED.append(self._ssd_ctx)
+                self._ssd_ctx = None
+            raise err
         if getattr(self, "_ssd_ctx", None) is not None:  # after the engines: their I/O threads use it
             self._ssd_ctx.close()
             self._ssd_ctx = None

@@ -296,6 +296,12 @@ int fkv_engine_poll(fkv_engine *e, int64_t *graph_ids, int64_t *op_ids, int *sta
 int64_t fkv_engine_pending_ops(fkv_engine *e);
 /* Finish the ops already submitted, then release the engine. */
 void fkv_engine_destroy(fkv_engine *e);
+/* fkv_engine_destroy with a bound (the reference's worker shutdown joins
+ * for 5 s and then terminates, worker.py:190-202): waits at most timeout_ms
+ * (< 0: no limit) for the submitted ops to drain.  FKV_ERR_TIMEOUT if they
+ * did not: the engine keeps running detached until they finish, stays
+ * allocated, and must not be used again (its buffers must stay valid). */
+int fkv_engine_shutdown(fkv_engine *e, int timeout_ms);
 
 /* ---- XXH64 block hashing (hash.cpp) ------------------------------------ */
 typedef struct fkv_hasher fkv_hasher;

@@ -232,3 +232,43 @@ def test_from_reference_style_handles():
             assert torch.equal(view[10:13, layer].cpu(), layers[layer][:, 5:8].transpose(0, 1).cpu())
     finally:
         eng.shutdown()
+
+
+def test_bounded_shutdown_drains_submitted_ops():
+    case = Case("drain", 4, 2, 64, 16, 256, 512)
+    st, imgs, cpu_img, layers, cpu = _pools(case, 1100)
+    gl, cl = case.gpu_layout(), case.cpu_layout_obj()
+    eng = TransferEngine([[t.view(torch.bfloat16) for t in layers]], cpu.view(torch.bfloat16), gl, cl)
+    gids, cids = make_ids(128, 256, 512, 21, 0.5, max_run=8)
+    g, _ = one_op_graph(TransferType.D2H, gids, cids)
+    eng.submit_transfer_graph(g)
+    eng.shutdown(timeout=30.0)  # returns once the op has drained
+    want = cpu_img.copy()
+    oracle_transfer(case, [x.copy() for x in imgs], want, gids, cids, False)
+    assert np.array_equal(cpu.numpy(), want)
+
+
+def test_shutdown_timeout_is_reported_and_the_engine_finishes_detached():
+    """Host-side failure injection: a zero shutdown budget while a 1024-block
+    D2H is in flight.  The call reports the timeout; the engine finishes its
+    op detached (its tensors are kept alive for it), and the bytes land."""
+    from flexkv_b200 import engine as engine_mod
+    case = Case("detach", 4, 8, 128, 16, 1024, 2048)
+    st, imgs, cpu_img, layers, cpu = _pools(case, 1300)
+    gl, cl = case.gpu_layout(), case.cpu_layout_obj()
+    eng = TransferEngine([[t.view(torch.bfloat16) for t in layers]], cpu.view(torch.bfloat16), gl, cl)
+    gids, cids = make_ids(1024, 1024, 2048, 22, 0.5, max_run=16)
+    g, _ = one_op_graph(TransferType.D2H, gids, cids)
+    eng.submit_transfer_graph(g)
+    before = len(engine_mod._DETACHED)
+    with pytest.raises(RuntimeError, match="did not drain"):
+        eng.shutdown(timeout=0.0)
+    assert len(engine_mod._DETACHED) == before + 1
+    want = cpu_img.copy()
+    oracle_transfer(case, [x.copy() for x in imgs], want, gids, cids, False)
+    for _ in range(100):  # the detached dispatcher launches and drains on its own
+        torch.cuda.synchronize()
+        if np.array_equal(cpu.numpy(), want):
+            break
+        time.sleep(0.05)
+    assert np.array_equal(cpu.numpy(), want)
