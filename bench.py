@@ -15,18 +15,25 @@ consecutive steps touch different blocks.  Every batch is far larger than L2
 Other configurations (--config): cfg5_dsv3_mla (DeepSeek-V3 MLA latent KV,
 1024-block batches, runs of 128 : singletons 1:1, both directions at once),
 cfg4_qwen2_7b (Qwen2-7B shape, 256 requests of U[1,32] scattered blocks per
-step, mixed get/put, directions overlapped).
+step, mixed get/put, directions overlapped), cfg3_llama3_70b_tp (Llama-3-70B,
+one TP group of --tp ranks driven from one process).
 
   value  — device-timed GB/s (CUDA events on the launch streams) of plans
            prepared before the timed region (ids validated, coalesced and
            resident on the device).
-  e2e    — GB/s through the reference-facing call
-           flexkv_b200.c_ext.transfer_kv_blocks with host id tensors, wall
-           clock (synchronous calls, or async per direction when the
-           workload overlaps directions).
+  e2e    — GB/s through the public API that replaces FlexKV's
+           TransferEngine (flexkv_b200.engine.TransferEngine: one graph per
+           op, host id tensors, wall clock; H2D and D2H ops in flight
+           together); per_op_calls beside it is one synchronous
+           c_ext.transfer_kv_blocks call per op, the reference worker's
+           pattern.
+  extras — link peaks measured live (each rank alone, and all ranks at
+           once when N > 1), the duplex rate, and at N = 1 on cfg2 the
+           XXH64 hashing, small-op latency and SSD-tier measurements.
   --impl reference — the reference's own transfer.cu built from its source
            (oracle/_ref) driven the way its worker drives it: one op at a
            time, transfer_sms=8, pinned id tensors, synchronous.
+  --hash-only / --ssd-only — only that measurement, one JSON line.
 
 Multi-GPU (torchrun): every rank runs the same per-GPU workload on its own
 GPU and pools (data parallel, no collective on the data path); value is the
@@ -767,6 +774,10 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
         if with_hash and rank == 0 and ws == 1:
             extras["hash"] = measure_hash()
             extras["op_latency"] = measure_op_latency(S, args)
+            try:  # the SSD tier on the box's own disk; a failure is recorded, not fatal
+                extras["ssd"] = measure_ssd()
+            except Exception as e:  # noqa: BLE001
+                extras["ssd"] = {"error": f"{type(e).__name__}: {e}"}
 
     # Per-direction rates.
     dir_ms = {"h2d": [], "d2h": []}
