@@ -545,6 +545,56 @@ def measure_hash():
     return out
 
 
+def measure_host_torch_path(S, n_blocks: int = 512, reps: int = 3):
+    """The reference's host-side torch path on the box's own cores (a
+    baseline beside the kernels): H2D gathers the blocks' chunks from the
+    pinned pool's view with index_select into pinned staging, copies the
+    staging to the GPU in one cudaMemcpyAsync and scatters it into every
+    layer with index_copy_; D2H is the mirror image.  A bounded sample of
+    n_blocks blocks of the workload's first H2D and D2H batches; torch uses
+    every core of this process's affinity."""
+    n = len(os.sched_getaffinity(0))
+    torch.set_num_threads(n)
+    L = len(S.layers)
+    if S.cpu_layout.type.name == "LAYERWISE":
+        view = S.cpu.view(L, S.kv, S.cpu_blocks, -1)  # [layer, kv, block, chunk]
+        bdim = 2
+    else:
+        view = S.cpu.view(S.cpu_blocks, L, S.kv, -1)  # [block, layer, kv, chunk]
+        bdim = 0
+    gpu_views = [t.view(S.kv, S.gpu_layout.num_block, -1) for t in S.layers]  # [kv, block, chunk]
+    ops = {h: (g[:n_blocks], c[:n_blocks]) for g, c, h in S.steps[0]}
+    out = {}
+    for h2d in (True, False):
+        g, c = ops[h2d]
+        gi, ci = torch.from_numpy(g).cuda(), torch.from_numpy(c)
+        ts = []
+        for _ in range(reps + 1):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            if h2d:
+                stage = torch.index_select(view, bdim, ci).pin_memory()
+                dev = stage.cuda(non_blocking=True)
+                for l in range(L):
+                    part = dev[:, l] if bdim == 0 else dev[l]  # [block, kv, chunk] or [kv, block, chunk]
+                    if bdim == 0:
+                        part = part.transpose(0, 1)
+                    gpu_views[l].index_copy_(1, gi, part)
+            else:
+                stage = torch.stack([gpu_views[l].index_select(1, gi) for l in range(L)], 0)  # [L, kv, n, chunk]
+                host = stage.cpu()
+                if bdim == 2:
+                    view.index_copy_(2, ci, host)
+                else:
+                    view.index_copy_(0, ci, host.permute(2, 0, 1, 3).contiguous())
+            torch.cuda.synchronize()
+            ts.append(time.perf_counter() - t0)
+        out["h2d" if h2d else "d2h"] = round(n_blocks * S.block_bytes / statistics.median(ts[1:]) / 1e9, 2)
+    return {"per_direction_gbs": out, "unit": "GB/s", "cores": n, "blocks": n_blocks,
+            "how": "index_select gather / index_copy_ scatter on the pool view, one staged copy, "
+                   "median of %d" % reps}
+
+
 def measure_op_latency(S, args, n: int = 200):
     """Latency of one small op, each submitted after the previous finished:
     a 1-block H2D (every layer: 64 chunks of the workload's chunk size)
@@ -774,6 +824,10 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
         if with_hash and rank == 0 and ws == 1:
             extras["hash"] = measure_hash()
             extras["op_latency"] = measure_op_latency(S, args)
+            try:  # a reported baseline; a failure is recorded, not fatal
+                extras["host_torch_path"] = measure_host_torch_path(S)
+            except Exception as e:  # noqa: BLE001
+                extras["host_torch_path"] = {"error": f"{type(e).__name__}: {e}"}
             try:  # the SSD tier on the box's own disk; a failure is recorded, not fatal
                 extras["ssd"] = measure_ssd()
             except Exception as e:  # noqa: BLE001
