@@ -533,6 +533,8 @@ def measure_hash():
     t_bd = best(lambda: (c_ext.gen_hashes_batched(rt_dev, offs, tpb), torch.cuda.synchronize()))
     t_bh = best(lambda: c_ext.gen_hashes_batched(rt_host, offs, tpb))
     t_bc = best(lambda: O.gen_hashes_batched(rt, offs, tpb), 3)
+    ncores = len(os.sched_getaffinity(0))
+    t_bm = best(lambda: O.gen_hashes_batched(rt, offs, tpb, ncores), 3)
     if not np.array_equal(c_ext.gen_hashes_batched(rt_host, offs, tpb).numpy(), O.gen_hashes_batched(rt, offs, tpb)):
         raise RuntimeError("batched GPU block hashes differ from the oracle")
     out["batched_4096_requests"] = {
@@ -540,7 +542,9 @@ def measure_hash():
         "gpu_host_buffers_ms": round(t_bh * 1e3, 3), "cpu_port_1thread_ms": round(t_bc * 1e3, 3),
         "gpu_device_mtokens_s": round(sizes.sum() / t_bd / 1e6, 1),
         "gpu_host_buffers_mtokens_s": round(sizes.sum() / t_bh / 1e6, 1),
-        "cpu_port_mtokens_s": round(sizes.sum() / t_bc / 1e6, 1)}
+        "cpu_port_mtokens_s": round(sizes.sum() / t_bc / 1e6, 1),
+        "cpu_port_ncores_ms": round(t_bm * 1e3, 3), "cpu_port_ncores": ncores,
+        "cpu_port_ncores_mtokens_s": round(sizes.sum() / t_bm / 1e6, 1)}
     h.close()
     return out
 

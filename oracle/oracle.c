@@ -265,6 +265,53 @@ void oracle_gen_hashes_batched(const int64_t *token_ids, const int64_t *seq_offs
   }
 }
 
+/* The same over num_threads threads, each taking a contiguous range of
+ * sequences (one hasher per sequence, as the reference creates per
+ * SequenceMeta): the n-core CPU baseline of the batched hash. */
+typedef struct {
+  const int64_t *tokens, *offs;
+  int q0, q1, tpb;
+  uint64_t *out;
+  int64_t o0;
+} oracle_hash_job;
+
+static void *oracle_hash_worker(void *arg) {
+  oracle_hash_job *j = (oracle_hash_job *)arg;
+  int64_t o = j->o0;
+  for (int q = j->q0; q < j->q1; ++q) {
+    oracle_xxh64_state s;
+    oracle_xxh64_reset(&s, 0);
+    int64_t nb = (j->offs[q + 1] - j->offs[q]) / j->tpb;
+    oracle_gen_hashes(&s, j->tokens + j->offs[q], j->tpb, j->out + o, nb);
+    o += nb;
+  }
+  return NULL;
+}
+
+void oracle_gen_hashes_batched_mt(const int64_t *token_ids, const int64_t *seq_offsets, int num_seqs,
+                                  int tokens_per_block, uint64_t *block_hashes, int num_threads) {
+  if (num_threads < 1) num_threads = 1;
+  if (num_threads > num_seqs) num_threads = num_seqs > 0 ? num_seqs : 1;
+  pthread_t *th = (pthread_t *)calloc((size_t)num_threads, sizeof(pthread_t));
+  oracle_hash_job *jobs = (oracle_hash_job *)calloc((size_t)num_threads, sizeof(oracle_hash_job));
+  char *started = (char *)calloc((size_t)num_threads, 1);
+  int64_t o = 0;
+  int q = 0;
+  for (int t = 0; t < num_threads; ++t) {
+    const int q1 = (int)((int64_t)num_seqs * (t + 1) / num_threads);
+    jobs[t] = (oracle_hash_job){token_ids, seq_offsets, q, q1, tokens_per_block, block_hashes, o};
+    for (int k = q; k < q1; ++k) o += (seq_offsets[k + 1] - seq_offsets[k]) / tokens_per_block;
+    q = q1;
+    started[t] = pthread_create(&th[t], NULL, oracle_hash_worker, &jobs[t]) == 0;
+    if (!started[t]) oracle_hash_worker(&jobs[t]);
+  }
+  for (int t = 0; t < num_threads; ++t)
+    if (started[t]) pthread_join(th[t], NULL);
+  free(started);
+  free(jobs);
+  free(th);
+}
+
 
 /* ------------------------------------------------------------------ */
 /* 3. SSD tier (reference-style loop)                                  */

@@ -51,6 +51,7 @@ def lib() -> ctypes.CDLL:
         L.oracle_xxh64.argtypes = [_vp, ctypes.c_size_t, ctypes.c_uint64]
         L.oracle_gen_hashes.argtypes = [_vp, _vp, _c_int, _vp, _c_i64]
         L.oracle_gen_hashes_batched.argtypes = [_vp, _vp, _c_int, _c_int, _vp]
+        L.oracle_gen_hashes_batched_mt.argtypes = [_vp, _vp, _c_int, _c_int, _vp, _c_int]
         L.oracle_ssd_transfer.restype = _c_int
         L.oracle_ssd_transfer.argtypes = [
             _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int, _c_i64, _c_i64, _c_i64,
@@ -114,13 +115,17 @@ def gen_hashes(token_ids: np.ndarray, tokens_per_block: int) -> np.ndarray:
 
 
 def gen_hashes_batched(token_ids: np.ndarray, seq_offsets: Sequence[int],
-                       tokens_per_block: int) -> np.ndarray:
+                       tokens_per_block: int, num_threads: int = 1) -> np.ndarray:
     t = np.ascontiguousarray(token_ids, dtype=np.int64)
     offs = np.ascontiguousarray(seq_offsets, dtype=np.int64)
     n = offs.size - 1
-    total = int(sum((offs[i + 1] - offs[i]) // tokens_per_block for i in range(n)))
+    total = int(((offs[1:] - offs[:-1]) // tokens_per_block).sum()) if n > 0 else 0
     out = np.zeros(max(total, 1), dtype=np.uint64)
-    lib().oracle_gen_hashes_batched(_ptr(t), _ptr(offs), n, int(tokens_per_block), _ptr(out))
+    if num_threads > 1:
+        lib().oracle_gen_hashes_batched_mt(_ptr(t), _ptr(offs), n, int(tokens_per_block), _ptr(out),
+                                           int(num_threads))
+    else:
+        lib().oracle_gen_hashes_batched(_ptr(t), _ptr(offs), n, int(tokens_per_block), _ptr(out))
     return out[:total]
 
 

@@ -119,3 +119,14 @@ def test_layout_mirror_matches_reference():
             assert per.get_kv_stride() == v["kv_stride"], key
             assert per.get_block_stride() == v["block_stride"], key
             assert per.get_total_elements() == v["total_per_layer"], key
+
+
+def test_batched_hash_threads_agree():
+    """The n-core CPU baseline of the batched hash gives the same digests."""
+    rng = np.random.default_rng(12)
+    sizes = rng.integers(0, 40, 97) * 3 + rng.integers(0, 5, 97)  # ragged, some shorter than a block
+    offs = np.concatenate([[0], np.cumsum(sizes)])
+    toks = rng.integers(0, 152064, int(sizes.sum())).astype(np.int64)
+    one = O.gen_hashes_batched(toks, offs, 16)
+    for n in (2, 5, 200):
+        assert np.array_equal(O.gen_hashes_batched(toks, offs, 16, n), one)
