@@ -507,7 +507,7 @@ def measure_hash():
         "cpu_port_1thread_ms": round(t_cpu * 1e3, 3),
         "gpu_device_gbs": round(nbytes / t_dev / 1e9, 2), "cpu_port_gbs": round(nbytes / t_cpu / 1e9, 2)}
     sizes = rng.integers(1, 33, 256) * tpb
-    offs = np.concatenate([[0], np.cumsum(sizes)]).tolist()
+    offs = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
     rt = rng.integers(0, 152064, int(sizes.sum())).astype(np.int64)
     rt_dev = torch.from_numpy(rt).cuda()
     rt_host = torch.from_numpy(rt).pin_memory()
@@ -526,7 +526,7 @@ def measure_hash():
         "cpu_port_mtokens_s": round(sizes.sum() / t_bc / 1e6, 1)}
     # A scheduling step's worth of requests: 4096 of U[1,32] blocks (~1 M tokens).
     sizes = rng.integers(1, 33, 4096) * tpb
-    offs = np.concatenate([[0], np.cumsum(sizes)]).tolist()
+    offs = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
     rt = rng.integers(0, 152064, int(sizes.sum())).astype(np.int64)
     rt_dev = torch.from_numpy(rt).cuda()
     rt_host = torch.from_numpy(rt).pin_memory()

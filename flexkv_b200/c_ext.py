@@ -337,13 +337,15 @@ def gen_hashes_batched(token_ids: torch.Tensor, seq_offsets: Sequence[int], toke
     """gen_hashes over many independent sequences at once, each with a fresh
     hasher (one SequenceMeta each, block.py:49-57).  Sequence s is
     token_ids[seq_offsets[s]:seq_offsets[s+1]]; its floor(len/tpb) hashes
-    follow those of sequence s-1 in the output."""
-    offs_np = np.ascontiguousarray(np.asarray(seq_offsets, dtype=np.int64))
-    offs = torch.from_numpy(offs_np)
+    follow those of sequence s-1 in the output.  seq_offsets may be a list,
+    a numpy array or a CPU tensor (arrays avoid a per-call conversion)."""
+    if isinstance(seq_offsets, torch.Tensor):
+        seq_offsets = seq_offsets.detach().cpu().numpy()
+    offs_np = np.ascontiguousarray(seq_offsets, dtype=np.int64)
     n = offs_np.size - 1
     total = int((np.diff(offs_np) // tokens_per_block).sum()) if n > 0 else 0
-    if block_hashes is None:
-        block_hashes = torch.zeros(total, dtype=torch.uint64, device=token_ids.device)
+    if block_hashes is None:  # every entry is written
+        block_hashes = torch.empty(total, dtype=torch.uint64, device=token_ids.device)
     if block_hashes.numel() < total:
         raise RuntimeError("block_hashes is too small")
     tok = token_ids.contiguous()
@@ -352,7 +354,7 @@ def gen_hashes_batched(token_ids: torch.Tensor, seq_offsets: Sequence[int], toke
     dev = tok.device if tok.is_cuda else None
     ctx = torch.cuda.device(dev) if dev is not None else torch.cuda.device(torch.cuda.current_device())
     with ctx:
-        check(_lib.load().fkv_gen_hashes_batched(tok.data_ptr(), offs.data_ptr(), n,
+        check(_lib.load().fkv_gen_hashes_batched(tok.data_ptr(), offs_np.ctypes.data, n,
                                                  int(tokens_per_block), block_hashes.data_ptr(),
                                                  _stream_handle()), "gen_hashes_batched")
     return block_hashes
