@@ -156,3 +156,54 @@ def test_ssd_ops_need_an_ssd_context():
             eng.submit_transfer_graph(g)
     finally:
         eng.shutdown()
+
+
+def test_from_handles_configures_the_ssd_tier(tmp_path):
+    """TransferEngine.from_handles takes the reference constructor's
+    arguments (transfer_engine.py:43-49) including an SSD StorageHandle
+    (file list, layout, blocks per file; storage.py:159-200), by duck typing."""
+    from enum import Enum
+    from types import SimpleNamespace as NS
+
+    class LT(Enum):
+        LAYERWISE = "LAYERWISE"
+        BLOCKWISE = "BLOCKWISE"
+
+    L, H, D, tpb, ng, nc, ns = 2, 4, 64, 16, 32, 64, 64
+    gpu_l = NS(type=LT.LAYERWISE, num_layer=L, num_block=ng, tokens_per_block=tpb, num_head=H, head_size=D,
+               is_mla=False)
+    cpu_l = NS(type=LT.BLOCKWISE, num_layer=L, num_block=nc, tokens_per_block=tpb, num_head=H, head_size=D,
+               is_mla=False)
+    ssd_l = NS(type=LT.BLOCKWISE, num_layer=L, num_block=ns, tokens_per_block=tpb, num_head=H, head_size=D,
+               is_mla=False)
+    files, per_file = allocate_ssd_files(
+        KVCacheLayout(KVCacheLayoutType.BLOCKWISE, L, ns, tpb, H, D), 2, str(tmp_path / "ssd"),
+        max_blocks_per_file=16)
+    gen = torch.Generator().manual_seed(4)
+    gt = [torch.randn(2, ng, tpb, H, D, generator=gen).to(torch.float16) for _ in range(L)]
+    layers = [x.cuda() for x in gt]
+    cpu = torch.zeros(nc * L * 2 * tpb * H * D, dtype=torch.float16)
+    gh = NS(get_tensor_list=lambda: layers, kv_layout=gpu_l)
+    ch = NS(get_tensor=lambda: cpu, kv_layout=cpu_l)
+    sh = NS(get_file_list=lambda: files, kv_layout=ssd_l, num_blocks_per_file=per_file)
+    mc = NS(tp_size=1, dp_size=1)
+    cc = NS(transfer_sms_h2d=-1, transfer_sms_d2h=-1, use_ce_transfer_h2d=False, use_ce_transfer_d2h=False,
+            ssd_cache_iouring_entries=512, ssd_cache_iouring_flags=0)
+    eng = TransferEngine.from_handles([gh], mc, cc, ch, ssd_handle=sh)
+    try:
+        ids = torch.arange(3, 19, dtype=torch.int64)
+        g = write_graph(ids, ids + 7, ids * 3, L)  # SSD ids spread over all four files
+        eng.submit_transfer_graph(g)
+        wait_graphs(eng, [g.graph_id])
+        for x in layers:
+            x[:, ids.cuda()].zero_()
+        cpu.zero_()
+        g = read_graph(ids, ids + 7, ids * 3, L)
+        eng.submit_transfer_graph(g)
+        wait_graphs(eng, [g.graph_id])
+        assert not eng.failed_ops
+        torch.cuda.synchronize()
+        for x, y in zip(layers, gt):
+            assert torch.equal(x.cpu(), y)
+    finally:
+        eng.shutdown()
