@@ -32,6 +32,7 @@ struct fkv_tp_group {
 
   std::vector<std::thread> threads;
   std::vector<cudaStream_t> streams;
+  std::mutex call_mu;  // one transfer at a time: concurrent callers take turns
   std::mutex mu;
   std::condition_variable cv_job, cv_done;
   uint64_t job_seq = 0;
@@ -164,6 +165,7 @@ int fkv_tp_group_transfer(fkv_tp_group *g, const int64_t *gpu_block_ids,
     return fkv::fail(FKV_ERR_INVALID_ARG, "num_gpus * gpu_chunk exceeds cpu_chunk: rank slices would overflow the cpu chunk");
   if (num_blocks <= 0 || layer_granularity == 0) return FKV_OK;
 
+  std::lock_guard<std::mutex> call(g->call_mu);
   fkv_transfer_desc d;
   fkv_transfer_desc_init(&d);
   d.num_blocks = num_blocks;

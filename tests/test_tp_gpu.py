@@ -159,3 +159,44 @@ def test_gpu_cpu_round_trip(tp_size, dp_size, use_mla, layout_type):
                                        gt[dp][layer][:, :, :, sl, :])
     finally:
         c_ext.cudaHostUnregister(cpu)
+
+
+def test_concurrent_callers_take_turns():
+    """Two host threads drive one group at once on disjoint blocks (D2H); the
+    group serializes them and both land exactly."""
+    import threading
+    tp = 2
+    case = Case("tpc", 4, 4, 64, 16, 128, 256, "BLOCKWISE", tp=tp)
+    st = case.strides()
+    gids, cids = make_ids(96, case.gpu_blocks, case.cpu_blocks, 61, 0.4, max_run=8)
+    imgs = [[fill_bytes(st["gpu_layer_bytes"], 300 * r + l) for l in range(case.num_layers)] for r in range(tp)]
+    cpu_img = fill_bytes(st["cpu_pool_bytes"], 9)
+    layers = [[torch.from_numpy(x.copy()).to(dev(r)) for x in imgs[r]] for r in range(tp)]
+    cpu = torch.from_numpy(cpu_img.copy()).pin_memory()
+    grp = c_ext.TPTransferThreadGroup(tp, layers, cpu, 0)
+    args = dict(gpu_kv_stride_in_bytes=st["gpu_kv"], gpu_block_stride_in_bytes=st["gpu_block"],
+                gpu_chunk_size_in_bytes=st["gpu_chunk"], cpu_kv_stride_in_bytes=st["cpu_kv"],
+                cpu_layer_stride_in_bytes=st["cpu_layer"], cpu_block_stride_in_bytes=st["cpu_block"],
+                cpu_chunk_size_in_bytes=st["cpu_chunk"], transfer_sms=8, use_ce_transfer=False, layer_id=0,
+                layer_granularity=case.num_layers, is_mla=False, is_host_to_device=False)
+    errors = []
+
+    def run(part):
+        try:
+            for _ in range(5):
+                grp.tp_group_transfer(torch.from_numpy(gids[part]), cpu_block_id_tensor=torch.from_numpy(cids[part]),
+                                      **args)
+        except Exception as e:  # reported below
+            errors.append(e)
+
+    halves = [slice(0, 48), slice(48, 96)]
+    threads = [threading.Thread(target=run, args=(h,)) for h in halves]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(60)
+    assert not errors and not any(t.is_alive() for t in threads)
+    for r in range(tp):
+        oracle_transfer(case, imgs[r], cpu_img, gids, cids, False, rank=r)
+    assert np.array_equal(cpu.numpy(), cpu_img)
+    grp.close()
