@@ -35,10 +35,10 @@ def test_cross_process_transfer_through_ipc_handles(alloc):
     proc = ctx.Process(target=ipc_peer.child_main,
                        args=(handles, case, gids, cids, 1301, 1302, 1300, q))
     proc.start()
-    try:
-        status, info = q.get(timeout=300)
+    try:  # well inside the per-test limit, so a stuck child fails this test alone
+        status, info = q.get(timeout=150)
     finally:
-        proc.join(timeout=60)
+        proc.join(timeout=30)
         if proc.is_alive():
             proc.kill()
             proc.join()
