@@ -110,24 +110,43 @@ __device__ __forceinline__ void copy_chunk(const uint4 *__restrict__ src,
   for (int64_t v = base + lane; v < n_vec; v += 32) st_stream(dst + v, ld_stream<PF256>(src + v));
 }
 
+// Table entries of chunk c: its block ids and its layer's GPU pointer.
+struct ChunkRef {
+  int64_t g, h;
+  char *layer;
+};
+
+__device__ __forceinline__ ChunkRef chunk_ref(const CopyParams &p, uint32_t c) {
+  const uint32_t layer = c / p.per_layer;
+  const uint32_t rem = c - layer * p.per_layer;
+  const uint32_t i = rem - (rem / p.n) * p.n;
+  return {p.gpu_ids[i], p.cpu_ids[i], p.layer_ptrs[layer]};
+}
+
+// Each warp walks its chunks with the next chunk's table entries loaded
+// before the current chunk's copy starts: the copy's loads and stores are
+// volatile asm (compiler barriers), so without this order every chunk
+// would begin with a dependent round trip to the id and pointer tables.
 template <bool H2D, int UNROLL, bool PF256>
 __global__ void __launch_bounds__(kThreads) kv_copy_kernel(const CopyParams p) {
   const int lane = threadIdx.x & 31;
   const uint32_t warp = (blockIdx.x * kThreads + threadIdx.x) >> 5;
   const uint32_t nwarps = (gridDim.x * kThreads) >> 5;
-  for (uint32_t c = warp; c < p.num_chunks; c += nwarps) {
+  uint32_t c = warp;
+  if (c >= p.num_chunks) return;
+  ChunkRef cur = chunk_ref(p, c);
+  for (; c < p.num_chunks; c += nwarps) {
+    const uint32_t nxt_c = c + nwarps;
+    const ChunkRef nxt = nxt_c < p.num_chunks ? chunk_ref(p, nxt_c) : cur;
     const uint32_t layer = c / p.per_layer;
-    const uint32_t rem = c - layer * p.per_layer;
-    const uint32_t kv = rem / p.n;
-    const uint32_t i = rem - kv * p.n;
-    const int64_t g = p.gpu_ids[i];
-    const int64_t h = p.cpu_ids[i];
-    char *gpu = p.layer_ptrs[layer] + kv * p.gpu_kv_stride + g * p.gpu_block_stride;
+    const uint32_t kv = (c - layer * p.per_layer) / p.n;
+    char *gpu = cur.layer + kv * p.gpu_kv_stride + cur.g * p.gpu_block_stride;
     char *cpu = p.cpu_base + layer * p.cpu_layer_stride + kv * p.cpu_kv_stride +
-                h * p.cpu_block_stride;
+                cur.h * p.cpu_block_stride;
     const uint4 *src = reinterpret_cast<const uint4 *>(H2D ? cpu : gpu);
     uint4 *dst = reinterpret_cast<uint4 *>(H2D ? gpu : cpu);
     copy_chunk<UNROLL, PF256>(src, dst, p.n_vec, lane);
+    cur = nxt;
   }
 }
 
