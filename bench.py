@@ -75,7 +75,7 @@ CONFIGS = {
 }
 # DRAM traffic per payload byte of the SM copy kernel, from its ncu capture
 # (profiles/kv_copy_kernel_cfg2_small_full.md): H2D writes, D2H reads.
-TRAFFIC_RATIO = {"h2d": 0.781, "d2h": 1.016}
+TRAFFIC_RATIO = {"h2d": 0.787, "d2h": 1.010}
 
 
 def log(*a):
