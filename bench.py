@@ -409,6 +409,7 @@ def measure_ssd(steps: int = 3):
         back = pin(torch.zeros(nbytes_pool, dtype=torch.uint8))
         batches = [make_batch(batch, nblk, nblk, 70 + j, 0.5, 64) for j in range(steps + 1)]
         ours = c_ext.SSDIOCTX(files, 1)
+        ours_ring = c_ext.SSDIOCTX(files, 1, 128, 0)  # io_uring, 128 requests in flight
         ref = O.SsdRefContext(files, 1)
         layers = torch.arange(0, L, dtype=torch.int32)
 
@@ -419,11 +420,21 @@ def measure_ssd(steps: int = 3):
                                          st.ssd_kv_stride_in_bytes, st.chunk_size_in_bytes,
                                          st.block_stride_in_bytes, is_read, per_file, 1, 32, False)
 
+        def run_ring(pool_t, s_ids, c_ids, is_read):
+            c_ext.transfer_kv_blocks_ssd(ours_ring, layers, pool_t.data_ptr(), torch.from_numpy(s_ids),
+                                         torch.from_numpy(c_ids), st.cpu_layer_stride_in_bytes,
+                                         st.cpu_kv_stride_in_bytes, st.ssd_layer_stride_in_bytes,
+                                         st.ssd_kv_stride_in_bytes, st.chunk_size_in_bytes,
+                                         st.block_stride_in_bytes, is_read, per_file, 1, 32, False)
+
         def run_ref(pool_t, s_ids, c_ids, is_read):
             ref.transfer(0, L, pool_t.data_ptr(), s_ids, c_ids, st, is_read, 1, 32, False)
 
+        arms = [("reference_style", run_ref), ("ours", run_ours)]
+        if ours_ring.uses_io_uring:
+            arms.append(("ours_io_uring", run_ring))
         res = {}
-        for name, fn in (("reference_style", run_ref), ("ours", run_ours)):
+        for name, fn in arms:
             tw, tr = [], []
             for j, (g, c) in enumerate(batches):  # ssd ids = g, cpu ids = c
                 t0 = time.perf_counter()
@@ -449,12 +460,14 @@ def measure_ssd(steps: int = 3):
         if not np.array_equal(got.reshape(nblk, -1)[c], want.reshape(nblk, -1)[c]):
             raise RuntimeError("SSD tier read different bytes than the reference-style loop")
         ours.close()
+        ours_ring.close()
         ref.close()
         return {"config": {"workload": "cfg2 Llama-3-8B blocks, BLOCKWISE CPU and SSD", "block_bytes": 2 << 20,
                            "batch_blocks": batch, "batch_bytes": batch * (2 << 20), "ssd_devices": 1,
                            "filesystem": _fs_type(root), "threads_per_device": 32,
                            "reads": "after os.sync(); O_DIRECT where the filesystem allows it"},
-                "ours": res["ours"], "reference_style": res["reference_style"],
+                "ours": res["ours"], "ours_io_uring": res.get("ours_io_uring"),
+                "reference_style": res["reference_style"],
                 "requests_per_batch": {"ours": int(n_ios), "reference_style": batch * L * 2},
                 "how": "wall clock around each synchronous call, median of %d batches" % steps}
     finally:

@@ -184,6 +184,7 @@ _SIGNATURES = {
          c_int, c_int, c_int, c_int, c_int],
     ),
     "fkv_ssd_last_stats": (c_int, [c_vp, P_i64, P_i64]),
+    "fkv_ssd_ctx_uses_io_uring": (c_int, [c_vp]),
     "fkv_transfer_kv_blocks_noalloc": (
         c_int,
         [c_int, c_int, c_int, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64,

@@ -365,8 +365,9 @@ class SSDIOCTX:
     bindings.cpp:141-142): ``SSDIOCTX(ssd_files, num_devices,
     iouring_entries, iouring_flags)`` with ``ssd_files[d]`` the file paths of
     SSD device d (all devices hold as many files as device 0, as the
-    reference assumes).  Opens every file read-write; the io_uring settings
-    are accepted and unused (a thread pool issues the requests)."""
+    reference assumes).  Opens every file read-write.  iouring_entries > 0
+    issues requests through io_uring rings of that depth; 0 (or a kernel
+    without io_uring) issues them from a thread pool."""
 
     def __init__(self, ssd_files: Dict[int, List[str]], num_devices: int, iouring_entries: int = 0,
                  iouring_flags: int = 0):
@@ -379,6 +380,10 @@ class SSDIOCTX:
                                              int(iouring_flags), ctypes.byref(h)), "SSDIOCTX")
         self._handle = h
         self.num_devices, self.num_files_per_device = int(num_devices), nf
+
+    @property
+    def uses_io_uring(self) -> bool:
+        return bool(_lib.load().fkv_ssd_ctx_uses_io_uring(self._handle))
 
     def last_stats(self) -> Tuple[int, int]:
         """(file requests, bytes) of the most recent transfer on this context."""

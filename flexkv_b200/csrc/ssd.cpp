@@ -21,10 +21,18 @@
 //     reads fall back to the buffered descriptor instead of failing;
 //   * partial reads and writes are resumed; a short read (end of file) or
 //     an I/O error fails the call with the file and offset in the message.
-// io_uring (the reference's optional path) is not used: queue depth comes
-// from the pool threads, one synchronous request each.
+// With iouring_entries > 0 (the reference's optional io_uring path,
+// transfer_ssd.h:9-168) requests go through io_uring instead, one ring per
+// direction, driven by the kernel interface directly (no liburing): up to
+// iouring_entries requests in flight from the calling thread.  When the
+// ring cannot be set up, the thread pool serves, as the reference falls
+// back to its threads.
 #include <fcntl.h>
+#include <linux/io_uring.h>
+#include <sys/mman.h>
 #include <sys/stat.h>
+#include <sys/syscall.h>
+#include <sys/uio.h>
 #include <unistd.h>
 
 #include <algorithm>
@@ -125,6 +133,169 @@ struct Seg {
   int64_t len;
 };
 
+// One file request for the ring path.
+struct Req {
+  int fd;
+  int file;
+  char *buf;
+  int64_t len;
+  int64_t off;
+};
+
+// A minimal io_uring: READV / WRITEV submissions from one thread at a time.
+class IoRing {
+ public:
+  ~IoRing() {
+    if (sqes_) munmap(sqes_, sqes_sz_);
+    if (cq_ptr_ && cq_ptr_ != sq_ptr_) munmap(cq_ptr_, cq_sz_);
+    if (sq_ptr_) munmap(sq_ptr_, sq_sz_);
+    if (fd_ >= 0) close(fd_);
+  }
+  bool init(unsigned entries, unsigned flags) {
+    io_uring_params p;
+    std::memset(&p, 0, sizeof(p));
+    p.flags = flags;
+    fd_ = (int)syscall(__NR_io_uring_setup, entries, &p);
+    if (fd_ < 0) return false;
+    sq_sz_ = p.sq_off.array + p.sq_entries * sizeof(unsigned);
+    cq_sz_ = p.cq_off.cqes + p.cq_entries * sizeof(io_uring_cqe);
+    const bool single = (p.features & IORING_FEAT_SINGLE_MMAP) != 0;
+    if (single) sq_sz_ = cq_sz_ = std::max(sq_sz_, cq_sz_);
+    sq_ptr_ = mmap(nullptr, sq_sz_, PROT_READ | PROT_WRITE, MAP_SHARED | MAP_POPULATE, fd_, IORING_OFF_SQ_RING);
+    if (sq_ptr_ == MAP_FAILED) {
+      sq_ptr_ = nullptr;
+      return false;
+    }
+    cq_ptr_ = single ? sq_ptr_
+                     : mmap(nullptr, cq_sz_, PROT_READ | PROT_WRITE, MAP_SHARED | MAP_POPULATE, fd_,
+                            IORING_OFF_CQ_RING);
+    if (cq_ptr_ == MAP_FAILED) {
+      cq_ptr_ = nullptr;
+      return false;
+    }
+    sqes_sz_ = p.sq_entries * sizeof(io_uring_sqe);
+    void *q = mmap(nullptr, sqes_sz_, PROT_READ | PROT_WRITE, MAP_SHARED | MAP_POPULATE, fd_, IORING_OFF_SQES);
+    if (q == MAP_FAILED) return false;
+    sqes_ = static_cast<io_uring_sqe *>(q);
+    char *sq = static_cast<char *>(sq_ptr_), *cq = static_cast<char *>(cq_ptr_);
+    sq_head_ = reinterpret_cast<unsigned *>(sq + p.sq_off.head);
+    sq_tail_ = reinterpret_cast<unsigned *>(sq + p.sq_off.tail);
+    sq_mask_ = *reinterpret_cast<unsigned *>(sq + p.sq_off.ring_mask);
+    sq_array_ = reinterpret_cast<unsigned *>(sq + p.sq_off.array);
+    cq_head_ = reinterpret_cast<unsigned *>(cq + p.cq_off.head);
+    cq_tail_ = reinterpret_cast<unsigned *>(cq + p.cq_off.tail);
+    cq_mask_ = *reinterpret_cast<unsigned *>(cq + p.cq_off.ring_mask);
+    cqes_ = reinterpret_cast<io_uring_cqe *>(cq + p.cq_off.cqes);
+    depth_ = p.sq_entries;
+    return true;
+  }
+  // Move every request; partial transfers are resubmitted for the rest.
+  // On a failure no new requests start, the ones in flight are reaped, and
+  // the first error is returned.
+  int run(const std::vector<Req> &reqs, bool read, const std::vector<std::string> &paths, std::string &err) {
+    std::lock_guard<std::mutex> lk(mu_);
+    struct Slot {
+      Req r;
+      iovec iov;
+    };
+    std::vector<Slot> slots(depth_);
+    std::vector<unsigned> free_slots(depth_);
+    for (unsigned k = 0; k < depth_; ++k) free_slots[k] = depth_ - 1 - k;
+    std::deque<Req> pending(reqs.begin(), reqs.end());
+    unsigned inflight = 0;
+    int rc = FKV_OK;
+    int enter_failures = 0;  // consecutive io_uring_enter failures other than interrupts
+    while ((rc == FKV_OK && !pending.empty()) || inflight > 0) {
+      unsigned tail = *sq_tail_;
+      unsigned added = 0;
+      while (rc == FKV_OK && !pending.empty() && !free_slots.empty()) {
+        const unsigned k = free_slots.back();
+        free_slots.pop_back();
+        Slot &sl = slots[k];
+        sl.r = pending.front();
+        pending.pop_front();
+        sl.iov.iov_base = sl.r.buf;
+        sl.iov.iov_len = (size_t)sl.r.len;
+        const unsigned idx = tail & sq_mask_;
+        io_uring_sqe *e = &sqes_[idx];
+        std::memset(e, 0, sizeof(*e));
+        e->opcode = read ? IORING_OP_READV : IORING_OP_WRITEV;
+        e->fd = sl.r.fd;
+        e->off = (uint64_t)sl.r.off;
+        e->addr = (uint64_t)(uintptr_t)&sl.iov;
+        e->len = 1;
+        e->user_data = k;
+        sq_array_[idx] = idx;
+        ++tail;
+        ++added;
+      }
+      __atomic_store_n(sq_tail_, tail, __ATOMIC_RELEASE);
+      inflight += added;  // every queued entry completes once the kernel consumes it
+      // Submit everything the kernel has not consumed yet (an interrupted
+      // call may leave entries behind) and wait for at least one completion.
+      const unsigned unsub = tail - __atomic_load_n(sq_head_, __ATOMIC_ACQUIRE);
+      const int got = (int)syscall(__NR_io_uring_enter, fd_, unsub, inflight > 0 ? 1 : 0,
+                                   IORING_ENTER_GETEVENTS, nullptr, 0);
+      if (got < 0 && errno != EINTR && errno != EAGAIN && errno != EBUSY) {
+        if (rc == FKV_OK) {
+          rc = FKV_ERR_IO;
+          err = std::string("io_uring_enter failed: ") + std::strerror(errno);
+        }
+        // Entries the kernel never took will not complete: stop counting
+        // them.  Those it took complete and are reaped below; a ring that
+        // keeps failing is given up after a few tries.
+        const unsigned left = tail - __atomic_load_n(sq_head_, __ATOMIC_ACQUIRE);
+        inflight -= std::min(inflight, left);
+        if (++enter_failures >= 4) break;
+      } else if (got >= 0) {
+        enter_failures = 0;
+      }
+      unsigned head = *cq_head_;
+      const unsigned ctail = __atomic_load_n(cq_tail_, __ATOMIC_ACQUIRE);
+      for (; head != ctail; ++head) {
+        const io_uring_cqe &c = cqes_[head & cq_mask_];
+        const unsigned k = (unsigned)c.user_data;
+        Req r = slots[k].r;
+        free_slots.push_back(k);
+        --inflight;
+        if (c.res < 0) {
+          if (c.res == -EINTR || c.res == -EAGAIN) {
+            pending.push_front(r);
+          } else if (rc == FKV_OK) {
+            rc = FKV_ERR_IO;
+            err = std::string(read ? "read" : "write") + " of " + std::to_string(r.len) + " bytes at offset " +
+                  std::to_string(r.off) + " in " + paths[r.file] + " failed: " + std::strerror(-c.res);
+          }
+        } else if (c.res == 0 && r.len > 0) {
+          if (rc == FKV_OK) {
+            rc = FKV_ERR_IO;
+            err = "short read at offset " + std::to_string(r.off) + " in " + paths[r.file] +
+                  " (past the end of the file)";
+          }
+        } else if (c.res < r.len) {
+          r.buf += c.res;
+          r.off += c.res;
+          r.len -= c.res;
+          pending.push_front(r);
+        }
+      }
+      __atomic_store_n(cq_head_, head, __ATOMIC_RELEASE);
+    }
+    return rc;
+  }
+
+ private:
+  int fd_ = -1;
+  void *sq_ptr_ = nullptr, *cq_ptr_ = nullptr;
+  size_t sq_sz_ = 0, cq_sz_ = 0, sqes_sz_ = 0;
+  io_uring_sqe *sqes_ = nullptr;
+  io_uring_cqe *cqes_ = nullptr;
+  unsigned *sq_head_ = nullptr, *sq_tail_ = nullptr, *sq_array_ = nullptr, *cq_head_ = nullptr,
+           *cq_tail_ = nullptr;
+  unsigned sq_mask_ = 0, cq_mask_ = 0, depth_ = 0;
+  std::mutex mu_;
+};
+
 int io_all(int fd, char *p, int64_t len, int64_t off, bool read, std::string &err, const std::string &path) {
   while (len > 0) {
     const ssize_t n = read ? pread(fd, p, (size_t)len, (off_t)off) : pwrite(fd, p, (size_t)len, (off_t)off);
@@ -153,6 +324,7 @@ struct fkv_ssd_ctx {
   std::vector<std::string> paths;
   std::vector<int> fd_buf, fd_direct;  // [d * F + f]; fd_direct -1 if O_DIRECT is refused
   IoPool pool;
+  std::unique_ptr<IoRing> ring[2];  // [0] reads, [1] writes; null = thread pool
   std::atomic<int64_t> last_ios{0}, last_bytes{0};
 };
 
@@ -163,8 +335,6 @@ extern "C" {
 int fkv_ssd_ctx_create(const char *const *paths, int num_devices, int files_per_device, int iouring_entries,
                        int iouring_flags, fkv_ssd_ctx **out) {
   fkv::clear_error();
-  (void)iouring_entries;  // accepted for the reference's constructor; see the file comment
-  (void)iouring_flags;
   if (!out) return fail(FKV_ERR_INVALID_ARG, "null output");
   *out = nullptr;
   if (!paths || num_devices <= 0 || files_per_device <= 0)
@@ -189,6 +359,12 @@ int fkv_ssd_ctx_create(const char *const *paths, int num_devices, int files_per_
     posix_fadvise(fb, 0, 0, POSIX_FADV_SEQUENTIAL);
     c->fd_buf.push_back(fb);
     c->fd_direct.push_back(open(c->paths[i].c_str(), O_RDWR | O_DIRECT));  // -1: filesystem refuses it
+  }
+  if (iouring_entries > 0) {
+    for (auto &r : c->ring) {
+      r.reset(new IoRing());
+      if (!r->init((unsigned)iouring_entries, (unsigned)iouring_flags)) r.reset();  // thread pool instead
+    }
   }
   *out = c.release();
   return FKV_OK;
@@ -319,13 +495,40 @@ int fkv_transfer_kv_blocks_ssd(fkv_ssd_ctx *ctx, int start_layer, int num_layers
       });
     }
   }
-  ctx->pool.ensure(D * threads);
   std::string err;
-  const int rc = ctx->pool.run(jobs, err);
+  int rc = FKV_OK;
+  if (IoRing *ring = ctx->ring[is_read ? 0 : 1].get()) {
+    // Ring path: the devices' requests interleaved, so every device has
+    // requests in flight.
+    std::vector<Req> reqs;
+    reqs.reserve((size_t)n_ios);
+    for (size_t k = 0;; ++k) {
+      bool any = false;
+      for (int d = 0; d < D; ++d) {
+        if (k >= segs[d].size()) continue;
+        any = true;
+        const Seg &s = segs[d][k];
+        int fd = ctx->fd_buf[s.file];
+        if (direct_ok && ctx->fd_direct[s.file] >= 0 && s.off % kDirectAlign == 0 &&
+            reinterpret_cast<uintptr_t>(s.cpu) % kDirectAlign == 0)
+          fd = ctx->fd_direct[s.file];
+        reqs.push_back({fd, s.file, s.cpu, s.len, s.off});
+      }
+      if (!any) break;
+    }
+    rc = ring->run(reqs, is_read != 0, ctx->paths, err);
+  } else {
+    ctx->pool.ensure(D * threads);
+    rc = ctx->pool.run(jobs, err);
+  }
   ctx->last_ios = n_ios;
   ctx->last_bytes = n_bytes;
   if (rc != FKV_OK) return fail(rc, err);
   return FKV_OK;
+}
+
+int fkv_ssd_ctx_uses_io_uring(const fkv_ssd_ctx *ctx) {
+  return ctx && ctx->ring[0] && ctx->ring[1] ? 1 : 0;
 }
 
 int fkv_ssd_last_stats(const fkv_ssd_ctx *ctx, int64_t *num_ios, int64_t *bytes) {

@@ -390,8 +390,10 @@ int fkv_ipc_open_count(void);
  * ---------------------------------------------------------------------- */
 /* paths[d * files_per_device + f] is file f of device d; every file is
  * opened read-write (buffered, plus O_DIRECT where the filesystem allows).
- * iouring_entries / iouring_flags are accepted for the reference's
- * constructor and unused: requests are issued by a thread pool. */
+ * iouring_entries > 0 issues requests through io_uring rings of that depth
+ * (one per direction; iouring_flags go to io_uring_setup), as the
+ * reference's optional io_uring path does; 0, or a ring that cannot be set
+ * up, issues them from a thread pool. */
 int fkv_ssd_ctx_create(const char *const *paths, int num_devices,
                        int files_per_device, int iouring_entries,
                        int iouring_flags, fkv_ssd_ctx **out);
@@ -415,6 +417,9 @@ int fkv_transfer_kv_blocks_ssd(fkv_ssd_ctx *ctx, int start_layer, int num_layers
                                int64_t block_stride_in_bytes, int is_read,
                                int num_blocks_per_file, int round_robin,
                                int num_threads_per_device, int is_mla);
+
+/* 1 if the context issues requests through io_uring, 0 for the thread pool. */
+int fkv_ssd_ctx_uses_io_uring(const fkv_ssd_ctx *ctx);
 
 /* File requests and bytes of the context's most recent transfer (chunks
  * adjacent in both the file and the pool are merged into one request). */

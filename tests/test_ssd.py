@@ -71,15 +71,32 @@ def oracle(imgs, st, pool, sids, cids, l0, nl, is_read, rr, mla):
                    st.block_stride_in_bytes, is_read, rr, mla)
 
 
-@pytest.mark.parametrize("threads", [1, 16])
+def io_uring_available() -> bool:
+    import tempfile
+    with tempfile.TemporaryDirectory() as d:
+        p = os.path.join(d, "f")
+        open(p, "wb").close()
+        ctx = c_ext.SSDIOCTX({0: [p]}, 1, 8, 0)
+        ok = ctx.uses_io_uring
+        ctx.close()
+    return ok
+
+
+@pytest.mark.parametrize("engine", ["threads1", "threads16", "io_uring"])
 @pytest.mark.parametrize("ci", range(len(CASES)), ids=[c[0] for c in CASES])
-def test_write_then_read_matches_oracle(ci, threads, tmp_path):
+def test_write_then_read_matches_oracle(ci, engine, tmp_path):
+    """Both request engines: the thread pool (1 or 16 threads per device)
+    and io_uring (64 entries)."""
+    if engine == "io_uring" and not io_uring_available():
+        pytest.skip("io_uring not available on this kernel")
+    threads = 1 if engine == "threads1" else 16
     case = CASES[ci]
     mla, rr, (l0, nl) = case[6], case[11], case[12]
     cpu_layout, files, per_file, st, cids, sids = setup(case, tmp_path)
     pool = aligned(cpu_layout.get_total_elements() * 2, 77 + ci)
     want = images(files)  # fresh files are all zero
-    ctx = c_ext.SSDIOCTX(files, len(files))
+    ctx = c_ext.SSDIOCTX(files, len(files), 64 if engine == "io_uring" else 0, 0)
+    assert ctx.uses_io_uring == (engine == "io_uring")
     run(ctx, st, pool, sids, cids, l0, nl, False, per_file, rr, mla, threads)
     oracle(want, st, pool, sids, cids, l0, nl, False, rr, mla)
     got = images(files)
@@ -210,3 +227,22 @@ def test_allocation_and_stride_helpers(tmp_path):
     assert st.block_stride_in_bytes == lay.get_block_stride() * 2
     with pytest.raises(ValueError):  # one layout type on both sides, as the reference requires
         SsdStrides.of(lay, KVCacheLayout(BW, 4, 30, 16, 2, 64), 8, 2)
+
+
+def test_io_uring_errors_and_stats(tmp_path):
+    """The io_uring path reports a read past the end of a file like the
+    thread pool, and merges requests the same way."""
+    if not io_uring_available():
+        pytest.skip("io_uring not available on this kernel")
+    case = CASES[0]
+    cpu_layout, files, per_file, st, cids, sids = setup(case, tmp_path)
+    pool = aligned(cpu_layout.get_total_elements() * 2, 1)
+    ctx = c_ext.SSDIOCTX(files, 1, 16, 0)
+    with pytest.raises(FlexKVError) as ei:
+        run(ctx, st, pool, np.array([per_file + 3], np.int64), np.array([0], np.int64), 0, 4, True,
+            per_file, 1, False)
+    assert ei.value.code == FKV_ERR_IO
+    ids = np.arange(8, 16, dtype=np.int64)
+    run(ctx, st, pool, ids, ids + 4, 0, 4, False, per_file, 1, False)
+    assert ctx.last_stats()[0] == 1  # BLOCKWISE joint run of 8 blocks: one request
+    ctx.close()
