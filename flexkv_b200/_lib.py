@@ -190,6 +190,17 @@ _SIGNATURES = {
         [c_int, c_int, c_int, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64,
          c_i64, c_i64, c_i64, c_vp, c_int, c_int, c_int],
     ),
+    "fkv_cache_index_create": (c_int, [c_int, c_i64, c_int, ctypes.POINTER(c_vp)]),
+    "fkv_cache_index_destroy": (None, [c_vp]),
+    "fkv_cache_index_match": (c_int, [c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_vp]),
+    "fkv_cache_index_put": (
+        c_int, [c_vp, c_vp, c_vp, c_int, c_vp, ctypes.POINTER(TransferDesc), c_int, c_vp, c_vp, c_vp,
+                c_vp, c_vp]),
+    "fkv_cache_index_set_ready": (c_int, [c_vp, c_vp, c_i64, c_int, P_i64, c_vp]),
+    "fkv_cache_index_remove": (c_int, [c_vp, c_vp, c_i64, c_vp, c_vp]),
+    "fkv_cache_index_recycle": (c_int, [c_vp, c_vp, c_i64, c_vp]),
+    "fkv_cache_index_take": (c_int, [c_vp, c_i64, c_vp, P_i64, c_vp]),
+    "fkv_cache_index_stats": (c_int, [c_vp, c_vp, c_vp]),
 }
 
 _lock = threading.Lock()

@@ -20,7 +20,8 @@ REPO_DIR = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_DIR = os.path.join(PKG_DIR, "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libflexkv_b200.so")
-SOURCES = ["fkv_common.cpp", "transfer.cu", "tp_group.cpp", "xxh64.cu", "engine.cpp", "ipc.cpp", "ssd.cpp"]
+SOURCES = ["fkv_common.cpp", "transfer.cu", "tp_group.cpp", "xxh64.cu", "engine.cpp", "ipc.cpp", "ssd.cpp",
+           "block_index.cu"]
 HEADERS = [os.path.join(CSRC, "fkv_common.h"), os.path.join(REPO_DIR, "include", "flexkv_b200.h")]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

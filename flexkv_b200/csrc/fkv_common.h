@@ -73,6 +73,14 @@ int release_staging(ThreadDeviceCtx *ctx, cudaStream_t stream);
 int transfer_enqueue(const fkv_transfer_desc &d, cudaStream_t s, char *ext_stage, size_t ext_cap);
 // Upper bound of the staging bytes transfer_enqueue needs for `d`.
 size_t transfer_stage_bytes(const fkv_transfer_desc &d);
+// Enqueue the SM copy kernel over device-resident id lists (capacity n_max)
+// whose length an earlier kernel on `s` writes to *n_dev.  `d` gives the
+// layout and direction; its id arrays and num_blocks are not used.  The
+// producer of the lists guarantees the GPU ids are in range; cpu ids are at
+// most max_cpu_id, checked here against d.cpu_pool_bytes when that is set.
+int transfer_enqueue_device_ids(const fkv_transfer_desc &d, const int64_t *gpu_ids_dev,
+                                const int64_t *cpu_ids_dev, const int64_t *n_dev, int64_t n_max,
+                                int64_t max_cpu_id, cudaStream_t s);
 
 // Classify a pointer: 1 = device memory (or managed), 0 = host.
 int pointer_is_device(const void *p, int *is_device, int *device);

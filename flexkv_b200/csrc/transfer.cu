@@ -128,7 +128,7 @@ __device__ __forceinline__ ChunkRef chunk_ref(const CopyParams &p, uint32_t c) {
 // volatile asm (compiler barriers), so without this order every chunk
 // would begin with a dependent round trip to the id and pointer tables.
 template <bool H2D, int UNROLL, bool PF256>
-__global__ void __launch_bounds__(kThreads) kv_copy_kernel(const CopyParams p) {
+__device__ __forceinline__ void copy_body(const CopyParams &p) {
   const int lane = threadIdx.x & 31;
   const uint32_t warp = (blockIdx.x * kThreads + threadIdx.x) >> 5;
   const uint32_t nwarps = (gridDim.x * kThreads) >> 5;
@@ -148,6 +148,27 @@ __global__ void __launch_bounds__(kThreads) kv_copy_kernel(const CopyParams p) {
     copy_chunk<UNROLL, PF256>(src, dst, p.n_vec, lane);
     cur = nxt;
   }
+}
+
+template <bool H2D, int UNROLL, bool PF256>
+__global__ void __launch_bounds__(kThreads) kv_copy_kernel(const CopyParams p) {
+  copy_body<H2D, UNROLL, PF256>(p);
+}
+
+// The same copy over id lists whose length a preceding kernel on the stream
+// wrote to *n_dev (clamped to n_max, the capacity of the lists): the fused
+// put path decides on the device which blocks move.
+template <bool H2D>
+__global__ void __launch_bounds__(kThreads) kv_copy_devn_kernel(CopyParams p, const int64_t *n_dev,
+                                                                uint32_t kv_dim, uint32_t num_layers,
+                                                                uint32_t n_max) {
+  const int64_t nd = *n_dev;
+  const uint32_t n = nd <= 0 ? 0u : (nd >= (int64_t)n_max ? n_max : (uint32_t)nd);
+  if (n == 0) return;
+  p.n = n;
+  p.per_layer = kv_dim * n;
+  p.num_chunks = num_layers * p.per_layer;
+  copy_body<H2D, 8, false>(p);
 }
 
 struct CeCopy {
@@ -254,7 +275,8 @@ struct HostPlan {
   int num_layers = 0;
   int64_t copy_bytes = 0;
   int64_t gkv = 0, gbs = 0, cls = 0, ckv = 0, cbs = 0;
-  char *cpu_dev_base = nullptr;  // device view of cpu_ptr + start_layer*cls + startoff
+  int64_t base_off = 0;          // start_layer*cls + startoff
+  char *cpu_dev_base = nullptr;  // device view of cpu_ptr + base_off
   const char *cpu_host_base = nullptr;
   std::vector<int64_t> sm_gpu, sm_cpu;  // blocks for the SM kernel
   std::vector<CeCopy> ce;
@@ -282,23 +304,18 @@ int validate_desc(const fkv_transfer_desc &d) {
   return FKV_OK;
 }
 
-int build_host_plan(const fkv_transfer_desc &d, int device, HostPlan &hp) {
-  if (int rc = validate_desc(d)) return rc;
-  hp.h2d = d.is_host_to_device != 0;
-  hp.kv_dim = d.is_mla ? 1 : 2;
-  hp.num_layers = d.num_layers;
-  hp.copy_bytes = (d.chunk_size_in_bytes / 16) * 16;  // transfer.cu:35 floor to float4
-  if (d.num_blocks == 0 || d.num_layers == 0 || hp.copy_bytes == 0) return FKV_OK;
-  if (!d.gpu_block_ids || !d.cpu_block_ids || !d.gpu_layer_ptrs || !d.cpu_ptr)
-    return fail(FKV_ERR_INVALID_ARG, "null id array, layer pointer table or cpu pointer");
-
+// Checks of the layout every copy path shares: int64-unit strides, the
+// page-locked host pool and its device view, 16-byte alignment of every
+// chunk base and GPU layer pointer.  n = blocks the op may move.  Fills the
+// stride and base fields of hp.
+int layout_checks(const fkv_transfer_desc &d, int64_t n, HostPlan &hp) {
   hp.gkv = trunc8(d.gpu_kv_stride_in_bytes);
   hp.gbs = trunc8(d.gpu_block_stride_in_bytes);
   hp.cls = trunc8(d.cpu_layer_stride_in_bytes);
   hp.ckv = trunc8(d.cpu_kv_stride_in_bytes);
   hp.cbs = trunc8(d.cpu_block_stride_in_bytes);
   const int64_t startoff = trunc8(d.cpu_startoff_inside_chunks);
-  const int64_t L = d.num_layers, KV = hp.kv_dim, n = d.num_blocks;
+  const int64_t L = d.num_layers, KV = hp.kv_dim;
   if ((uint64_t)L * KV * n >= (1ull << 31))
     return fail(FKV_ERR_INVALID_ARG, "num_layers*kv_dim*num_blocks must stay below 2^31; split the op");
 
@@ -327,6 +344,22 @@ int build_host_plan(const fkv_transfer_desc &d, int device, HostPlan &hp) {
     if ((uintptr_t)d.gpu_layer_ptrs[l] & 15)
       return fail(FKV_ERR_MISALIGNED, "gpu layer pointer " + std::to_string(l) + " is not 16-byte aligned");
   }
+  hp.base_off = base_off;
+  return FKV_OK;
+}
+
+int build_host_plan(const fkv_transfer_desc &d, int device, HostPlan &hp) {
+  if (int rc = validate_desc(d)) return rc;
+  hp.h2d = d.is_host_to_device != 0;
+  hp.kv_dim = d.is_mla ? 1 : 2;
+  hp.num_layers = d.num_layers;
+  hp.copy_bytes = (d.chunk_size_in_bytes / 16) * 16;  // transfer.cu:35 floor to float4
+  if (d.num_blocks == 0 || d.num_layers == 0 || hp.copy_bytes == 0) return FKV_OK;
+  if (!d.gpu_block_ids || !d.cpu_block_ids || !d.gpu_layer_ptrs || !d.cpu_ptr)
+    return fail(FKV_ERR_INVALID_ARG, "null id array, layer pointer table or cpu pointer");
+  const int64_t L = d.num_layers, KV = hp.kv_dim, n = d.num_blocks;
+  if (int rc = layout_checks(d, n, hp)) return rc;
+  const int64_t base_off = hp.base_off;
 
   // Per-id checks: range, alignment, pool bounds (reference truncates ids
   // to int, transfer.cu:41-42, so ids must fit in [0, 2^31)).
@@ -631,6 +664,72 @@ int transfer_enqueue(const fkv_transfer_desc &d, cudaStream_t s, char *ext_stage
     if (rc == FKV_OK) rc = rf;
   }
   return rc;
+}
+
+int transfer_enqueue_device_ids(const fkv_transfer_desc &d, const int64_t *gpu_ids_dev,
+                                const int64_t *cpu_ids_dev, const int64_t *n_dev, int64_t n_max,
+                                int64_t max_cpu_id, cudaStream_t s) {
+  if (int rc = validate_desc(d)) return rc;
+  if (n_max <= 0 || d.num_layers == 0 || d.chunk_size_in_bytes < 16) return FKV_OK;
+  if (!d.gpu_layer_ptrs || !d.cpu_ptr || !gpu_ids_dev || !cpu_ids_dev || !n_dev)
+    return fail(FKV_ERR_INVALID_ARG, "null layer pointer table, cpu pointer or id list");
+  int device = 0;
+  if (int rc = current_device(&device)) return rc;
+  HostPlan hp;
+  hp.h2d = d.is_host_to_device != 0;
+  hp.kv_dim = d.is_mla ? 1 : 2;
+  hp.num_layers = d.num_layers;
+  hp.copy_bytes = (d.chunk_size_in_bytes / 16) * 16;
+  if (int rc = layout_checks(d, n_max, hp)) return rc;
+  // Every id the lists can hold must be 16-byte aligned and, when the pool
+  // sizes are given, inside them (the ids are produced on the device).
+  if ((hp.cbs & 15) || (hp.gbs & 15))
+    return fail(FKV_ERR_MISALIGNED, "block strides must be multiples of 16 bytes for device-side id lists");
+  const int64_t L = d.num_layers, KV = hp.kv_dim;
+  if (d.cpu_pool_bytes > 0 &&
+      max_cpu_id * hp.cbs + hp.base_off + (L - 1) * hp.cls + (KV - 1) * hp.ckv + hp.copy_bytes > d.cpu_pool_bytes)
+    return fail(FKV_ERR_OUT_OF_RANGE, "cpu block id " + std::to_string(max_cpu_id) + " addresses past the cpu pool");
+  ThreadDeviceCtx *ctx = nullptr;
+  if (int rc = get_ctx(device, &ctx)) return rc;
+  const void *k = hp.h2d ? (const void *)kv_copy_devn_kernel<true> : (const void *)kv_copy_devn_kernel<false>;
+  int occ = 1;
+  FKV_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, kThreads, 0));
+  int sms = d.transfer_sms > 0 ? d.transfer_sms : env_int("FKV_TRANSFER_SMS", kDefaultSms);
+  sms = std::min(sms, ctx->num_sms);
+  const int64_t warps_per_cta = kThreads / 32;
+  int64_t grid = std::min<int64_t>((int64_t)sms * std::max(occ, 1), (L * KV * n_max + warps_per_cta - 1) / warps_per_cta);
+  grid = std::max<int64_t>(grid, 1);
+  // Layer pointer table: staged, uploaded on s, freed on s after the kernel.
+  const size_t tb = 8 * (size_t)L;
+  char *stage = nullptr;
+  if (int rc = acquire_staging(ctx, tb, &stage)) return rc;
+  for (int64_t l = 0; l < L; ++l) reinterpret_cast<int64_t *>(stage)[l] = (int64_t)(uintptr_t)d.gpu_layer_ptrs[l];
+  char *dev_table = nullptr;
+  if (int rc = scratch_alloc(device, tb, s, (void **)&dev_table)) return rc;
+  cudaError_t e = cudaMemcpyAsync(dev_table, stage, tb, cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) {
+    scratch_free(dev_table, s);
+    return fail_cuda(e, "cudaMemcpyAsync(layer table)");
+  }
+  if (int rc = release_staging(ctx, s)) return rc;
+  CopyParams p{};
+  p.layer_ptrs = reinterpret_cast<char *const *>(dev_table);
+  p.gpu_ids = gpu_ids_dev;
+  p.cpu_ids = cpu_ids_dev;
+  p.cpu_base = hp.cpu_dev_base;
+  p.gpu_kv_stride = hp.gkv;
+  p.gpu_block_stride = hp.gbs;
+  p.cpu_layer_stride = hp.cls;
+  p.cpu_kv_stride = hp.ckv;
+  p.cpu_block_stride = hp.cbs;
+  p.n_vec = hp.copy_bytes / 16;
+  const uint32_t kvd = (uint32_t)KV, nl = (uint32_t)L, nm = (uint32_t)n_max;
+  void *args[] = {&p, const_cast<int64_t **>(&n_dev), (void *)&kvd, (void *)&nl, (void *)&nm};
+  e = cudaLaunchKernel(k, dim3((unsigned)grid), dim3(kThreads), args, 0, s);
+  int rc = e == cudaSuccess ? FKV_OK : fail_cuda(e, "cudaLaunchKernel(kv_copy_devn_kernel)");
+  if (rc == FKV_OK) note_launch();
+  int rf = scratch_free(dev_table, s);
+  return rc != FKV_OK ? rc : rf;
 }
 
 }  // namespace fkv

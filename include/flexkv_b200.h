@@ -425,6 +425,80 @@ int fkv_ssd_ctx_uses_io_uring(const fkv_ssd_ctx *ctx);
  * adjacent in both the file and the pool are merged into one request). */
 int fkv_ssd_last_stats(const fkv_ssd_ctx *ctx, int64_t *num_ios, int64_t *bytes);
 
+/* ------------------------------------------------------------------------
+ * Put path of the CPU tier on the device: block index, block pool and the
+ * fused put (hash -> match -> allocate -> insert -> D2H copy -> ready in one
+ * stream of kernels).  Replaces, for the CPU tier:
+ *   GlobalCacheEngine.put / _put_impl_local  flexkv/cache/cache_engine.py:550-615, 787-902
+ *   CacheEngine.match / insert / take / cleanup / recycle   cache_engine.py:63-107
+ *   RadixTreeIndex.match_prefix / insert / set_ready         flexkv/cache/radixtree.py:143-316
+ *   Mempool.allocate_blocks / recycle_blocks                 flexkv/cache/mempool.py:28-55
+ * A batch is num_seqs token sequences, sequence s owning tokens
+ * [seq_offsets[s], seq_offsets[s+1]) of token_ids (int64, host or device;
+ * seq_offsets on the host) and floor(len_s / tokens_per_block) blocks at
+ * block offset blk_s (running sum of the previous sequences' blocks).  The
+ * requests of a batch take effect in order, as consecutive puts do.  Every
+ * call is synchronous on `stream` when it returns.
+ *
+ * Not done on the device: eviction.  When the pool is short a put comes back
+ * empty, as the reference's does when take() finds nothing evictable; the
+ * caller evicts with fkv_cache_index_remove + fkv_cache_index_recycle. */
+typedef struct fkv_cache_index fkv_cache_index;
+
+/* An empty index over a pool of num_total_blocks blocks (ids handed out in
+ * the reference Mempool's order). */
+int fkv_cache_index_create(int device, int64_t num_total_blocks, int tokens_per_block,
+                           fkv_cache_index **out);
+void fkv_cache_index_destroy(fkv_cache_index *ci);
+
+/* match_prefix of each sequence: num_matched[s] leading blocks cached,
+ * num_ready[s] of them ready; physical_blocks (optional, one entry per block
+ * of the batch) gets the pool block of every matched block and -1 after. */
+int fkv_cache_index_match(fkv_cache_index *ci, const int64_t *token_ids, const int64_t *seq_offsets,
+                          int num_seqs, int64_t *num_matched, int64_t *num_ready,
+                          int64_t *physical_blocks, void *stream);
+
+/* put of each sequence (CPU tier): skip the matched prefix, take pool blocks
+ * for the rest, insert them not ready, copy those GPU blocks to them, then
+ * (mark_ready != 0) mark them ready, as the put callback does.
+ * gpu_block_ids: one GPU block per block of the batch (host or device; the
+ * reference derives them from the slot mapping).  layout: the D2H copy's
+ * layout as for fkv_transfer_kv_blocks_ex (layer pointers, strides, cpu
+ * pointer, chunk size, is_mla, transfer_sms, cpu_pool_bytes,
+ * gpu_layer_bytes); its id arrays, num_blocks and direction are not used.
+ * Out: num_skipped[s] / num_transferred[s] (both 0 for an empty put, which
+ * includes a put the pool could not hold); cpu_block_ids (optional, per
+ * block: the pool block it was copied to, -1 if not copied); block_hashes
+ * (optional, per block). */
+int fkv_cache_index_put(fkv_cache_index *ci, const int64_t *token_ids, const int64_t *seq_offsets,
+                        int num_seqs, const int64_t *gpu_block_ids, const fkv_transfer_desc *layout,
+                        int mark_ready, int64_t *num_skipped, int64_t *num_transferred,
+                        int64_t *cpu_block_ids, uint64_t *block_hashes, void *stream);
+
+/* Mark cached blocks ready (ready != 0) or not, by block hash (host array);
+ * *num_found = how many were cached. */
+int fkv_cache_index_set_ready(fkv_cache_index *ci, const uint64_t *block_hashes, int64_t n, int ready,
+                              int64_t *num_found, void *stream);
+
+/* Drop cached blocks by hash (the caller's eviction); removed_blocks[q] =
+ * the pool block block q held, -1 if it was not cached.  The blocks stay
+ * allocated until fkv_cache_index_recycle. */
+int fkv_cache_index_remove(fkv_cache_index *ci, const uint64_t *block_hashes, int64_t n,
+                           int64_t *removed_blocks, void *stream);
+
+/* Mempool.recycle_blocks: return blocks to the pool; FKV_ERR_INVALID_ARG if
+ * one is already free (nothing changes) or appears twice. */
+int fkv_cache_index_recycle(fkv_cache_index *ci, const int64_t *block_ids, int64_t n, void *stream);
+
+/* CacheEngine.take(num, strict=False) with nothing to evict: allocate
+ * min(num, free) blocks into block_ids; *num_taken = how many. */
+int fkv_cache_index_take(fkv_cache_index *ci, int64_t num, int64_t *block_ids, int64_t *num_taken,
+                         void *stream);
+
+/* out[0..6] = free blocks, cached blocks, ready blocks, pool snapshot
+ * length, snapshot offset, deleted table slots, table slots. */
+int fkv_cache_index_stats(fkv_cache_index *ci, int64_t *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,74 @@
+"""The CPU restatement of the CPU-tier index and put decision
+(oracle/cache_index.py) against the reference's own GlobalCacheEngine,
+through the fixture tests/golden/put_path.json (made by
+tests/golden/make_put_golden.py)."""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from oracle import cache_index as CI
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "put_path.json")
+
+
+def scenarios():
+    with open(GOLDEN) as f:
+        return json.load(f)["scenarios"]
+
+
+def replay(sc):
+    """Run a golden scenario through the oracle; yield (kind, got, want)."""
+    tier = CI.CpuTier(sc["num_cpu_blocks"], sc["tpb"])
+    for b, batch in enumerate(sc["batches"]):
+        results = []
+        for req, want in zip(batch, sc["results"][b]):
+            r = tier.put(np.array(req["tokens"], dtype=np.int64), np.array(req["gpu_blocks"], dtype=np.int64))
+            results.append(r)
+            yield "put", (r.num_skipped, r.num_transferred, r.gpu_blocks.tolist(), r.cpu_blocks.tolist()), \
+                (want["skipped"], want["transferred"], want["gpu_blocks"], want["cpu_blocks"])
+        if sc["complete_each_batch"]:
+            for r in results:
+                tier.complete(r)
+        for p in sc["probes"][b]:
+            m = tier.match(np.array(p["tokens"], dtype=np.int64))
+            yield "probe", (m.num_matched, m.num_ready, m.blocks[:m.num_matched]), \
+                (p["num_matched"], p["num_ready"], p["blocks"])
+        yield "totals", (tier.pool.num_free, tier.tree.total_blocks(), tier.tree.total_ready()), \
+            (sc["num_free"][b], sc["total_cached"][b], sc["total_ready"][b])
+
+
+@pytest.mark.parametrize("name", [s["name"] for s in scenarios()])
+def test_oracle_matches_reference_put_path(name):
+    sc = next(s for s in scenarios() if s["name"] == name)
+    n = 0
+    for kind, got, want in replay(sc):
+        assert got == tuple(want), f"{name}: {kind} #{n}: got {got}, want {want}"
+        n += 1
+    assert n > 0
+
+
+def test_golden_covers_the_edge_cases():
+    scs = {s["name"]: s for s in scenarios()}
+    res = [r for s in scs.values() for b in s["results"] for r in b]
+    assert any(r["transferred"] == 0 for r in res)                       # empty puts
+    assert any(r["skipped"] > 0 and r["transferred"] > 0 for r in res)   # partial prefix hits
+    full = [r for b in scs["pool_full"]["results"] for r in b]
+    assert scs["pool_full"]["num_free"][-1] == 0 and sum(r["transferred"] == 0 for r in full) > 5
+    assert all(t == 0 for t in scs["callbacks_deferred"]["total_ready"])
+    tokens = [len(q["tokens"]) for s in scs.values() for b in s["batches"] for q in b]
+    assert min(tokens) < 4  # a request shorter than one block
+
+
+def test_pool_refreshes_its_snapshot_only_when_short():
+    """mempool.py:28-55: recycled ids wait until the snapshot runs out."""
+    p = CI.BlockPool(8)
+    a = p.allocate(3)
+    assert a.tolist() == [0, 1, 2]
+    p.recycle(np.array([1]))
+    assert p.allocate(4).tolist() == [3, 4, 5, 6]
+    assert p.allocate(2).tolist() == [1, 7]  # 2 > 1 left in the snapshot: refresh
+    p.recycle(np.array([0]))
+    with pytest.raises(ValueError):
+        p.recycle(np.array([0]))  # already free

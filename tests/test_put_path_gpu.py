@@ -1,0 +1,266 @@
+"""GPU tests of the CPU tier's device index and fused put path
+(flexkv_b200.cache_index over csrc/block_index.cu):
+
+* the reference's own put results (tests/golden/put_path.json, made by
+  running its GlobalCacheEngine): per-put outcomes and D2H block lists,
+  match results of probe sequences, pool and index totals;
+* the CPU restatement (oracle/cache_index.py) on large random batches;
+* the bytes the put copied (oracle transfer);
+* the pool's id order under take / recycle (Mempool restatement);
+* the caller's eviction (remove + recycle) and the error paths.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from flexkv_b200 import c_ext
+from flexkv_b200._lib import FKV_ERR_INVALID_ARG, FKV_ERR_OUT_OF_RANGE, FlexKVError
+from flexkv_b200.cache_index import CpuCacheIndex, KVLayout
+from gpu_util import oracle_transfer
+from kvcase import Case, fill_bytes
+from oracle import cache_index as CI
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "put_path.json")
+
+
+def golden():
+    with open(GOLDEN) as f:
+        return {s["name"]: s for s in json.load(f)["scenarios"]}
+
+
+class Pools:
+    """GPU layers and the pinned CPU pool of a case, with host images that
+    the oracle transfer updates alongside."""
+
+    def __init__(self, case: Case, seed: int = 7):
+        st = case.strides()
+        self.case, self.st = case, st
+        self.gpu_imgs = [fill_bytes(st["gpu_layer_bytes"], seed + l) for l in range(case.num_layers)]
+        self.cpu_img = fill_bytes(st["cpu_pool_bytes"], seed + 99)
+        self.layers = [torch.from_numpy(x.copy()).cuda() for x in self.gpu_imgs]
+        self.cpu = torch.from_numpy(self.cpu_img.copy()).pin_memory()
+        self.layout = KVLayout(torch.tensor([t.data_ptr() for t in self.layers], dtype=torch.int64),
+                               st["gpu_kv"], st["gpu_block"], self.cpu, st["cpu_kv"], st["cpu_layer"],
+                               st["cpu_block"], st["gpu_chunk"], case.is_mla, -1, st["gpu_layer_bytes"])
+
+    def expect_d2h(self, gids, cids):
+        if len(gids):
+            oracle_transfer(self.case, self.gpu_imgs, self.cpu_img, np.asarray(gids, dtype=np.int64),
+                            np.asarray(cids, dtype=np.int64), False)
+
+    def pool_matches(self) -> bool:
+        return np.array_equal(self.cpu.numpy(), self.cpu_img)
+
+
+@pytest.mark.parametrize("name", list(golden()))
+def test_device_put_path_matches_the_reference(name):
+    sc = golden()[name]
+    tpb = sc["tpb"]
+    pools = Pools(Case("golden", 2, 1, 8, tpb, 256, sc["num_cpu_blocks"]))
+    ci = CpuCacheIndex(sc["num_cpu_blocks"], tpb)
+    launches0 = c_ext.kernel_launch_count()
+    for b, batch in enumerate(sc["batches"]):
+        toks = [np.array(q["tokens"], dtype=np.int64) for q in batch]
+        gids = [np.array(q["gpu_blocks"], dtype=np.int64) for q in batch]
+        res = ci.put(toks, gids, pools.layout, mark_ready=sc["complete_each_batch"])
+        for r, want in enumerate(sc["results"][b]):
+            got = (int(res.num_skipped[r]), int(res.num_transferred[r]), res.gpu_blocks[r].tolist(),
+                   res.cpu_blocks[r].tolist())
+            assert got == (want["skipped"], want["transferred"], want["gpu_blocks"], want["cpu_blocks"]), \
+                f"batch {b} request {r}"
+            pools.expect_d2h(want["gpu_blocks"], want["cpu_blocks"])
+        assert pools.pool_matches(), f"batch {b}: pool bytes"
+        probes = sc["probes"][b]
+        m = ci.match([np.array(p["tokens"], dtype=np.int64) for p in probes])
+        for i, p in enumerate(probes):
+            assert (int(m.num_matched[i]), int(m.num_ready[i]), m.physical_blocks[i].tolist()) == \
+                (p["num_matched"], p["num_ready"], p["blocks"]), f"batch {b} probe {i}"
+        s = ci.stats()
+        assert (s["num_free_blocks"], s["total_cached_blocks"], s["total_ready_blocks"]) == \
+            (sc["num_free"][b], sc["total_cached"][b], sc["total_ready"][b])
+    assert c_ext.kernel_launch_count() > launches0
+    ci.close()
+
+
+def test_put_requests_gives_the_reference_return_masks():
+    """The reference-facing form: (token_ids, token_mask, slot_mapping) per
+    request, partial last blocks ignored, return masks as the reference's."""
+    sc = golden()["shared_prefixes"]
+    tpb = sc["tpb"]
+    pools = Pools(Case("golden", 2, 1, 8, tpb, 256, sc["num_cpu_blocks"]))
+    ci = CpuCacheIndex(sc["num_cpu_blocks"], tpb)
+    for b, batch in enumerate(sc["batches"]):
+        reqs = []
+        for q in batch:
+            tok = torch.tensor(q["tokens"], dtype=torch.int64)
+            g = np.array(q["gpu_blocks"], dtype=np.int64)
+            slots = np.zeros(len(tok), dtype=np.int64)
+            slots[:len(g) * tpb] = np.repeat(g, tpb) * tpb + np.tile(np.arange(tpb), len(g))
+            slots[len(g) * tpb:] = 255 * tpb + np.arange(len(tok) - len(g) * tpb)
+            reqs.append((tok, torch.ones(len(tok), dtype=torch.bool), torch.from_numpy(slots)))
+        masks, _ = ci.put_requests(reqs, pools.layout)
+        for r, want in enumerate(sc["results"][b]):
+            m = masks[r]
+            idx = torch.nonzero(m).flatten()
+            assert (int(idx[0]) // tpb if len(idx) else 0, len(idx) // tpb) == (want["skipped"], want["transferred"])
+    ci.close()
+
+
+def _requests(rng, n, tpb, max_blocks, vocab, seen, share, gpu_pool):
+    toks, gids = [], []
+    for _ in range(n):
+        if seen and rng.random() < share:
+            base = seen[rng.integers(len(seen))]
+            cut = int(rng.integers(0, len(base) + 1))
+            tok = np.concatenate([base[:cut], rng.integers(0, vocab, int(rng.integers(0, max_blocks * tpb // 2 + 1)))])
+        else:
+            tok = rng.integers(0, vocab, int(rng.integers(0, max_blocks * tpb + tpb)))
+        tok = tok[:max_blocks * tpb + tpb - 1].astype(np.int64)
+        seen.append(tok)
+        toks.append(tok)
+        gids.append(rng.choice(gpu_pool, size=len(tok) // tpb, replace=False).astype(np.int64))
+    return toks, gids
+
+
+@pytest.mark.parametrize("pool_blocks", [20000, 1500])
+def test_large_batches_match_the_oracle(pool_blocks):
+    """Batches of 256 requests of up to 32 blocks with shared prefixes, in
+    the Qwen2-7B token shape (tpb 16); the small pool runs out and its
+    puts come back empty from then on, as the reference's would."""
+    tpb = 16
+    rng = np.random.default_rng(pool_blocks)
+    pools = Pools(Case("big", 2, 1, 64, tpb, 2048, pool_blocks), seed=31)
+    tier = CI.CpuTier(pool_blocks, tpb)
+    ci = CpuCacheIndex(pool_blocks, tpb)
+    seen = []
+    for b in range(4):
+        toks, gids = _requests(rng, 256, tpb, 32, 2000, seen, 0.5, 2048)
+        res = ci.put(toks, gids, pools.layout)
+        want = [tier.put(t, g) for t, g in zip(toks, gids)]
+        for r, w in enumerate(want):
+            assert (int(res.num_skipped[r]), int(res.num_transferred[r])) == (w.num_skipped, w.num_transferred), r
+            assert res.cpu_blocks[r].tolist() == w.cpu_blocks.tolist(), r
+            assert res.gpu_blocks[r].tolist() == w.gpu_blocks.tolist(), r
+            pools.expect_d2h(w.gpu_blocks, w.cpu_blocks)
+        for w in want:
+            tier.complete(w)
+        assert pools.pool_matches()
+        probes = [seen[i] for i in rng.choice(len(seen), 64, replace=False)]
+        m = ci.match(probes)
+        for i, p in enumerate(probes):
+            w = tier.match(p)
+            assert (int(m.num_matched[i]), int(m.num_ready[i]), m.physical_blocks[i].tolist()) == \
+                (w.num_matched, w.num_ready, [int(x) for x in w.blocks])
+        s = ci.stats()
+        assert (s["num_free_blocks"], s["total_cached_blocks"], s["total_ready_blocks"]) == \
+            (tier.pool.num_free, tier.tree.total_blocks(), tier.tree.total_ready())
+    ci.close()
+
+
+def test_match_accepts_device_tokens_and_empty_sequences():
+    tpb = 16
+    pools = Pools(Case("dev", 2, 1, 64, tpb, 256, 512))
+    ci = CpuCacheIndex(512, tpb)
+    rng = np.random.default_rng(5)
+    toks = [rng.integers(0, 500, n).astype(np.int64) for n in (0, 7, 16, 100, 333)]
+    gids = [np.arange(len(t) // tpb, dtype=np.int64) + 10 * i for i, t in enumerate(toks)]
+    ci.put(toks, gids, pools.layout)
+    m_host = ci.match(toks)
+    m_dev = ci.match([torch.from_numpy(t).cuda() for t in toks])
+    assert m_host.num_matched.tolist() == m_dev.num_matched.tolist() == [len(t) // tpb for t in toks]
+    assert [x.tolist() for x in m_host.physical_blocks] == [x.tolist() for x in m_dev.physical_blocks]
+    assert ci.match([]).num_matched.tolist() == []
+    ci.close()
+
+
+def test_pool_order_under_take_and_recycle_matches_mempool():
+    """Ids come in the reference Mempool's order: a snapshot of the free
+    ids, refreshed only when a request does not fit in what is left."""
+    ci = CpuCacheIndex(700, 16)
+    pool = CI.BlockPool(700)
+    rng = np.random.default_rng(17)
+    live = []
+    for _ in range(80):
+        if rng.random() < 0.55 or not live:
+            n = int(rng.integers(0, 90))
+            got = ci.take(n)
+            want = pool.allocate(min(n, pool.num_free))
+            assert got.tolist() == want.tolist()
+            live.extend(got.tolist())
+        else:
+            k = int(rng.integers(1, min(len(live), 70) + 1))
+            pick = set(rng.choice(len(live), k, replace=False).tolist())
+            ids = np.array([live[i] for i in sorted(pick)], dtype=np.int64)
+            ci.recycle(ids)
+            pool.recycle(ids)
+            live = [x for j, x in enumerate(live) if j not in pick]
+        s = ci.stats()
+        assert (s["num_free_blocks"], s["pool_snapshot_len"], s["pool_snapshot_offset"]) == \
+            (pool.num_free, len(pool.ids), pool.offset)
+    ci.close()
+
+
+def test_caller_eviction_then_put():
+    """Eviction is the caller's: remove a request's own blocks, recycle them;
+    its match falls back to the shared prefix and later puts reuse the ids
+    in Mempool order."""
+    tpb = 16
+    pools = Pools(Case("evict", 2, 1, 64, tpb, 512, 256))
+    ci = CpuCacheIndex(256, tpb)
+    pool = CI.BlockPool(256)
+    rng = np.random.default_rng(23)
+    prefix = rng.integers(0, 1000, 4 * tpb).astype(np.int64)
+    a = np.concatenate([prefix, rng.integers(0, 1000, 6 * tpb)]).astype(np.int64)
+    b = np.concatenate([prefix, rng.integers(0, 1000, 3 * tpb)]).astype(np.int64)
+    res = ci.put([a, b], [np.arange(10), np.arange(100, 107)], pools.layout)
+    assert res.num_transferred.tolist() == [10, 3] and res.num_skipped.tolist() == [0, 4]
+    pool.allocate(10)
+    pool.allocate(3)
+    # evict b's own suffix (3 blocks, a leaf)
+    removed = ci.remove(res.block_hashes[1][4:])
+    assert removed.tolist() == res.cpu_blocks[1].tolist()
+    assert ci.remove(res.block_hashes[1][4:]).tolist() == [-1, -1, -1]  # already gone
+    ci.recycle(removed)
+    pool.recycle(removed)
+    m = ci.match([b, a])
+    assert m.num_matched.tolist() == [4, 10]
+    s = ci.stats()
+    assert (s["total_cached_blocks"], s["num_free_blocks"], s["deleted_slots"]) == (10, 246, 3)
+    fresh = [rng.integers(1000, 2000, n * tpb).astype(np.int64) for n in (30, 200, 20)]
+    res2 = ci.put(fresh, [np.arange(200, 200 + len(f) // tpb) % 512 for f in fresh], pools.layout)
+    want = [pool.allocate(min(len(f) // tpb, pool.num_free)) for f in fresh[:2]]
+    assert res2.cpu_blocks[0].tolist() == want[0].tolist()
+    assert res2.cpu_blocks[1].tolist() == want[1].tolist()
+    assert res2.num_transferred.tolist() == [30, 200, 0]  # 16 blocks left: the last put is empty
+    ci.close()
+
+
+def test_errors_leave_the_index_unchanged():
+    tpb = 16
+    pools = Pools(Case("err", 2, 1, 64, tpb, 64, 128))
+    ci = CpuCacheIndex(128, tpb)
+    tok = np.arange(5 * tpb, dtype=np.int64)
+    ci.put([tok], [np.arange(5)], pools.layout)
+    before = ci.stats()
+    with pytest.raises(FlexKVError) as e:
+        ci.recycle([100])  # never allocated: already free
+    assert e.value.code == FKV_ERR_INVALID_ARG
+    with pytest.raises(FlexKVError) as e:
+        ci.recycle([1, 1])
+    assert e.value.code == FKV_ERR_INVALID_ARG
+    with pytest.raises(FlexKVError) as e:
+        ci.recycle([128])
+    assert e.value.code == FKV_ERR_OUT_OF_RANGE
+    with pytest.raises(FlexKVError) as e:  # GPU block 64 is past the 64-block layer
+        ci.put([np.arange(100, 100 + 2 * tpb, dtype=np.int64)], [np.array([3, 64])], pools.layout)
+    assert e.value.code == FKV_ERR_OUT_OF_RANGE
+    with pytest.raises(ValueError):
+        ci.put([tok], [np.arange(4)], pools.layout)  # one GPU block per full block
+    assert ci.stats() == before
+    assert ci.match([tok]).num_matched.tolist() == [5]
+    ci.close()
