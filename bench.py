@@ -29,11 +29,14 @@ one TP group of --tp ranks driven from one process).
            pattern.
   extras — link peaks measured live (each rank alone, and all ranks at
            once when N > 1), the duplex rate, and at N = 1 on cfg2 the
-           XXH64 hashing, small-op latency and SSD-tier measurements.
+           XXH64 hashing, small-op latency, CPU-tier put path (device index
+           + fused put against the reference's per-request path) and
+           SSD-tier measurements.
   --impl reference — the reference's own transfer.cu built from its source
            (oracle/_ref) driven the way its worker drives it: one op at a
            time, transfer_sms=8, pinned id tensors, synchronous.
-  --hash-only / --ssd-only — only that measurement, one JSON line.
+  --hash-only / --ssd-only / --put-only — only that measurement, one JSON
+           line (--put-only on the --config shape).
 
 Multi-GPU (torchrun): every rank runs the same per-GPU workload on its own
 GPU and pools (data parallel, no collective on the data path); value is the
@@ -654,6 +657,122 @@ def measure_layerwise_read(S, groups: int = 8, reps: int = 3):
             "how": "one graph of chained layer-group H2D ops through the TransferEngine; wall clock"}
 
 
+def put_batches(S, n_batches: int, n_req: int = 256, seed: int = 77, vocab: int = 128256):
+    """Put batches: n_req requests of U[1,32] full blocks each; half of
+    them extend a prefix (1..all of its blocks) of an earlier request of the
+    same or an earlier batch by U[0,16] new blocks.  Token ids int64."""
+    tpb = S.cfg["tpb"]
+    rng = np.random.default_rng(seed)
+    seen, out = [], []
+    for _ in range(n_batches):
+        toks, gids = [], []
+        for _ in range(n_req):
+            if seen and rng.random() < 0.5:
+                base = seen[rng.integers(len(seen))]
+                cut = int(rng.integers(1, len(base) // tpb + 1))
+                tok = np.concatenate([base[:cut * tpb], rng.integers(0, vocab, int(rng.integers(0, 17)) * tpb)])
+            else:
+                tok = rng.integers(0, vocab, int(rng.integers(1, 33)) * tpb)
+            tok = tok.astype(np.int64)
+            seen.append(tok)
+            toks.append(tok)
+            gids.append(rng.choice(S.gpu_layout.num_block, len(tok) // tpb, replace=False).astype(np.int64))
+        out.append((toks, gids))
+    return out
+
+
+def measure_put_path(S, reps: int = 3):
+    """The CPU tier's put for batches of requests (cache_engine.py:787-902),
+    two consecutive 256-request batches per repetition on a fresh index.
+
+    ours: one flexkv_b200.cache_index.CpuCacheIndex.put per batch -- hash,
+      match, allocate, insert, D2H copy of the new blocks, mark ready, all on
+      the device, from host token buffers (wall clock, synchronous).
+    reference-style: per request, the CPU restatement of the reference's
+      tree and pool (oracle/cache_index.py: Python control flow like the
+      reference's, with the C XXH64) to decide, the reference's own
+      transfer.cu (oracle/_ref, transfer_sms=8, ids pinned per op,
+      synchronous) to copy, then the completion callback.
+    control only: the second batch put again -- every block cached, nothing
+      copied -- so the time is hashing, matching and deciding."""
+    from oracle import cache_index as CI
+    from oracle import oracle as O
+    from flexkv_b200.cache_index import CpuCacheIndex, KVLayout
+    tpb = S.cfg["tpb"]
+    layout = KVLayout(S.ptrs, S.g_kv, S.g_blk, S.cpu, S.c_kv, S.c_layer, S.c_blk, S.chunk, S.mla, -1,
+                      S.gpu_layer_bytes)
+    batches = put_batches(S, 2)
+    n_req = len(batches[0][0])
+    ours, ctl, ref, ref_ctl, moved = [], [], [], [], []
+    ref_lib = O.ref_lib() if O.reference_available() else None
+    ptrs = S.ptrs.pin_memory()
+    stream = torch.cuda.current_stream().cuda_stream
+    for rep in range(reps + 1):
+        ci = CpuCacheIndex(S.cpu_blocks, tpb)
+        try:
+            ts, blocks = [], 0
+            for toks, gids in batches:
+                t0 = time.perf_counter()
+                res = ci.put(toks, gids, layout)
+                ts.append(time.perf_counter() - t0)
+                blocks += int(res.num_transferred.sum())
+            t0 = time.perf_counter()
+            again = ci.put(*batches[1], layout)
+            tc = time.perf_counter() - t0
+            assert int(again.num_transferred.sum()) == 0
+        finally:
+            ci.close()
+        if rep:
+            ours.append(sum(ts))
+            ctl.append(tc)
+            moved.append(blocks)
+        if ref_lib is None:
+            continue
+        tier = CI.CpuTier(S.cpu_blocks, tpb)
+        t_all = t_dec = 0.0
+        ref_blocks = 0
+        for toks, gids in batches:
+            for tok, g in zip(toks, gids):
+                t0 = time.perf_counter()
+                r = tier.put(tok, g)
+                t1 = time.perf_counter()
+                if r.num_transferred:
+                    gp = torch.from_numpy(r.gpu_blocks).pin_memory()
+                    cp = torch.from_numpy(r.cpu_blocks).pin_memory()
+                    rc = ref_lib.ref_transfer_kv_blocks(len(gp), 0, len(S.layers), gp.data_ptr(), ptrs.data_ptr(),
+                                                        S.g_kv, S.g_blk, cp.data_ptr(), S.cpu.data_ptr(), S.c_kv,
+                                                        S.c_layer, S.c_blk, 0, S.chunk, stream, 8, 0, 0, int(S.mla))
+                    if rc != 0:
+                        raise RuntimeError(f"reference transfer_kv_blocks CUDA error {rc}")
+                t2 = time.perf_counter()
+                tier.complete(r)
+                t3 = time.perf_counter()
+                t_all += t3 - t0
+                t_dec += (t1 - t0) + (t3 - t2)
+                ref_blocks += r.num_transferred
+        if rep:
+            ref.append(t_all)
+            ref_ctl.append(t_dec)
+            assert ref_blocks == moved[-1], (ref_blocks, moved[-1])
+    bb = S.block_bytes
+    med = statistics.median
+    out = {
+        "requests_per_batch": n_req, "batches": len(batches), "blocks_copied": moved[-1],
+        "bytes_copied": moved[-1] * bb,
+        "ours": {"ms": round(med(ours) * 1e3, 2), "GBps": round(moved[-1] * bb / med(ours) / 1e9, 2),
+                 "requests_per_s": round(len(batches) * n_req / med(ours)),
+                 "control_us_per_request": round(med(ctl) / n_req * 1e6, 2)},
+        "how": "wall clock, median of %d repetitions of two consecutive batches on a fresh index" % reps,
+    }
+    if ref:
+        out["reference_style"] = {
+            "ms": round(med(ref) * 1e3, 2), "GBps": round(moved[-1] * bb / med(ref) / 1e9, 2),
+            "requests_per_s": round(len(batches) * n_req / med(ref)),
+            "control_us_per_request": round(med(ref_ctl) / (len(batches) * n_req) * 1e6, 2)}
+        out["speedup"] = round(med(ref) / med(ours), 2)
+    return out
+
+
 def measure_op_latency(S, args, n: int = 200):
     """Latency of one small op, each submitted after the previous finished:
     a 1-block H2D (every layer: 64 chunks of the workload's chunk size)
@@ -884,6 +1003,10 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
             extras["hash"] = measure_hash()
             extras["op_latency"] = measure_op_latency(S, args)
             extras["layerwise_read"] = measure_layerwise_read(S)
+            try:
+                extras["put_path"] = measure_put_path(S)
+            except Exception as e:  # reported, never fatal to the main line
+                extras["put_path"] = {"error": f"{type(e).__name__}: {e}"}
             try:  # a reported baseline; a failure is recorded, not fatal
                 extras["host_torch_path"] = measure_host_torch_path(S)
             except Exception as e:  # noqa: BLE001
@@ -1345,6 +1468,8 @@ def main():
                     help="only the XXH64 block-hash measurement (one JSON line)")
     ap.add_argument("--ssd-only", action="store_true",
                     help="only the SSD-tier measurement (one JSON line)")
+    ap.add_argument("--put-only", action="store_true",
+                    help="only the CPU-tier put-path measurement (one JSON line; --config picks the shape)")
     ap.add_argument("--tp", type=int, default=0,
                     help="TP ranks for cfg3 (one process drives them; default: all visible GPUs)")
     ap.add_argument("--no-extras", action="store_true",
@@ -1359,6 +1484,15 @@ def main():
         return
     if args.ssd_only:
         print(json.dumps({"ssd": measure_ssd()}), flush=True)
+        return
+    if args.put_only:
+        torch.cuda.set_device(0)
+        cfg = dict(CONFIGS[args.config])
+        S = Setup(cfg, args.layout or cfg["layout"], 1, 0, args.cpu_blocks, args.gpu_alloc)
+        try:
+            print(json.dumps({"put_path": dict(measure_put_path(S), workload=args.config)}), flush=True)
+        finally:
+            S.close()
         return
     if args.impl == "reference" and int(os.environ.get("RANK", "0")) != 0:
         return  # the reference arm runs on rank 0 only

@@ -74,20 +74,56 @@ class KVLayout:
         return d
 
 
-@dataclass
 class MatchBatch:
-    num_matched: np.ndarray        # [R] leading blocks cached (num_matched_blocks)
-    num_ready: np.ndarray          # [R] of them ready (num_ready_matched_blocks)
-    physical_blocks: List[np.ndarray]  # per request: pool blocks of the matched prefix
+    """Results of a batched match: per-request counts, and the pool blocks of
+    every matched block in one flat array (block offsets blk_off)."""
+
+    def __init__(self, num_matched: np.ndarray, num_ready: np.ndarray, phys_flat: np.ndarray,
+                 blk_off: np.ndarray):
+        self.num_matched = num_matched   # [R] leading blocks cached (num_matched_blocks)
+        self.num_ready = num_ready       # [R] of them ready (num_ready_matched_blocks)
+        self.phys_flat = phys_flat       # per block: its pool block, -1 past the match
+        self.blk_off = blk_off
+
+    @property
+    def physical_blocks(self) -> List[np.ndarray]:
+        """Per request: pool blocks of the matched prefix."""
+        o = self.blk_off
+        return [self.phys_flat[o[r]:o[r] + int(m)] for r, m in enumerate(self.num_matched)]
 
 
-@dataclass
 class PutBatch:
-    num_skipped: np.ndarray        # [R] leading blocks already cached, not copied
-    num_transferred: np.ndarray    # [R] blocks copied (0: empty put)
-    cpu_blocks: List[np.ndarray]   # per request: pool blocks the copied blocks went to
-    gpu_blocks: List[np.ndarray]   # per request: the GPU blocks copied
-    block_hashes: List[np.ndarray]  # per request: every block's hash (uint64)
+    """Results of a batched put, flat per block of the batch (block offsets
+    blk_off); per-request views on demand."""
+
+    def __init__(self, num_skipped, num_transferred, cpu_flat, gpu_flat, hashes_flat, blk_off):
+        self.num_skipped = num_skipped          # [R] leading blocks already cached, not copied
+        self.num_transferred = num_transferred  # [R] blocks copied (0: empty put)
+        self.cpu_flat = cpu_flat                # per block: pool block it went to, -1 if not copied
+        self.gpu_flat = gpu_flat                # per block: its GPU block
+        self.hashes_flat = hashes_flat          # per block: its hash (uint64)
+        self.blk_off = blk_off
+
+    def _moved(self, flat) -> List[np.ndarray]:
+        o = self.blk_off
+        return [flat[o[r] + int(s):o[r] + int(s) + int(t)]
+                for r, (s, t) in enumerate(zip(self.num_skipped, self.num_transferred))]
+
+    @property
+    def cpu_blocks(self) -> List[np.ndarray]:
+        """Per request: pool blocks the copied blocks went to."""
+        return self._moved(self.cpu_flat)
+
+    @property
+    def gpu_blocks(self) -> List[np.ndarray]:
+        """Per request: the GPU blocks copied."""
+        return self._moved(self.gpu_flat)
+
+    @property
+    def block_hashes(self) -> List[np.ndarray]:
+        """Per request: every full block's hash."""
+        o = self.blk_off
+        return [self.hashes_flat[o[r]:o[r + 1]] for r in range(len(o) - 1)]
 
     def return_mask(self, r: int, num_tokens: int, tokens_per_block: int) -> torch.Tensor:
         """The reference put's return mask: True over the copied tokens
@@ -98,20 +134,32 @@ class PutBatch:
         return m
 
 
-def _pack_tokens(token_ids: Sequence) -> Tuple[object, np.ndarray, object]:
-    """Concatenate a batch of token sequences (int64; host or CUDA) and give
-    the token offsets.  Returns (buffer kept alive, offsets, pointer)."""
+def _pack_tokens(token_ids: Sequence) -> Tuple[object, np.ndarray, int]:
+    """Concatenate a batch of token sequences (int64; numpy, host or CUDA
+    tensors) and give the token offsets.  Returns (buffer kept alive,
+    offsets, pointer)."""
+    if all(isinstance(t, np.ndarray) for t in token_ids):
+        lens = np.fromiter((t.size for t in token_ids), dtype=np.int64, count=len(token_ids))
+        buf = np.ascontiguousarray(np.concatenate(token_ids).astype(np.int64, copy=False)) \
+            if len(token_ids) and lens.sum() else np.zeros(1, dtype=np.int64)
+        offsets = np.zeros(len(token_ids) + 1, dtype=np.int64)
+        np.cumsum(lens, out=offsets[1:])
+        return buf, offsets, buf.ctypes.data
     seqs = [t if isinstance(t, torch.Tensor) else torch.as_tensor(np.asarray(t, dtype=np.int64))
             for t in token_ids]
     lens = np.array([int(t.numel()) for t in seqs], dtype=np.int64)
     offsets = np.zeros(len(seqs) + 1, dtype=np.int64)
     np.cumsum(lens, out=offsets[1:])
-    on_gpu = any(t.is_cuda for t in seqs)
-    dev = next((t.device for t in seqs if t.is_cuda), None)
-    parts = [t.reshape(-1).to(dtype=torch.int64, device=dev if on_gpu else "cpu") for t in seqs]
-    buf = torch.cat(parts) if parts and offsets[-1] > 0 else torch.zeros(1, dtype=torch.int64,
-                                                                        device=dev if on_gpu else "cpu")
+    dev = next((t.device for t in seqs if t.is_cuda), torch.device("cpu"))
+    parts = [t.reshape(-1).to(dtype=torch.int64, device=dev) for t in seqs]
+    buf = torch.cat(parts) if parts and offsets[-1] > 0 else torch.zeros(1, dtype=torch.int64, device=dev)
     return buf, offsets, buf.data_ptr()
+
+
+def _blk_off(offsets: np.ndarray, tpb: int) -> np.ndarray:
+    out = np.zeros(len(offsets), dtype=np.int64)
+    np.cumsum((offsets[1:] - offsets[:-1]) // tpb, out=out[1:])
+    return out
 
 
 class CpuCacheIndex:
@@ -133,24 +181,26 @@ class CpuCacheIndex:
         with torch.cuda.device(self.device):
             return int(torch.cuda.current_stream().cuda_stream)
 
-    def _split(self, flat: np.ndarray, offsets: np.ndarray) -> List[np.ndarray]:
-        tpb = self.tokens_per_block
-        blk = np.concatenate([[0], np.cumsum((offsets[1:] - offsets[:-1]) // tpb)])
-        return [flat[blk[r]:blk[r + 1]] for r in range(len(offsets) - 1)]
-
     def match(self, token_ids: Sequence) -> MatchBatch:
         """match_prefix of every sequence (radixtree.py:143-195)."""
         buf, offsets, ptr = _pack_tokens(token_ids)
+        return self.match_packed(ptr, offsets)
+
+    def match_packed(self, token_ptr: int, seq_offsets: np.ndarray) -> MatchBatch:
+        """match over a packed batch: token_ptr addresses the int64 tokens of
+        all sequences (host or device), seq_offsets (R+1, host) delimits
+        them."""
+        offsets = np.ascontiguousarray(seq_offsets, dtype=np.int64)
         R = len(offsets) - 1
-        nb = int(((offsets[1:] - offsets[:-1]) // self.tokens_per_block).sum())
+        blk = _blk_off(offsets, self.tokens_per_block)
+        nb = int(blk[-1])
         nm = np.zeros(R, dtype=np.int64)
         nr = np.zeros(R, dtype=np.int64)
         phys = np.full(max(nb, 1), -1, dtype=np.int64)
-        check(_lib.load().fkv_cache_index_match(self._h, ptr, offsets.ctypes.data, R, nm.ctypes.data,
+        check(_lib.load().fkv_cache_index_match(self._h, token_ptr, offsets.ctypes.data, R, nm.ctypes.data,
                                                 nr.ctypes.data, phys.ctypes.data, self._stream()),
               "CpuCacheIndex.match")
-        per = self._split(phys[:nb], offsets)
-        return MatchBatch(nm, nr, [p[:int(m)].copy() for p, m in zip(per, nm)])
+        return MatchBatch(nm, nr, phys[:nb], blk)
 
     def put(self, token_ids: Sequence, gpu_block_ids: Sequence, layout: KVLayout,
             mark_ready: bool = True) -> PutBatch:
@@ -161,38 +211,46 @@ class CpuCacheIndex:
         gpu_block_ids[r] (one per full block) and, with mark_ready, marked
         ready once the copy is done (the put callback).  Returns when the
         copies are complete."""
-        tpb = self.tokens_per_block
         if len(token_ids) != len(gpu_block_ids):
             raise ValueError("one gpu block list per request")
         buf, offsets, ptr = _pack_tokens(token_ids)
+        nblk = (offsets[1:] - offsets[:-1]) // self.tokens_per_block
+        glen = np.fromiter((len(g) for g in gpu_block_ids), dtype=np.int64, count=len(gpu_block_ids))
+        bad = np.flatnonzero(glen != nblk)
+        if len(bad):
+            r = int(bad[0])
+            raise ValueError(f"request {r}: {glen[r]} gpu blocks for {nblk[r]} full blocks")
+        parts = [np.asarray(g.cpu() if isinstance(g, torch.Tensor) else g, dtype=np.int64).reshape(-1)
+                 for g in gpu_block_ids]
+        gids = np.concatenate(parts) if parts else np.zeros(0, dtype=np.int64)
+        return self.put_packed(ptr, offsets, gids, layout, mark_ready)
+
+    def put_packed(self, token_ptr: int, seq_offsets: np.ndarray, gpu_block_ids: np.ndarray,
+                   layout: KVLayout, mark_ready: bool = True) -> PutBatch:
+        """put over a packed batch: token_ptr addresses the int64 tokens of
+        all sequences (host or device), seq_offsets (R+1, host) delimits
+        them, gpu_block_ids holds one GPU block per full block of the batch,
+        sequence by sequence."""
+        offsets = np.ascontiguousarray(seq_offsets, dtype=np.int64)
         R = len(offsets) - 1
-        nblk = (offsets[1:] - offsets[:-1]) // tpb
-        gparts = []
-        for r, g in enumerate(gpu_block_ids):
-            g = np.asarray(g.cpu() if isinstance(g, torch.Tensor) else g, dtype=np.int64).reshape(-1)
-            if len(g) != nblk[r]:
-                raise ValueError(f"request {r}: {len(g)} gpu blocks for {nblk[r]} full blocks")
-            gparts.append(g)
-        nb = int(nblk.sum())
-        gids = np.ascontiguousarray(np.concatenate(gparts) if gparts else np.zeros(0, np.int64))
+        blk = _blk_off(offsets, self.tokens_per_block)
+        nb = int(blk[-1])
+        gids = np.ascontiguousarray(gpu_block_ids, dtype=np.int64).reshape(-1)
+        if len(gids) != nb:
+            raise ValueError(f"{len(gids)} gpu blocks for {nb} full blocks in the batch")
         if nb == 0:
             gids = np.zeros(1, dtype=np.int64)
         nsk = np.zeros(R, dtype=np.int64)
         ntr = np.zeros(R, dtype=np.int64)
-        cpu = np.full(max(nb, 1), -1, dtype=np.int64)
-        hashes = np.zeros(max(nb, 1), dtype=np.uint64)
+        cpu = np.empty(max(nb, 1), dtype=np.int64)
+        hashes = np.empty(max(nb, 1), dtype=np.uint64)
         d = layout.desc()
-        check(_lib.load().fkv_cache_index_put(self._h, ptr, offsets.ctypes.data, R, gids.ctypes.data,
+        check(_lib.load().fkv_cache_index_put(self._h, token_ptr, offsets.ctypes.data, R, gids.ctypes.data,
                                               ctypes.byref(d), int(bool(mark_ready)), nsk.ctypes.data,
                                               ntr.ctypes.data, cpu.ctypes.data, hashes.ctypes.data,
                                               self._stream()),
               "CpuCacheIndex.put")
-        cpu_per = self._split(cpu[:nb], offsets)
-        g_per = self._split(gids[:nb], offsets)
-        h_per = self._split(hashes[:nb], offsets)
-        cpu_blocks = [c[int(s):int(s) + int(t)].copy() for c, s, t in zip(cpu_per, nsk, ntr)]
-        gpu_blocks = [g[int(s):int(s) + int(t)].copy() for g, s, t in zip(g_per, nsk, ntr)]
-        return PutBatch(nsk, ntr, cpu_blocks, gpu_blocks, [h.copy() for h in h_per])
+        return PutBatch(nsk, ntr, cpu[:nb], gids[:nb], hashes[:nb], blk)
 
     def put_requests(self, requests: Sequence[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]],
                      layout: KVLayout, mark_ready: bool = True) -> Tuple[List[torch.Tensor], PutBatch]:

@@ -692,8 +692,18 @@ int transfer_enqueue_device_ids(const fkv_transfer_desc &d, const int64_t *gpu_i
   ThreadDeviceCtx *ctx = nullptr;
   if (int rc = get_ctx(device, &ctx)) return rc;
   const void *k = hp.h2d ? (const void *)kv_copy_devn_kernel<true> : (const void *)kv_copy_devn_kernel<false>;
-  int occ = 1;
-  FKV_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, kThreads, 0));
+  static int occ_cache[64][2] = {{0}};  // CTAs per SM, per device and direction
+  int occ = 0;
+  {
+    std::lock_guard<std::mutex> lk(g_occ.mu);
+    occ = occ_cache[device & 63][hp.h2d ? 1 : 0];
+  }
+  if (occ == 0) {
+    FKV_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, kThreads, 0));
+    occ = std::max(occ, 1);
+    std::lock_guard<std::mutex> lk(g_occ.mu);
+    occ_cache[device & 63][hp.h2d ? 1 : 0] = occ;
+  }
   int sms = d.transfer_sms > 0 ? d.transfer_sms : env_int("FKV_TRANSFER_SMS", kDefaultSms);
   sms = std::min(sms, ctx->num_sms);
   const int64_t warps_per_cta = kThreads / 32;
