@@ -4,6 +4,8 @@
 KV-block gather/scatter, the tensor-parallel group, the XXH64 block hashes
 and the SSD tier; ``flexkv_b200.engine.TransferEngine`` mirrors FlexKV's
 TransferEngine (GPU, CPU and SSD ops with dependencies);
+``flexkv_b200.cache_index.CpuCacheIndex`` runs the CPU tier's put path
+(block index, block pool, fused put) on the device;
 ``flexkv_b200.memory_handle.TensorSharedHandle`` shares the inference
 engine's GPU KV tensors across processes.  Everything runs in
 libflexkv_b200.so (C ABI: include/flexkv_b200.h).
