@@ -682,18 +682,21 @@ def put_batches(S, n_batches: int, n_req: int = 256, seed: int = 77, vocab: int 
 
 
 def measure_put_path(S, reps: int = 3):
-    """The CPU tier's put for batches of requests (cache_engine.py:787-902),
-    two consecutive 256-request batches per repetition on a fresh index.
+    """The CPU tier's put and get for batches of requests
+    (cache_engine.py:150-219, 412-615, 787-902): per repetition, on a fresh
+    index, two consecutive 256-request put batches, then a 256-request get
+    batch of sequences the puts cached (all blocks, into new GPU blocks).
 
-    ours: one flexkv_b200.cache_index.CpuCacheIndex.put per batch -- hash,
-      match, allocate, insert, D2H copy of the new blocks, mark ready, all on
-      the device, from host token buffers (wall clock, synchronous).
+    ours: one flexkv_b200.cache_index.CpuCacheIndex call per batch -- put:
+      hash, match, allocate, insert, D2H copy of the new blocks, mark ready;
+      get: hash, match, H2D copy of the ready prefix -- all on the device,
+      from host token buffers (wall clock, synchronous).
     reference-style: per request, the CPU restatement of the reference's
       tree and pool (oracle/cache_index.py: Python control flow like the
       reference's, with the C XXH64) to decide, the reference's own
       transfer.cu (oracle/_ref, transfer_sms=8, ids pinned per op,
-      synchronous) to copy, then the completion callback.
-    control only: the second batch put again -- every block cached, nothing
+      synchronous) to copy, then the put's completion callback.
+    control only: the second put batch again -- every block cached, nothing
       copied -- so the time is hashing, matching and deciding."""
     from oracle import cache_index as CI
     from oracle import oracle as O
@@ -703,10 +706,29 @@ def measure_put_path(S, reps: int = 3):
                       S.gpu_layer_bytes)
     batches = put_batches(S, 2)
     n_req = len(batches[0][0])
-    ours, ctl, ref, ref_ctl, moved = [], [], [], [], []
+    rng = np.random.default_rng(91)
+    every = [t for toks, _ in batches for t in toks]
+    gtoks = [every[i] for i in rng.choice(len(every), n_req, replace=False)]
+    # distinct GPU destinations across the get batch
+    perm = rng.permutation(S.gpu_layout.num_block).astype(np.int64)
+    cuts = np.cumsum([0] + [len(t) // tpb for t in gtoks])
+    if cuts[-1] > len(perm):
+        raise RuntimeError("get batch larger than the GPU pool")
+    ggids = [perm[cuts[i]:cuts[i + 1]] for i in range(len(gtoks))]
+    ours, ctl, ours_get, ref, ref_ctl, ref_get, moved, got_blocks = [], [], [], [], [], [], [], []
     ref_lib = O.ref_lib() if O.reference_available() else None
     ptrs = S.ptrs.pin_memory()
     stream = torch.cuda.current_stream().cuda_stream
+
+    def ref_copy(g, c, h2d):
+        gp = torch.from_numpy(g).pin_memory()
+        cp = torch.from_numpy(c).pin_memory()
+        rc = ref_lib.ref_transfer_kv_blocks(len(gp), 0, len(S.layers), gp.data_ptr(), ptrs.data_ptr(),
+                                            S.g_kv, S.g_blk, cp.data_ptr(), S.cpu.data_ptr(), S.c_kv,
+                                            S.c_layer, S.c_blk, 0, S.chunk, stream, 8, int(h2d), 0, int(S.mla))
+        if rc != 0:
+            raise RuntimeError(f"reference transfer_kv_blocks CUDA error {rc}")
+
     for rep in range(reps + 1):
         ci = CpuCacheIndex(S.cpu_blocks, tpb)
         try:
@@ -720,12 +742,17 @@ def measure_put_path(S, reps: int = 3):
             again = ci.put(*batches[1], layout)
             tc = time.perf_counter() - t0
             assert int(again.num_transferred.sum()) == 0
+            t0 = time.perf_counter()
+            gres = ci.get(gtoks, ggids, layout)
+            tg = time.perf_counter() - t0
         finally:
             ci.close()
         if rep:
             ours.append(sum(ts))
             ctl.append(tc)
+            ours_get.append(tg)
             moved.append(blocks)
+            got_blocks.append(int(gres.num_transferred.sum()))
         if ref_lib is None:
             continue
         tier = CI.CpuTier(S.cpu_blocks, tpb)
@@ -737,39 +764,48 @@ def measure_put_path(S, reps: int = 3):
                 r = tier.put(tok, g)
                 t1 = time.perf_counter()
                 if r.num_transferred:
-                    gp = torch.from_numpy(r.gpu_blocks).pin_memory()
-                    cp = torch.from_numpy(r.cpu_blocks).pin_memory()
-                    rc = ref_lib.ref_transfer_kv_blocks(len(gp), 0, len(S.layers), gp.data_ptr(), ptrs.data_ptr(),
-                                                        S.g_kv, S.g_blk, cp.data_ptr(), S.cpu.data_ptr(), S.c_kv,
-                                                        S.c_layer, S.c_blk, 0, S.chunk, stream, 8, 0, 0, int(S.mla))
-                    if rc != 0:
-                        raise RuntimeError(f"reference transfer_kv_blocks CUDA error {rc}")
+                    ref_copy(r.gpu_blocks, r.cpu_blocks, False)
                 t2 = time.perf_counter()
                 tier.complete(r)
                 t3 = time.perf_counter()
                 t_all += t3 - t0
                 t_dec += (t1 - t0) + (t3 - t2)
                 ref_blocks += r.num_transferred
+        t0 = time.perf_counter()
+        ref_got = 0
+        for tok, g in zip(gtoks, ggids):
+            r = tier.get(tok, g)
+            if r.num_transferred:
+                ref_copy(r.gpu_blocks, r.cpu_blocks, True)
+            ref_got += r.num_transferred
+        tg_ref = time.perf_counter() - t0
         if rep:
             ref.append(t_all)
             ref_ctl.append(t_dec)
+            ref_get.append(tg_ref)
             assert ref_blocks == moved[-1], (ref_blocks, moved[-1])
+            assert ref_got == got_blocks[-1], (ref_got, got_blocks[-1])
     bb = S.block_bytes
     med = statistics.median
     out = {
-        "requests_per_batch": n_req, "batches": len(batches), "blocks_copied": moved[-1],
-        "bytes_copied": moved[-1] * bb,
+        "requests_per_batch": n_req, "put_batches": len(batches), "blocks_copied": moved[-1],
+        "bytes_copied": moved[-1] * bb, "get_blocks_read": got_blocks[-1],
         "ours": {"ms": round(med(ours) * 1e3, 2), "GBps": round(moved[-1] * bb / med(ours) / 1e9, 2),
                  "requests_per_s": round(len(batches) * n_req / med(ours)),
                  "control_us_per_request": round(med(ctl) / n_req * 1e6, 2)},
-        "how": "wall clock, median of %d repetitions of two consecutive batches on a fresh index" % reps,
+        "ours_get": {"ms": round(med(ours_get) * 1e3, 2),
+                     "GBps": round(got_blocks[-1] * bb / med(ours_get) / 1e9, 2)},
+        "how": "wall clock, median of %d repetitions on a fresh index" % reps,
     }
     if ref:
         out["reference_style"] = {
             "ms": round(med(ref) * 1e3, 2), "GBps": round(moved[-1] * bb / med(ref) / 1e9, 2),
             "requests_per_s": round(len(batches) * n_req / med(ref)),
             "control_us_per_request": round(med(ref_ctl) / (len(batches) * n_req) * 1e6, 2)}
+        out["reference_style_get"] = {"ms": round(med(ref_get) * 1e3, 2),
+                                      "GBps": round(got_blocks[-1] * bb / med(ref_get) / 1e9, 2)}
         out["speedup"] = round(med(ref) / med(ours), 2)
+        out["speedup_get"] = round(med(ref_get) / med(ours_get), 2)
     return out
 
 

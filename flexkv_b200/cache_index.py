@@ -49,7 +49,7 @@ class KVLayout:
     transfer_sms: int = -1
     gpu_layer_bytes: int = 0
 
-    def desc(self) -> TransferDesc:
+    def desc(self, host_to_device: bool = False) -> TransferDesc:
         ptrs = self.gpu_layer_ptrs
         if ptrs.dtype != torch.int64 or ptrs.is_cuda:
             raise RuntimeError("gpu_layer_ptrs must be an int64 CPU tensor")
@@ -58,7 +58,7 @@ class KVLayout:
         d = TransferDesc()
         _lib.load().fkv_transfer_desc_init(ctypes.byref(d))
         d.num_layers = ptrs.numel()
-        d.is_host_to_device = 0
+        d.is_host_to_device = int(bool(host_to_device))
         d.is_mla = int(bool(self.is_mla))
         d.transfer_sms = int(self.transfer_sms)
         d.gpu_layer_ptrs = ptrs.data_ptr()
@@ -130,6 +130,36 @@ class PutBatch:
         (cache_engine.py:600-602)."""
         m = torch.zeros(num_tokens, dtype=torch.bool)
         a = int(self.num_skipped[r]) * tokens_per_block
+        m[a:a + int(self.num_transferred[r]) * tokens_per_block] = True
+        return m
+
+
+class GetBatch:
+    """Results of a batched get: per request the first block read
+    (block_starts) and how many were read, and per GPU entry the pool block
+    read into it (-1 if none; offsets goff)."""
+
+    def __init__(self, block_starts, num_transferred, cpu_flat, gpu_flat, goff):
+        self.block_starts = block_starts
+        self.num_transferred = num_transferred
+        self.cpu_flat = cpu_flat
+        self.gpu_flat = gpu_flat
+        self.goff = goff
+
+    @property
+    def cpu_blocks(self) -> List[np.ndarray]:
+        """Per request: the pool blocks read."""
+        return [self.cpu_flat[self.goff[r]:self.goff[r] + int(t)] for r, t in enumerate(self.num_transferred)]
+
+    @property
+    def gpu_blocks(self) -> List[np.ndarray]:
+        """Per request: the GPU blocks written."""
+        return [self.gpu_flat[self.goff[r]:self.goff[r] + int(t)] for r, t in enumerate(self.num_transferred)]
+
+    def return_mask(self, r: int, num_tokens: int, tokens_per_block: int) -> torch.Tensor:
+        """The reference get's return mask (cache_engine.py:201-203)."""
+        m = torch.zeros(num_tokens, dtype=torch.bool)
+        a = int(self.block_starts[r]) * tokens_per_block
         m[a:a + int(self.num_transferred[r]) * tokens_per_block] = True
         return m
 
@@ -251,6 +281,81 @@ class CpuCacheIndex:
                                               self._stream()),
               "CpuCacheIndex.put")
         return PutBatch(nsk, ntr, cpu[:nb], gids[:nb], hashes[:nb], blk)
+
+    def get(self, token_ids: Sequence, gpu_block_ids: Sequence, layout: KVLayout,
+            block_starts: Optional[Sequence[int]] = None) -> GetBatch:
+        """Gets of the CPU tier for a batch of requests (cache_engine.py:
+        412-548, SSD off): request r selects its full blocks from
+        block_starts[r] (default 0) on and brings one GPU block per selected
+        block; its ready cached blocks in that range are read into the
+        leading GPU blocks.  Returns when the copies are complete."""
+        if len(token_ids) != len(gpu_block_ids):
+            raise ValueError("one gpu block list per request")
+        buf, offsets, ptr = _pack_tokens(token_ids)
+        parts = [np.asarray(g.cpu() if isinstance(g, torch.Tensor) else g, dtype=np.int64).reshape(-1)
+                 for g in gpu_block_ids]
+        gids = np.concatenate(parts) if parts else np.zeros(0, dtype=np.int64)
+        return self.get_packed(ptr, offsets, gids, layout, block_starts)
+
+    def get_packed(self, token_ptr: int, seq_offsets: np.ndarray, gpu_block_ids: np.ndarray, layout: KVLayout,
+                   block_starts: Optional[Sequence[int]] = None) -> GetBatch:
+        """get over a packed batch (as put_packed; gpu_block_ids holds
+        n_r - block_starts[r] GPU blocks per request)."""
+        offsets = np.ascontiguousarray(seq_offsets, dtype=np.int64)
+        R = len(offsets) - 1
+        nblk = (offsets[1:] - offsets[:-1]) // self.tokens_per_block
+        starts = np.zeros(R, dtype=np.int64) if block_starts is None else \
+            np.ascontiguousarray(block_starts, dtype=np.int64).reshape(-1)
+        if len(starts) != R:
+            raise ValueError("one block start per request")
+        starts = np.where(nblk > 0, starts, 0)
+        if ((starts < 0) | ((nblk > 0) & (starts >= nblk))).any():
+            raise ValueError("block starts must lie in [0, blocks)")
+        goff = np.zeros(R + 1, dtype=np.int64)
+        np.cumsum(nblk - starts, out=goff[1:])
+        gids = np.ascontiguousarray(gpu_block_ids, dtype=np.int64).reshape(-1)
+        if len(gids) != goff[-1]:
+            raise ValueError(f"{len(gids)} gpu blocks for {goff[-1]} selected blocks in the batch")
+        ng = int(goff[-1])
+        gbuf = gids if ng else np.zeros(1, dtype=np.int64)
+        moved = np.zeros(R, dtype=np.int64)
+        cpu = np.full(max(ng, 1), -1, dtype=np.int64)
+        d = layout.desc(host_to_device=True)
+        check(_lib.load().fkv_cache_index_get(self._h, token_ptr, offsets.ctypes.data, R, starts.ctypes.data,
+                                              gbuf.ctypes.data, ctypes.byref(d), moved.ctypes.data,
+                                              cpu.ctypes.data, self._stream()),
+              "CpuCacheIndex.get")
+        return GetBatch(starts, moved, cpu[:ng], gids, goff)
+
+    def get_requests(self, requests: Sequence[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]],
+                     layout: KVLayout) -> Tuple[List[torch.Tensor], GetBatch]:
+        """``GlobalCacheEngine.get(request_id, token_ids, token_mask,
+        slot_mapping)`` for a batch (cache_engine.py:150-219, CPU tier):
+        the mask selects a suffix of the full blocks that ends at the last
+        full block; the GPU block of each selected block is
+        slot_mapping[::tpb] // tpb.  Returns the reference's return masks and
+        the batch result."""
+        tpb = self.tokens_per_block
+        toks, gids, starts, lens = [], [], [], []
+        for r, (token_ids, token_mask, slot_mapping) in enumerate(requests):
+            token_ids = torch.as_tensor(token_ids)
+            token_mask = torch.as_tensor(token_mask, dtype=torch.bool).clone()
+            slot_mapping = torch.as_tensor(slot_mapping)
+            if len(token_ids) != len(token_mask) or len(slot_mapping) != int(token_mask.sum()):
+                raise ValueError(f"request {r}: lengths of token_ids, token_mask and slot_mapping disagree")
+            aligned = (len(token_ids) // tpb) * tpb
+            token_mask[aligned:] = False
+            idx = torch.nonzero(token_mask).flatten()
+            bs = int(idx[0]) // tpb if len(idx) else 0
+            be = int(idx[-1]) // tpb + 1 if len(idx) else 0
+            if be != aligned // tpb:  # cache_engine.py:169
+                raise ValueError(f"request {r}: the token mask must reach the last full block")
+            lens.append(len(token_ids))
+            toks.append(token_ids[:aligned].to(torch.int64).numpy())
+            starts.append(bs)
+            gids.append((slot_mapping[::tpb][:be - bs] // tpb).cpu().numpy().astype(np.int64))
+        res = self.get(toks, gids, layout, starts)
+        return [res.return_mask(r, lens[r], tpb) for r in range(len(lens))], res
 
     def put_requests(self, requests: Sequence[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]],
                      layout: KVLayout, mark_ready: bool = True) -> Tuple[List[torch.Tensor], PutBatch]:

@@ -334,6 +334,36 @@ __global__ void match_kernel(Table t, const uint64_t *hashes, const int64_t *blk
   }
 }
 
+// The get decisions (cache_engine.py:412-548, CPU tier), one warp, after
+// match_kernel: request r reads physical_blocks[:num_ready][start_r:n_r]
+// (the reference takes the first num_ready matched blocks) into its leading
+// GPU blocks.  Gets change neither the index nor the pool, so the order only
+// fixes the list layout.
+__global__ void __launch_bounds__(32) get_lists_kernel(int num_req, const int64_t *blk_off, const int64_t *starts,
+                                                       const int64_t *goff, const int64_t *match_res,
+                                                       const int64_t *phys, const int64_t *gpu_ids, int64_t *h2d_gpu,
+                                                       int64_t *h2d_cpu, int64_t *cpu_out, int64_t *moved,
+                                                       int64_t *count) {
+  const int lane = threadIdx.x;
+  int64_t cnt = 0;
+  for (int r = 0; r < num_req; ++r) {
+    const int64_t o = blk_off[r], n = blk_off[r + 1] - o, bs = starts[r];
+    const int64_t ready = match_res[2 * (int64_t)r + 1];
+    int64_t f = (ready < n ? ready : n) - bs;
+    if (f < 0 || n == 0) f = 0;
+    const int64_t go = goff[r];
+    for (int64_t t = lane; t < f; t += 32) {
+      const int64_t c = phys[o + bs + t];
+      h2d_gpu[cnt + t] = gpu_ids[go + t];
+      h2d_cpu[cnt + t] = c;
+      cpu_out[go + t] = c;
+    }
+    if (lane == 0) moved[r] = f;
+    cnt += f;
+  }
+  if (lane == 0) *count = cnt;
+}
+
 // Flag changes by hash (set_ready for a batch of blocks): ready or not.
 __global__ void set_flags_kernel(Table t, const uint64_t *hashes, int64_t n, int ready, int64_t *found) {
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -834,6 +864,107 @@ int fkv_cache_index_put(fkv_cache_index *ci, const int64_t *token_ids, const int
   }
   if (cpu_block_ids) std::memcpy(cpu_block_ids, ci->pin + down_res, 8 * nb);
   if (block_hashes) std::memcpy(block_hashes, ci->pin + down_res + 8 * nb, 8 * nb);
+  return FKV_OK;
+}
+
+int fkv_cache_index_get(fkv_cache_index *ci, const int64_t *token_ids, const int64_t *seq_offsets, int num_seqs,
+                        const int64_t *block_starts, const int64_t *gpu_block_ids, const fkv_transfer_desc *layout,
+                        int64_t *num_transferred, int64_t *cpu_block_ids, void *stream) {
+  clear_error();
+  if (!ci || !layout) return fail(FKV_ERR_INVALID_ARG, "null index or layout");
+  if (num_seqs < 0 || (num_seqs > 0 && (!seq_offsets || !num_transferred)))
+    return fail(FKV_ERR_INVALID_ARG, "bad batch description");
+  if (num_seqs == 0) return FKV_OK;
+  std::lock_guard<std::mutex> lk(ci->mu);
+  DeviceGuard g(ci->device);
+  cudaStream_t s = (cudaStream_t)stream;
+  std::vector<int64_t> blk;
+  if (int rc = batch_offsets(seq_offsets, num_seqs, ci->tpb, blk)) return rc;
+  const int64_t nb = blk[num_seqs];
+  for (int r = 0; r < num_seqs; ++r) num_transferred[r] = 0;
+  // GPU entries: request r brings n_r - start_r GPU blocks (the mask's range).
+  std::vector<int64_t> starts((size_t)num_seqs, 0), goff((size_t)num_seqs + 1, 0);
+  for (int r = 0; r < num_seqs; ++r) {
+    const int64_t n = blk[r + 1] - blk[r];
+    const int64_t bs = block_starts ? block_starts[r] : 0;
+    if (n > 0 && (bs < 0 || bs >= n))
+      return fail(FKV_ERR_INVALID_ARG, "block_starts[" + std::to_string(r) + "] must lie in [0, blocks)");
+    starts[r] = n > 0 ? bs : 0;
+    goff[r + 1] = goff[r] + (n - starts[r]);
+  }
+  const int64_t ng = goff[num_seqs];
+  if (nb == 0) return FKV_OK;
+  if (!token_ids || !gpu_block_ids) return fail(FKV_ERR_INVALID_ARG, "null token ids or gpu block ids");
+  if (nb >= (1ll << 29)) return fail(FKV_ERR_INVALID_ARG, "too many blocks in one batch (limit 2^29)");
+  if (!layout->is_host_to_device) return fail(FKV_ERR_INVALID_ARG, "the get path copies host to device");
+  std::vector<int64_t> gids((size_t)ng);
+  int gdev = 0, gd = -1;
+  pointer_is_device(gpu_block_ids, &gdev, &gd);
+  if (gdev) FKV_CUDA(cudaMemcpy(gids.data(), gpu_block_ids, 8 * ng, cudaMemcpyDeviceToHost));
+  else std::memcpy(gids.data(), gpu_block_ids, 8 * ng);
+  const int64_t gbs = (layout->gpu_block_stride_in_bytes / 8) * 8;
+  const int64_t gkv = (layout->gpu_kv_stride_in_bytes / 8) * 8;
+  const int64_t gpu_extent = (layout->is_mla ? 0 : gkv) + (layout->chunk_size_in_bytes / 16) * 16;
+  for (int64_t i = 0; i < ng; ++i) {
+    const int64_t gi = gids[i];
+    if (gi < 0 || gi >= (1ll << 31))
+      return fail(FKV_ERR_OUT_OF_RANGE, "gpu block id out of [0, 2^31) at index " + std::to_string(i));
+    if (layout->gpu_layer_bytes > 0 && gi * gbs + gpu_extent > layout->gpu_layer_bytes)
+      return fail(FKV_ERR_OUT_OF_RANGE, "gpu block id " + std::to_string(gi) + " at index " +
+                                            std::to_string(i) + " addresses past the gpu layer");
+  }
+  size_t off = 0;
+  auto carve = [&](size_t bytes) { const size_t at = off; off = al16(off + bytes); return at; };
+  const size_t R1 = (size_t)num_seqs + 1;
+  const size_t o_hash = carve(8 * nb), o_off = carve(8 * R1), o_start = carve(8 * num_seqs), o_goff = carve(8 * R1),
+               o_res = carve(16 * (size_t)num_seqs), o_phys = carve(8 * nb), o_gid = carve(8 * ng + 8),
+               o_h2dg = carve(8 * ng + 8), o_h2dc = carve(8 * ng + 8), o_cpu = carve(8 * ng + 8),
+               o_moved = carve(8 * num_seqs), o_cnt = carve(16);
+  Scratch sc, tok;
+  sc.s = s;
+  if (int rc = scratch_alloc(ci->device, off, s, (void **)&sc.base)) return rc;
+  char *b = sc.base;
+  uint64_t *hashes = reinterpret_cast<uint64_t *>(b + o_hash);
+  int64_t *d_cnt = reinterpret_cast<int64_t *>(b + o_cnt);
+  if (int rc = hash_batch(ci, token_ids, seq_offsets, num_seqs, hashes, s, tok)) return rc;
+  const size_t up = 8 * (R1 + num_seqs + R1 + ng);
+  const size_t down = 8 * (size_t)num_seqs + 8 * ng;
+  if (int rc = ensure_pin(ci, std::max(up, down))) return rc;
+  int64_t *pin = reinterpret_cast<int64_t *>(ci->pin);
+  std::memcpy(pin, blk.data(), 8 * R1);
+  std::memcpy(pin + R1, starts.data(), 8 * num_seqs);
+  std::memcpy(pin + R1 + num_seqs, goff.data(), 8 * R1);
+  std::memcpy(pin + 2 * R1 + num_seqs, gids.data(), 8 * ng);
+  FKV_CUDA(cudaMemcpyAsync(b + o_off, pin, 8 * R1, cudaMemcpyHostToDevice, s));
+  FKV_CUDA(cudaMemcpyAsync(b + o_start, pin + R1, 8 * num_seqs, cudaMemcpyHostToDevice, s));
+  FKV_CUDA(cudaMemcpyAsync(b + o_goff, pin + R1 + num_seqs, 8 * R1, cudaMemcpyHostToDevice, s));
+  if (ng) FKV_CUDA(cudaMemcpyAsync(b + o_gid, pin + 2 * R1 + num_seqs, 8 * ng, cudaMemcpyHostToDevice, s));
+  FKV_CUDA(cudaMemsetAsync(b + o_cpu, 0xff, 8 * ng + 8, s));  // -1: not read
+  FKV_CUDA(cudaMemsetAsync(d_cnt, 0, 16, s));
+  const int64_t *d_off = reinterpret_cast<int64_t *>(b + o_off);
+  int64_t *d_res = reinterpret_cast<int64_t *>(b + o_res);
+  int64_t *d_phys = reinterpret_cast<int64_t *>(b + o_phys);
+  match_kernel<<<grid_for(32ll * num_seqs), 256, 0, s>>>(ci->table(), hashes, d_off, num_seqs, d_res, d_phys);
+  FKV_CUDA(cudaGetLastError());
+  get_lists_kernel<<<1, 32, 0, s>>>(num_seqs, d_off, reinterpret_cast<int64_t *>(b + o_start),
+                                    reinterpret_cast<int64_t *>(b + o_goff), d_res, d_phys,
+                                    reinterpret_cast<int64_t *>(b + o_gid), reinterpret_cast<int64_t *>(b + o_h2dg),
+                                    reinterpret_cast<int64_t *>(b + o_h2dc), reinterpret_cast<int64_t *>(b + o_cpu),
+                                    reinterpret_cast<int64_t *>(b + o_moved), d_cnt);
+  FKV_CUDA(cudaGetLastError());
+  note_launch(2);
+  fkv_transfer_desc d = *layout;
+  d.is_host_to_device = 1;
+  if (ng > 0)
+    if (int rc = transfer_enqueue_device_ids(d, reinterpret_cast<int64_t *>(b + o_h2dg),
+                                             reinterpret_cast<int64_t *>(b + o_h2dc), d_cnt, ng,
+                                             ci->num_blocks - 1, s))
+      return rc;
+  FKV_CUDA(cudaMemcpyAsync(pin, b + o_moved, 8 * num_seqs, cudaMemcpyDeviceToHost, s));
+  if (ng) FKV_CUDA(cudaMemcpyAsync(pin + num_seqs, b + o_cpu, 8 * ng, cudaMemcpyDeviceToHost, s));
+  FKV_CUDA(cudaStreamSynchronize(s));
+  std::memcpy(num_transferred, pin, 8 * num_seqs);
+  if (cpu_block_ids && ng) std::memcpy(cpu_block_ids, pin + num_seqs, 8 * ng);
   return FKV_OK;
 }
 

@@ -426,10 +426,12 @@ int fkv_ssd_ctx_uses_io_uring(const fkv_ssd_ctx *ctx);
 int fkv_ssd_last_stats(const fkv_ssd_ctx *ctx, int64_t *num_ios, int64_t *bytes);
 
 /* ------------------------------------------------------------------------
- * Put path of the CPU tier on the device: block index, block pool and the
- * fused put (hash -> match -> allocate -> insert -> D2H copy -> ready in one
- * stream of kernels).  Replaces, for the CPU tier:
+ * Put and get paths of the CPU tier on the device: block index, block pool,
+ * the fused put (hash -> match -> allocate -> insert -> D2H copy -> ready in
+ * one stream of kernels) and the fused get (hash -> match -> H2D copy).
+ * Replaces, for the CPU tier:
  *   GlobalCacheEngine.put / _put_impl_local  flexkv/cache/cache_engine.py:550-615, 787-902
+ *   GlobalCacheEngine.get / _get_impl_local  cache_engine.py:150-219, 412-548 (SSD off)
  *   CacheEngine.match / insert / take / cleanup / recycle   cache_engine.py:63-107
  *   RadixTreeIndex.match_prefix / insert / set_ready         flexkv/cache/radixtree.py:143-316
  *   Mempool.allocate_blocks / recycle_blocks                 flexkv/cache/mempool.py:28-55
@@ -474,6 +476,21 @@ int fkv_cache_index_put(fkv_cache_index *ci, const int64_t *token_ids, const int
                         int num_seqs, const int64_t *gpu_block_ids, const fkv_transfer_desc *layout,
                         int mark_ready, int64_t *num_skipped, int64_t *num_transferred,
                         int64_t *cpu_block_ids, uint64_t *block_hashes, void *stream);
+
+/* get of each sequence (CPU tier, cache_engine.py:150-219, 412-548, SSD
+ * off): the mask selects full blocks [block_starts[s], n_s) (block_starts
+ * NULL: all from 0); of the sequence's first num_ready matched blocks, those
+ * in that range are read into its leading GPU blocks.  gpu_block_ids: per
+ * sequence n_s - block_starts[s] GPU blocks (the reference's slot mapping of
+ * the masked blocks), concatenated.  layout: the H2D copy's layout (as for
+ * fkv_cache_index_put).  Out: num_transferred[s] blocks read (the return
+ * mask covers blocks [block_starts[s], +num_transferred[s])); cpu_block_ids
+ * (optional, one per GPU entry): the pool block read into it, -1 if none.
+ * The index and the pool do not change. */
+int fkv_cache_index_get(fkv_cache_index *ci, const int64_t *token_ids, const int64_t *seq_offsets,
+                        int num_seqs, const int64_t *block_starts, const int64_t *gpu_block_ids,
+                        const fkv_transfer_desc *layout, int64_t *num_transferred,
+                        int64_t *cpu_block_ids, void *stream);
 
 /* Mark cached blocks ready (ready != 0) or not, by block hash (host array);
  * *num_found = how many were cached. */

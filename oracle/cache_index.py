@@ -246,3 +246,25 @@ class CpuTier:
             return
         r.node.locks -= 1
         self.tree.set_ready(r.node, r.node_size)
+
+    def get(self, token_ids: np.ndarray, gpu_blocks: np.ndarray, block_start: int = 0) -> PutResult:
+        """cache_engine.py:150-219 and 412-548 (CPU tier, SSD off): the mask
+        selects full blocks [block_start, n); gpu_blocks holds one GPU block
+        per selected block.  The reference takes the first num_ready matched
+        blocks (physical_blocks[:num_ready_matched_blocks]), keeps those in
+        the selected range, and reads them into the leading GPU blocks.  A
+        get changes neither the tree nor the pool (its lock and callback only
+        bracket the copy)."""
+        h = self.hashes(token_ids)
+        n = len(h)
+        gpu_blocks = np.asarray(gpu_blocks, dtype=np.int64)
+        empty = PutResult(0, 0, np.zeros(0, np.int64), np.zeros(0, np.int64))
+        if n == 0:
+            return empty
+        assert 0 <= block_start < n and len(gpu_blocks) >= n - block_start
+        m = self.tree.match(h)
+        ready = m.blocks[:m.num_ready][block_start:n]
+        f = len(ready)
+        if f == 0:
+            return empty
+        return PutResult(block_start, f, gpu_blocks[:f].copy(), np.asarray(ready, dtype=np.int64))

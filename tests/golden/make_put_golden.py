@@ -14,10 +14,13 @@ Each scenario is a sequence of batches of puts (token ids + one GPU block per
 full block).  For every put the fixture records the reference's D2H op (GPU
 and CPU block ids) and its return mask as (skipped, transferred) block
 counts; after each batch it optionally runs the put callbacks (unlock +
-set ready), then records match results of probe sequences and the pool and
-tree totals.  The "pool_full" scenario never runs callbacks, so no cached
-block is evictable and take() hands out fewer blocks than asked once the
-pool is short: those puts come back empty, as with no eviction.
+set ready), then records match results of probe sequences, gets of earlier
+sequences from a random first block (the H2D op's block lists and the return
+mask as (start, transferred) block counts; each get's callback runs at
+once), and the pool and tree totals.  The "pool_full" scenario never runs
+callbacks, so no cached block is evictable and take() hands out fewer
+blocks than asked once the pool is short: those puts come back empty, as
+with no eviction.
 """
 from __future__ import annotations
 
@@ -98,7 +101,7 @@ def run_scenario(torch, refmods, name, seed, tpb, num_cpu_blocks, n_batches, per
     eng = GlobalCacheEngine(cc, mc)
     out = {"name": name, "tpb": tpb, "num_cpu_blocks": num_cpu_blocks,
            "complete_each_batch": complete_each_batch, "batches": [], "results": [],
-           "probes": [], "num_free": [], "total_cached": [], "total_ready": []}
+           "probes": [], "gets": [], "num_free": [], "total_cached": [], "total_ready": []}
     rid = 0
     for batch in batches:
         res, callbacks = [], []
@@ -137,6 +140,32 @@ def run_scenario(torch, refmods, name, seed, tpb, num_cpu_blocks, n_batches, per
                            "num_ready": int(m.num_ready_matched_blocks),
                            "blocks": m.physical_blocks[:m.num_matched_blocks].tolist()})
         out["probes"].append(probes)
+        gets = []
+        full = [t for t in seen if len(t) >= tpb]
+        for i in rng.choice(len(full), size=min(6, len(full)), replace=False):
+            tok = full[i]
+            n = len(tok) // tpb
+            bs = int(rng.integers(0, n))
+            g = rng.choice(256, size=n - bs, replace=False).astype(np.int64)
+            mask = np.zeros(len(tok), dtype=bool)
+            mask[bs * tpb:] = True
+            slots = np.zeros(int(mask.sum()), dtype=np.int64)
+            slots[:len(g) * tpb] = np.repeat(g, tpb) * tpb + np.tile(np.arange(tpb), len(g))
+            slots[len(g) * tpb:] = 255 * tpb + np.arange(len(slots) - len(g) * tpb)
+            graph, rmask, cb, _ = eng.get(rid, torch.from_numpy(tok), torch.from_numpy(mask),
+                                          torch.from_numpy(slots))
+            rid += 1
+            idx = torch.nonzero(rmask).flatten()
+            gpu_ids, cpu_ids = [], []
+            for op in graph._op_map.values():
+                if op.transfer_type == TransferType.H2D:
+                    gpu_ids = op.dst_descriptor.physical_block_ids.tolist()
+                    cpu_ids = op.src_descriptor.physical_block_ids.tolist()
+            cb()
+            gets.append({"tokens": tok.tolist(), "block_start": bs, "gpu_blocks": g.tolist(),
+                         "mask_start": int(idx[0]) // tpb if len(idx) else 0, "transferred": len(idx) // tpb,
+                         "copied_gpu_blocks": gpu_ids, "copied_cpu_blocks": cpu_ids})
+        out["gets"].append(gets)
         out["num_free"].append(int(eng.cpu_cache_engine.mempool.num_free_blocks))
         out["total_cached"].append(int(eng.cpu_cache_engine.index.total_cached_blocks()))
         out["total_ready"].append(int(eng.cpu_cache_engine.index.total_ready_blocks()))

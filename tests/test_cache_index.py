@@ -1,4 +1,4 @@
-"""The CPU restatement of the CPU-tier index and put decision
+"""The CPU restatement of the CPU-tier index, put and get decisions
 (oracle/cache_index.py) against the reference's own GlobalCacheEngine,
 through the fixture tests/golden/put_path.json (made by
 tests/golden/make_put_golden.py)."""
@@ -35,6 +35,12 @@ def replay(sc):
             m = tier.match(np.array(p["tokens"], dtype=np.int64))
             yield "probe", (m.num_matched, m.num_ready, m.blocks[:m.num_matched]), \
                 (p["num_matched"], p["num_ready"], p["blocks"])
+        for g in sc["gets"][b]:
+            r = tier.get(np.array(g["tokens"], dtype=np.int64), np.array(g["gpu_blocks"], dtype=np.int64),
+                         g["block_start"])
+            start = r.num_skipped if r.num_transferred else 0
+            yield "get", (start, r.num_transferred, r.gpu_blocks.tolist(), r.cpu_blocks.tolist()), \
+                (g["mask_start"], g["transferred"], g["copied_gpu_blocks"], g["copied_cpu_blocks"])
         yield "totals", (tier.pool.num_free, tier.tree.total_blocks(), tier.tree.total_ready()), \
             (sc["num_free"][b], sc["total_cached"][b], sc["total_ready"][b])
 
@@ -57,6 +63,9 @@ def test_golden_covers_the_edge_cases():
     full = [r for b in scs["pool_full"]["results"] for r in b]
     assert scs["pool_full"]["num_free"][-1] == 0 and sum(r["transferred"] == 0 for r in full) > 5
     assert all(t == 0 for t in scs["callbacks_deferred"]["total_ready"])
+    gets = [g for s in scs.values() for b in s["gets"] for g in b]
+    assert any(g["transferred"] > 0 and g["block_start"] > 0 for g in gets)  # mid-sequence reads
+    assert any(g["transferred"] == 0 for g in gets)                          # nothing ready
     tokens = [len(q["tokens"]) for s in scs.values() for b in s["batches"] for q in b]
     assert min(tokens) < 4  # a request shorter than one block
 

@@ -1,9 +1,10 @@
-"""GPU tests of the CPU tier's device index and fused put path
+"""GPU tests of the CPU tier's device index and fused put / get paths
 (flexkv_b200.cache_index over csrc/block_index.cu):
 
-* the reference's own put results (tests/golden/put_path.json, made by
-  running its GlobalCacheEngine): per-put outcomes and D2H block lists,
-  match results of probe sequences, pool and index totals;
+* the reference's own put and get results (tests/golden/put_path.json, made
+  by running its GlobalCacheEngine): per-put outcomes and D2H block lists,
+  per-get H2D block lists and return masks, match results of probe
+  sequences, pool and index totals;
 * the CPU restatement (oracle/cache_index.py) on large random batches;
 * the bytes the put copied (oracle transfer);
 * the pool's id order under take / recycle (Mempool restatement);
@@ -53,8 +54,16 @@ class Pools:
             oracle_transfer(self.case, self.gpu_imgs, self.cpu_img, np.asarray(gids, dtype=np.int64),
                             np.asarray(cids, dtype=np.int64), False)
 
+    def expect_h2d(self, gids, cids):
+        if len(gids):
+            oracle_transfer(self.case, self.gpu_imgs, self.cpu_img, np.asarray(gids, dtype=np.int64),
+                            np.asarray(cids, dtype=np.int64), True)
+
     def pool_matches(self) -> bool:
         return np.array_equal(self.cpu.numpy(), self.cpu_img)
+
+    def layers_match(self) -> bool:
+        return all(np.array_equal(t.cpu().numpy(), w) for t, w in zip(self.layers, self.gpu_imgs))
 
 
 @pytest.mark.parametrize("name", list(golden()))
@@ -80,6 +89,15 @@ def test_device_put_path_matches_the_reference(name):
         for i, p in enumerate(probes):
             assert (int(m.num_matched[i]), int(m.num_ready[i]), m.physical_blocks[i].tolist()) == \
                 (p["num_matched"], p["num_ready"], p["blocks"]), f"batch {b} probe {i}"
+        for i, gq in enumerate(sc["gets"][b]):
+            got = ci.get([np.array(gq["tokens"], dtype=np.int64)], [np.array(gq["gpu_blocks"], dtype=np.int64)],
+                         pools.layout, [gq["block_start"]])
+            t = int(got.num_transferred[0])
+            assert (int(got.block_starts[0]) if t else 0, t, got.gpu_blocks[0].tolist(), got.cpu_blocks[0].tolist()) \
+                == (gq["mask_start"], gq["transferred"], gq["copied_gpu_blocks"], gq["copied_cpu_blocks"]), \
+                f"batch {b} get {i}"
+            pools.expect_h2d(gq["copied_gpu_blocks"], gq["copied_cpu_blocks"])
+        assert pools.layers_match(), f"batch {b}: GPU bytes after the gets"
         s = ci.stats()
         assert (s["num_free_blocks"], s["total_cached_blocks"], s["total_ready_blocks"]) == \
             (sc["num_free"][b], sc["total_cached"][b], sc["total_ready"][b])
@@ -111,6 +129,34 @@ def test_put_requests_gives_the_reference_return_masks():
     ci.close()
 
 
+def test_get_requests_gives_the_reference_return_masks():
+    """The reference-facing form of get: a mask from the request's first
+    block to read through its last full block, slot mapping of the masked
+    tokens; return masks as the reference's."""
+    sc = golden()["shared_prefixes"]
+    tpb = sc["tpb"]
+    pools = Pools(Case("golden", 2, 1, 8, tpb, 256, sc["num_cpu_blocks"]))
+    ci = CpuCacheIndex(sc["num_cpu_blocks"], tpb)
+    for b, batch in enumerate(sc["batches"]):
+        ci.put([np.array(q["tokens"], dtype=np.int64) for q in batch],
+               [np.array(q["gpu_blocks"], dtype=np.int64) for q in batch], pools.layout)
+        reqs = []
+        for gq in sc["gets"][b]:
+            tok = torch.tensor(gq["tokens"], dtype=torch.int64)
+            bs, g = gq["block_start"], np.array(gq["gpu_blocks"], dtype=np.int64)
+            mask = torch.zeros(len(tok), dtype=torch.bool)
+            mask[bs * tpb:] = True
+            slots = np.zeros(int(mask.sum()), dtype=np.int64)
+            slots[:len(g) * tpb] = np.repeat(g, tpb) * tpb + np.tile(np.arange(tpb), len(g))
+            slots[len(g) * tpb:] = 255 * tpb + np.arange(len(slots) - len(g) * tpb)
+            reqs.append((tok, mask, torch.from_numpy(slots)))
+        masks, _ = ci.get_requests(reqs, pools.layout)
+        for m, gq in zip(masks, sc["gets"][b]):
+            idx = torch.nonzero(m).flatten()
+            assert (int(idx[0]) // tpb if len(idx) else 0, len(idx) // tpb) == (gq["mask_start"], gq["transferred"])
+    ci.close()
+
+
 def _requests(rng, n, tpb, max_blocks, vocab, seen, share, gpu_pool):
     toks, gids = [], []
     for _ in range(n):
@@ -134,12 +180,12 @@ def test_large_batches_match_the_oracle(pool_blocks):
     puts come back empty from then on, as the reference's would."""
     tpb = 16
     rng = np.random.default_rng(pool_blocks)
-    pools = Pools(Case("big", 2, 1, 64, tpb, 2048, pool_blocks), seed=31)
+    pools = Pools(Case("big", 2, 1, 64, tpb, 8192, pool_blocks), seed=31)
     tier = CI.CpuTier(pool_blocks, tpb)
     ci = CpuCacheIndex(pool_blocks, tpb)
     seen = []
     for b in range(4):
-        toks, gids = _requests(rng, 256, tpb, 32, 2000, seen, 0.5, 2048)
+        toks, gids = _requests(rng, 256, tpb, 32, 2000, seen, 0.5, 8192)
         res = ci.put(toks, gids, pools.layout)
         want = [tier.put(t, g) for t, g in zip(toks, gids)]
         for r, w in enumerate(want):
@@ -159,6 +205,20 @@ def test_large_batches_match_the_oracle(pool_blocks):
         s = ci.stats()
         assert (s["num_free_blocks"], s["total_cached_blocks"], s["total_ready_blocks"]) == \
             (tier.pool.num_free, tier.tree.total_blocks(), tier.tree.total_ready())
+        # gets of earlier sequences from random first blocks
+        gtoks = [t for t in (seen[i] for i in rng.choice(len(seen), 256, replace=False)) if len(t) >= tpb]
+        starts = [int(rng.integers(0, len(t) // tpb)) for t in gtoks]
+        # distinct destinations across the batch (duplicate GPU destinations race, as in the reference)
+        perm = rng.permutation(8192).astype(np.int64)
+        cuts = np.cumsum([0] + [len(t) // tpb - bs for t, bs in zip(gtoks, starts)])
+        ggids = [perm[cuts[i]:cuts[i + 1]] for i in range(len(gtoks))]
+        got = ci.get(gtoks, ggids, pools.layout, starts)
+        for r, (t, g, bs) in enumerate(zip(gtoks, ggids, starts)):
+            w = tier.get(t, g, bs)
+            assert (int(got.num_transferred[r]), got.gpu_blocks[r].tolist(), got.cpu_blocks[r].tolist()) == \
+                (w.num_transferred, w.gpu_blocks.tolist(), w.cpu_blocks.tolist()), r
+            pools.expect_h2d(w.gpu_blocks, w.cpu_blocks)
+        assert pools.layers_match()
     ci.close()
 
 
