@@ -11,6 +11,9 @@
  *    byte of the layers with the original.
  * 2. Block hashes: gen_hashes over token ids 0..token_count-1 (int64) from
  *    host memory; prints the digests, one per line, for the caller to check.
+ * 3. CPU-tier cache index: put two 5-block sequences that share 3 blocks
+ *    (the second skips the shared prefix), match both, then get the first
+ *    into other GPU blocks and compare those bytes with its source blocks.
  * Exit status 0 on success; any failure prints fkv_last_error().
  */
 #include <cuda_runtime.h>
@@ -91,6 +94,72 @@ int main(int argc, char **argv) {
   CHECK(fkv_gen_hashes(h, tok, n_tok, tpb, hashes, nb, NULL));
   fkv_hasher_destroy(h);
   for (int64_t b = 0; b < nb; ++b) printf("%llu\n", (unsigned long long)hashes[b]);
+
+  /* CPU-tier cache index: put, match, get */
+  {
+    enum { TPB = 16, NB = 5 };
+    int64_t seq[2 * NB * TPB];
+    for (int i = 0; i < NB * TPB; ++i) seq[i] = 1000 + i;                       /* A */
+    for (int i = 0; i < NB * TPB; ++i) seq[NB * TPB + i] = i < 3 * TPB ? 1000 + i : 5000 + i; /* B */
+    const int64_t offs[3] = {0, NB * TPB, 2 * NB * TPB};
+    int64_t put_gpu[2 * NB], skipped[2], moved[2], cpu_of[2 * NB];
+    for (int i = 0; i < NB; ++i) { put_gpu[i] = i; put_gpu[NB + i] = 10 + i; }
+    fkv_transfer_desc d;
+    fkv_transfer_desc_init(&d);
+    d.num_layers = L;
+    d.gpu_layer_ptrs = (void *const *)layers;
+    d.cpu_ptr = pool;
+    d.gpu_kv_stride_in_bytes = NG * chunk;
+    d.gpu_block_stride_in_bytes = chunk;
+    d.cpu_kv_stride_in_bytes = NC * chunk;
+    d.cpu_layer_stride_in_bytes = KV * NC * chunk;
+    d.cpu_block_stride_in_bytes = chunk;
+    d.chunk_size_in_bytes = chunk;
+    d.cpu_pool_bytes = pool_bytes;
+    d.gpu_layer_bytes = layer_bytes;
+    fkv_cache_index *ci = NULL;
+    CHECK(fkv_cache_index_create(-1, NC, TPB, &ci));
+    d.is_host_to_device = 0;
+    CHECK(fkv_cache_index_put(ci, seq, offs, 2, put_gpu, &d, 1, skipped, moved, cpu_of, NULL, NULL));
+    if (skipped[0] != 0 || moved[0] != NB || skipped[1] != 3 || moved[1] != 2) {
+      fprintf(stderr, "put: skipped %lld/%lld moved %lld/%lld\n", (long long)skipped[0], (long long)skipped[1],
+              (long long)moved[0], (long long)moved[1]);
+      return 1;
+    }
+    int64_t matched[2], ready[2];
+    CHECK(fkv_cache_index_match(ci, seq, offs, 2, matched, ready, NULL, NULL));
+    if (matched[0] != NB || matched[1] != NB || ready[0] != NB || ready[1] != NB) {
+      fprintf(stderr, "match: %lld/%lld ready %lld/%lld\n", (long long)matched[0], (long long)matched[1],
+              (long long)ready[0], (long long)ready[1]);
+      return 1;
+    }
+    int64_t get_gpu[NB], got[1];
+    for (int i = 0; i < NB; ++i) get_gpu[i] = 20 + i;
+    d.is_host_to_device = 1;
+    CHECK(fkv_cache_index_get(ci, seq, offs, 1, NULL, get_gpu, &d, got, NULL, NULL));
+    if (got[0] != NB) {
+      fprintf(stderr, "get: %lld blocks\n", (long long)got[0]);
+      return 1;
+    }
+    for (int l = 0; l < L; ++l) {
+      CUDA(cudaMemcpy(back, layers[l], (size_t)layer_bytes, cudaMemcpyDeviceToHost));
+      for (int k = 0; k < KV; ++k)
+        for (int i = 0; i < NB; ++i)
+          if (memcmp(back + k * NG * chunk + (20 + i) * chunk, orig + l * layer_bytes + k * NG * chunk + i * chunk,
+                     (size_t)chunk) != 0) {
+            fprintf(stderr, "get: layer %d kv %d block %d differs\n", l, k, 20 + i);
+            return 1;
+          }
+    }
+    int64_t st[7];
+    CHECK(fkv_cache_index_stats(ci, st, NULL));
+    if (st[0] != NC - 7 || st[1] != 7 || st[2] != 7) {
+      fprintf(stderr, "stats: free %lld cached %lld ready %lld\n", (long long)st[0], (long long)st[1],
+              (long long)st[2]);
+      return 1;
+    }
+    fkv_cache_index_destroy(ci);
+  }
 
   for (int l = 0; l < L; ++l) cudaFree(layers[l]);
   cudaFreeHost(pool);

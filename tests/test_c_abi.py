@@ -1,8 +1,9 @@
 """The C ABI from C: tests/c_abi_demo.c is built with plain gcc against
 include/flexkv_b200.h and libflexkv_b200.so (no Python, no torch in the
 caller).  Building and linking is checked on the CPU; running it (a KV
-round trip through a page-locked pool and block hashes of a token range,
-checked against the oracle) needs a GPU."""
+round trip through a page-locked pool, block hashes of a token range
+checked against the oracle, and a put / match / get through the CPU-tier
+cache index, checked by the program itself) needs a GPU."""
 import os
 import shutil
 import subprocess
