@@ -768,6 +768,8 @@ int fkv_cache_index_put(fkv_cache_index *ci, const int64_t *token_ids, const int
   if (!token_ids || !gpu_block_ids) return fail(FKV_ERR_INVALID_ARG, "null token ids or gpu block ids");
   if (nb >= (1ll << 29)) return fail(FKV_ERR_INVALID_ARG, "too many blocks in one batch (limit 2^29)");
   if (layout->is_host_to_device) return fail(FKV_ERR_INVALID_ARG, "the put path copies device to host");
+  // The copy's layout is checked before any state changes.
+  if (int rc = transfer_check_device_ids(*layout, nb, ci->num_blocks - 1)) return rc;
 
   // GPU ids: on the host for the checks the copy kernel does not make.
   std::vector<int64_t> gids((size_t)nb);
@@ -897,6 +899,7 @@ int fkv_cache_index_get(fkv_cache_index *ci, const int64_t *token_ids, const int
   if (!token_ids || !gpu_block_ids) return fail(FKV_ERR_INVALID_ARG, "null token ids or gpu block ids");
   if (nb >= (1ll << 29)) return fail(FKV_ERR_INVALID_ARG, "too many blocks in one batch (limit 2^29)");
   if (!layout->is_host_to_device) return fail(FKV_ERR_INVALID_ARG, "the get path copies host to device");
+  if (int rc = transfer_check_device_ids(*layout, ng, ci->num_blocks - 1)) return rc;
   std::vector<int64_t> gids((size_t)ng);
   int gdev = 0, gd = -1;
   pointer_is_device(gpu_block_ids, &gdev, &gd);

@@ -81,6 +81,9 @@ size_t transfer_stage_bytes(const fkv_transfer_desc &d);
 int transfer_enqueue_device_ids(const fkv_transfer_desc &d, const int64_t *gpu_ids_dev,
                                 const int64_t *cpu_ids_dev, const int64_t *n_dev, int64_t n_max,
                                 int64_t max_cpu_id, cudaStream_t s);
+// The checks transfer_enqueue_device_ids makes before it launches, alone:
+// callers that change state before the copy run them first.
+int transfer_check_device_ids(const fkv_transfer_desc &d, int64_t n_max, int64_t max_cpu_id);
 
 // Classify a pointer: 1 = device memory (or managed), 0 = host.
 int pointer_is_device(const void *p, int *is_device, int *device);

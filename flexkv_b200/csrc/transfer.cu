@@ -666,20 +666,17 @@ int transfer_enqueue(const fkv_transfer_desc &d, cudaStream_t s, char *ext_stage
   return rc;
 }
 
-int transfer_enqueue_device_ids(const fkv_transfer_desc &d, const int64_t *gpu_ids_dev,
-                                const int64_t *cpu_ids_dev, const int64_t *n_dev, int64_t n_max,
-                                int64_t max_cpu_id, cudaStream_t s) {
+namespace {
+// The host-side checks of a device-id-list copy (see transfer_check_device_ids).
+int device_ids_plan(const fkv_transfer_desc &d, int64_t n_max, int64_t max_cpu_id, HostPlan &hp) {
   if (int rc = validate_desc(d)) return rc;
-  if (n_max <= 0 || d.num_layers == 0 || d.chunk_size_in_bytes < 16) return FKV_OK;
-  if (!d.gpu_layer_ptrs || !d.cpu_ptr || !gpu_ids_dev || !cpu_ids_dev || !n_dev)
-    return fail(FKV_ERR_INVALID_ARG, "null layer pointer table, cpu pointer or id list");
-  int device = 0;
-  if (int rc = current_device(&device)) return rc;
-  HostPlan hp;
   hp.h2d = d.is_host_to_device != 0;
   hp.kv_dim = d.is_mla ? 1 : 2;
   hp.num_layers = d.num_layers;
   hp.copy_bytes = (d.chunk_size_in_bytes / 16) * 16;
+  if (n_max <= 0 || d.num_layers == 0 || d.chunk_size_in_bytes < 16) return FKV_OK;
+  if (!d.gpu_layer_ptrs || !d.cpu_ptr)
+    return fail(FKV_ERR_INVALID_ARG, "null layer pointer table or cpu pointer");
   if (int rc = layout_checks(d, n_max, hp)) return rc;
   // Every id the lists can hold must be 16-byte aligned and, when the pool
   // sizes are given, inside them (the ids are produced on the device).
@@ -689,6 +686,25 @@ int transfer_enqueue_device_ids(const fkv_transfer_desc &d, const int64_t *gpu_i
   if (d.cpu_pool_bytes > 0 &&
       max_cpu_id * hp.cbs + hp.base_off + (L - 1) * hp.cls + (KV - 1) * hp.ckv + hp.copy_bytes > d.cpu_pool_bytes)
     return fail(FKV_ERR_OUT_OF_RANGE, "cpu block id " + std::to_string(max_cpu_id) + " addresses past the cpu pool");
+  return FKV_OK;
+}
+}  // namespace
+
+int transfer_check_device_ids(const fkv_transfer_desc &d, int64_t n_max, int64_t max_cpu_id) {
+  HostPlan hp;
+  return device_ids_plan(d, n_max, max_cpu_id, hp);
+}
+
+int transfer_enqueue_device_ids(const fkv_transfer_desc &d, const int64_t *gpu_ids_dev,
+                                const int64_t *cpu_ids_dev, const int64_t *n_dev, int64_t n_max,
+                                int64_t max_cpu_id, cudaStream_t s) {
+  HostPlan hp;
+  if (int rc = device_ids_plan(d, n_max, max_cpu_id, hp)) return rc;
+  if (n_max <= 0 || d.num_layers == 0 || d.chunk_size_in_bytes < 16) return FKV_OK;
+  if (!gpu_ids_dev || !cpu_ids_dev || !n_dev) return fail(FKV_ERR_INVALID_ARG, "null id list");
+  int device = 0;
+  if (int rc = current_device(&device)) return rc;
+  const int64_t L = d.num_layers, KV = hp.kv_dim;
   ThreadDeviceCtx *ctx = nullptr;
   if (int rc = get_ctx(device, &ctx)) return rc;
   const void *k = hp.h2d ? (const void *)kv_copy_devn_kernel<true> : (const void *)kv_copy_devn_kernel<false>;

@@ -321,6 +321,19 @@ def test_errors_leave_the_index_unchanged():
     assert e.value.code == FKV_ERR_OUT_OF_RANGE
     with pytest.raises(ValueError):
         ci.put([tok], [np.arange(4)], pools.layout)  # one GPU block per full block
+    # layouts the copy cannot use are refused before anything changes
+    import dataclasses
+    pageable = dataclasses.replace(pools.layout, cpu_tensor=torch.zeros_like(pools.cpu, device="cpu").clone())
+    with pytest.raises(FlexKVError) as e:
+        ci.put([np.arange(200, 200 + 3 * tpb, dtype=np.int64)], [np.arange(3)], pageable)
+    assert e.value.code == FKV_ERR_INVALID_ARG
+    small = dataclasses.replace(pools.layout, cpu_tensor=pools.cpu[: pools.cpu.numel() // 2])
+    with pytest.raises(FlexKVError) as e:  # the index hands out ids the half pool does not hold
+        ci.put([np.arange(300, 300 + 3 * tpb, dtype=np.int64)], [np.arange(3)], small)
+    assert e.value.code == FKV_ERR_OUT_OF_RANGE
+    with pytest.raises(FlexKVError) as e:
+        ci.get([tok], [np.arange(5)], small)
+    assert e.value.code == FKV_ERR_OUT_OF_RANGE
     assert ci.stats() == before
     assert ci.match([tok]).num_matched.tolist() == [5]
     ci.close()
