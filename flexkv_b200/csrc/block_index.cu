@@ -199,8 +199,10 @@ __device__ int64_t rebuild_free_ids(const uint8_t *mask, int64_t mask_bytes, int
 __global__ void __launch_bounds__(32) put_decide_kernel(
     int num_req, const int64_t *blk_off, const uint8_t *before, const int32_t *lslot, int32_t *ins_req,
     const int64_t *gpu_ids, uint8_t *free_mask, int64_t mask_bytes, int64_t *free_ids, int64_t *state,
-    int64_t *res, int64_t *cpu_out, int64_t *d2h_gpu, int64_t *d2h_cpu, int64_t *new_blk, int64_t *count) {
+    int64_t *res, int64_t *cpu_out, int64_t *d2h_gpu, int64_t *d2h_cpu, int64_t *new_blk, int64_t *count,
+    const int64_t *done) {
   const int lane = threadIdx.x;
+  if (*done) return;  // put_decide_fast_kernel decided the batch
   if (state[kErr] != kErrNone) {  // an earlier step failed: change nothing
     if (lane == 0) *count = 0;
     return;
@@ -263,6 +265,95 @@ __global__ void __launch_bounds__(32) put_decide_kernel(
     state[kListLen] = list_len;
     state[kOffset] = offset;
     *count = cnt;
+  }
+}
+
+// The same decisions in parallel, for the common case: when the batch's
+// new blocks all fit both the free count and what is left of the pool's id
+// snapshot, no request comes back empty and no snapshot refresh happens, so
+// a block is present for request r exactly when the index held it before
+// the call or an earlier request of the batch holds it (first_req, the
+// smallest request index per distinct hash), and ids are taken from the
+// snapshot in request order (a prefix sum of the counts).  One CTA; each
+// thread a contiguous run of requests.  Sets *done = 1 when it decided;
+// otherwise it changes nothing but res and first_req, and the one-warp walk
+// decides.
+constexpr int kDecideThreads = 1024;
+__global__ void __launch_bounds__(kDecideThreads) put_decide_fast_kernel(
+    int num_req, const int64_t *blk_off, const uint8_t *before, const int32_t *lslot, int32_t *first_req,
+    const int64_t *gpu_ids, uint8_t *free_mask, const int64_t *free_ids, int64_t *state, int64_t *res,
+    int64_t *cpu_out, int64_t *d2h_gpu, int64_t *d2h_cpu, int64_t *new_blk, int64_t *count, int64_t *done) {
+  __shared__ int64_t sums[kDecideThreads];
+  const int t = threadIdx.x;
+  if (state[kErr] != kErrNone) {  // an earlier step failed: change nothing
+    if (t == 0) {
+      *count = 0;
+      *done = 1;
+    }
+    return;
+  }
+  const int per = (num_req + kDecideThreads - 1) / kDecideThreads;
+  const int r0 = min(num_req, t * per), r1 = min(num_req, r0 + per);
+  for (int r = r0; r < r1; ++r)
+    for (int64_t i = blk_off[r]; i < blk_off[r + 1]; ++i) {
+      const int32_t sl = lslot[i];
+      if (sl >= 0) atomicMin(first_req + sl, r);
+    }
+  __syncthreads();
+  int64_t mine = 0;
+  for (int r = r0; r < r1; ++r) {
+    const int64_t o = blk_off[r], n = blk_off[r + 1] - o;
+    int64_t m = n;
+    for (int64_t j = 0; j < n; ++j) {
+      const int32_t sl = lslot[o + j];
+      if (!(before[o + j] || (sl >= 0 && first_req[sl] < r))) {
+        m = j;
+        break;
+      }
+    }
+    res[3 * (int64_t)r] = m;
+    res[3 * (int64_t)r + 1] = n - m;
+    mine += n - m;
+  }
+  sums[t] = mine;
+  __syncthreads();
+  for (int d = 1; d < kDecideThreads; d <<= 1) {  // inclusive scan (Hillis-Steele)
+    const int64_t add = t >= d ? sums[t - d] : 0;
+    __syncthreads();
+    sums[t] += add;
+    __syncthreads();
+  }
+  const int64_t total = sums[kDecideThreads - 1];
+  const int64_t num_free = state[kNumFree], list_len = state[kListLen], offset = state[kOffset];
+  if (total > num_free || total > list_len - offset) {  // the walk decides
+    if (t == 0) *done = 0;
+    return;
+  }
+  int64_t at = sums[t] - mine;
+  for (int r = r0; r < r1; ++r) {
+    const int64_t o = blk_off[r], m = res[3 * (int64_t)r], k = res[3 * (int64_t)r + 1];
+    if (k == 0) {
+      res[3 * (int64_t)r] = 0;
+      res[3 * (int64_t)r + 2] = kPutEmpty;
+      continue;
+    }
+    for (int64_t q = 0; q < k; ++q) {
+      const int64_t i = o + m + q, c = free_ids[offset + at + q];
+      free_mask[c] = 0;
+      cpu_out[i] = c;
+      d2h_gpu[at + q] = gpu_ids[i];
+      d2h_cpu[at + q] = c;
+      new_blk[at + q] = i;
+    }
+    res[3 * (int64_t)r + 2] = kPutDone;
+    at += k;
+  }
+  __syncthreads();
+  if (t == 0) {
+    state[kNumFree] = num_free - total;
+    state[kOffset] = offset + total;
+    *count = total;
+    *done = 1;
   }
 }
 
@@ -334,34 +425,51 @@ __global__ void match_kernel(Table t, const uint64_t *hashes, const int64_t *blk
   }
 }
 
-// The get decisions (cache_engine.py:412-548, CPU tier), one warp, after
+// The get decisions (cache_engine.py:412-548, CPU tier), after
 // match_kernel: request r reads physical_blocks[:num_ready][start_r:n_r]
 // (the reference takes the first num_ready matched blocks) into its leading
-// GPU blocks.  Gets change neither the index nor the pool, so the order only
-// fixes the list layout.
-__global__ void __launch_bounds__(32) get_lists_kernel(int num_req, const int64_t *blk_off, const int64_t *starts,
-                                                       const int64_t *goff, const int64_t *match_res,
-                                                       const int64_t *phys, const int64_t *gpu_ids, int64_t *h2d_gpu,
-                                                       int64_t *h2d_cpu, int64_t *cpu_out, int64_t *moved,
-                                                       int64_t *count) {
-  const int lane = threadIdx.x;
-  int64_t cnt = 0;
-  for (int r = 0; r < num_req; ++r) {
+// GPU blocks.  Gets change neither the index nor the pool, so requests are
+// independent: one CTA of kGetThreads threads, each thread a contiguous
+// run of requests; the per-thread block counts are scanned in shared
+// memory to place every request's entries in the copy lists.
+constexpr int kGetThreads = 1024;
+__global__ void __launch_bounds__(kGetThreads) get_lists_kernel(
+    int num_req, const int64_t *blk_off, const int64_t *starts, const int64_t *goff, const int64_t *match_res,
+    const int64_t *phys, const int64_t *gpu_ids, int64_t *h2d_gpu, int64_t *h2d_cpu, int64_t *cpu_out,
+    int64_t *moved, int64_t *count) {
+  __shared__ int64_t sums[kGetThreads];
+  const int t = threadIdx.x;
+  const int per = (num_req + kGetThreads - 1) / kGetThreads;
+  const int r0 = t * per, r1 = min(num_req, r0 + per);
+  int64_t mine = 0;
+  for (int r = r0; r < r1; ++r) {
     const int64_t o = blk_off[r], n = blk_off[r + 1] - o, bs = starts[r];
     const int64_t ready = match_res[2 * (int64_t)r + 1];
     int64_t f = (ready < n ? ready : n) - bs;
     if (f < 0 || n == 0) f = 0;
-    const int64_t go = goff[r];
-    for (int64_t t = lane; t < f; t += 32) {
-      const int64_t c = phys[o + bs + t];
-      h2d_gpu[cnt + t] = gpu_ids[go + t];
-      h2d_cpu[cnt + t] = c;
-      cpu_out[go + t] = c;
-    }
-    if (lane == 0) moved[r] = f;
-    cnt += f;
+    moved[r] = f;
+    mine += f;
   }
-  if (lane == 0) *count = cnt;
+  sums[t] = mine;
+  __syncthreads();
+  for (int d = 1; d < kGetThreads; d <<= 1) {  // inclusive scan (Hillis-Steele)
+    const int64_t add = t >= d ? sums[t - d] : 0;
+    __syncthreads();
+    sums[t] += add;
+    __syncthreads();
+  }
+  int64_t at = sums[t] - mine;  // exclusive prefix
+  for (int r = r0; r < r1; ++r) {
+    const int64_t o = blk_off[r], bs = starts[r], f = moved[r], go = goff[r];
+    for (int64_t q = 0; q < f; ++q) {
+      const int64_t c = phys[o + bs + q];
+      h2d_gpu[at + q] = gpu_ids[go + q];
+      h2d_cpu[at + q] = c;
+      cpu_out[go + q] = c;
+    }
+    at += f;
+  }
+  if (t == kGetThreads - 1) *count = sums[t];
 }
 
 // Flag changes by hash (set_ready for a batch of blocks): ready or not.
@@ -798,7 +906,7 @@ int fkv_cache_index_put(fkv_cache_index *ci, const int64_t *token_ids, const int
                o_lkeys = carve(8 * lslots), o_ins = carve(4 * lslots), o_off = carve(8 * (num_seqs + 1)),
                o_gid = carve(8 * nb), o_res = carve(24 * (size_t)num_seqs), o_cpu = carve(8 * nb),
                o_d2hg = carve(8 * nb), o_d2hc = carve(8 * nb), o_new = carve(8 * nb), o_slot = carve(8 * nb),
-               o_cnt = carve(16);
+               o_cnt = carve(16), o_first = carve(4 * lslots);
   Scratch sc, tok;
   sc.s = s;
   if (int rc = scratch_alloc(ci->device, off, s, (void **)&sc.base)) return rc;
@@ -817,14 +925,23 @@ int fkv_cache_index_put(fkv_cache_index *ci, const int64_t *token_ids, const int
   FKV_CUDA(cudaMemcpyAsync(b + o_gid, ci->pin + up_off, 8 * nb, cudaMemcpyHostToDevice, s));
   FKV_CUDA(cudaMemsetAsync(b + o_lkeys, 0xff, 8 * lslots, s));
   FKV_CUDA(cudaMemsetAsync(b + o_ins, 0x7f, 4 * lslots, s));  // 0x7f7f7f7f: after every request
+  FKV_CUDA(cudaMemsetAsync(b + o_first, 0x7f, 4 * lslots, s));
   FKV_CUDA(cudaMemsetAsync(b + o_cpu, 0xff, 8 * nb, s));      // -1: not moved
-  FKV_CUDA(cudaMemsetAsync(d_cnt, 0, 16, s));
+  FKV_CUDA(cudaMemsetAsync(d_cnt, 0, 16, s));  // d_cnt[0] = count, d_cnt[1] = decided by the parallel kernel
 
   const Table t = ci->table();
   put_lookup_kernel<<<grid_for(nb), 256, 0, s>>>(t, hashes, nb, reinterpret_cast<uint8_t *>(b + o_before),
                                                   reinterpret_cast<uint64_t *>(b + o_lkeys), lslots - 1,
                                                   64 - log2u(lslots), reinterpret_cast<int32_t *>(b + o_lslot),
                                                   ci->state);
+  FKV_CUDA(cudaGetLastError());
+  put_decide_fast_kernel<<<1, kDecideThreads, 0, s>>>(
+      num_seqs, reinterpret_cast<int64_t *>(b + o_off), reinterpret_cast<uint8_t *>(b + o_before),
+      reinterpret_cast<int32_t *>(b + o_lslot), reinterpret_cast<int32_t *>(b + o_first),
+      reinterpret_cast<int64_t *>(b + o_gid), ci->free_mask, ci->free_ids, ci->state,
+      reinterpret_cast<int64_t *>(b + o_res), reinterpret_cast<int64_t *>(b + o_cpu),
+      reinterpret_cast<int64_t *>(b + o_d2hg), reinterpret_cast<int64_t *>(b + o_d2hc),
+      reinterpret_cast<int64_t *>(b + o_new), d_cnt, d_cnt + 1);
   FKV_CUDA(cudaGetLastError());
   put_decide_kernel<<<1, 32, 0, s>>>(num_seqs, reinterpret_cast<int64_t *>(b + o_off),
                                      reinterpret_cast<uint8_t *>(b + o_before),
@@ -833,13 +950,13 @@ int fkv_cache_index_put(fkv_cache_index *ci, const int64_t *token_ids, const int
                                      ci->free_ids, ci->state, reinterpret_cast<int64_t *>(b + o_res),
                                      reinterpret_cast<int64_t *>(b + o_cpu), reinterpret_cast<int64_t *>(b + o_d2hg),
                                      reinterpret_cast<int64_t *>(b + o_d2hc), reinterpret_cast<int64_t *>(b + o_new),
-                                     d_cnt);
+                                     d_cnt, d_cnt + 1);
   FKV_CUDA(cudaGetLastError());
   put_insert_kernel<<<grid_for(nb), 256, 0, s>>>(t, hashes, reinterpret_cast<int64_t *>(b + o_new),
                                                   reinterpret_cast<int64_t *>(b + o_cpu), d_cnt,
                                                   reinterpret_cast<int64_t *>(b + o_slot), ci->state);
   FKV_CUDA(cudaGetLastError());
-  note_launch(3);
+  note_launch(4);
   fkv_transfer_desc d = *layout;
   d.is_host_to_device = 0;
   if (int rc = transfer_enqueue_device_ids(d, reinterpret_cast<int64_t *>(b + o_d2hg),
@@ -949,7 +1066,7 @@ int fkv_cache_index_get(fkv_cache_index *ci, const int64_t *token_ids, const int
   int64_t *d_phys = reinterpret_cast<int64_t *>(b + o_phys);
   match_kernel<<<grid_for(32ll * num_seqs), 256, 0, s>>>(ci->table(), hashes, d_off, num_seqs, d_res, d_phys);
   FKV_CUDA(cudaGetLastError());
-  get_lists_kernel<<<1, 32, 0, s>>>(num_seqs, d_off, reinterpret_cast<int64_t *>(b + o_start),
+  get_lists_kernel<<<1, kGetThreads, 0, s>>>(num_seqs, d_off, reinterpret_cast<int64_t *>(b + o_start),
                                     reinterpret_cast<int64_t *>(b + o_goff), d_res, d_phys,
                                     reinterpret_cast<int64_t *>(b + o_gid), reinterpret_cast<int64_t *>(b + o_h2dg),
                                     reinterpret_cast<int64_t *>(b + o_h2dc), reinterpret_cast<int64_t *>(b + o_cpu),
