@@ -337,3 +337,41 @@ def test_errors_leave_the_index_unchanged():
     assert ci.stats() == before
     assert ci.match([tok]).num_matched.tolist() == [5]
     ci.close()
+
+
+def test_edge_batches_match_the_oracle():
+    """Identical requests in one batch (the second is fully cached by the
+    first), a 3000-block sequence beside short ones, requests with no full
+    block, and gets that read only the last block."""
+    tpb = 16
+    rng = np.random.default_rng(41)
+    pools = Pools(Case("edge", 2, 1, 64, tpb, 4096, 4096), seed=53)
+    tier = CI.CpuTier(4096, tpb)
+    ci = CpuCacheIndex(4096, tpb)
+    a = rng.integers(0, 5000, 7 * tpb).astype(np.int64)
+    long_seq = rng.integers(0, 5000, 3000 * tpb + 5).astype(np.int64)
+    toks = [a, a.copy(), np.zeros(0, np.int64), long_seq, rng.integers(0, 5000, tpb - 1).astype(np.int64),
+            np.concatenate([a[:3 * tpb], rng.integers(0, 5000, 2 * tpb)]).astype(np.int64)]
+    perm = rng.permutation(4096).astype(np.int64)
+    cuts = np.cumsum([0] + [len(t) // tpb for t in toks])
+    gids = [perm[cuts[i]:cuts[i + 1]] for i in range(len(toks))]
+    res = ci.put(toks, gids, pools.layout)
+    for r, (t, g) in enumerate(zip(toks, gids)):
+        w = tier.put(t, g)
+        tier.complete(w)
+        assert (int(res.num_skipped[r]), int(res.num_transferred[r]), res.cpu_blocks[r].tolist()) == \
+            (w.num_skipped, w.num_transferred, w.cpu_blocks.tolist()), r
+        pools.expect_d2h(w.gpu_blocks, w.cpu_blocks)
+    assert res.num_transferred.tolist()[:3] == [7, 0, 0]
+    assert pools.pool_matches()
+    gt = [a, long_seq, toks[5]]
+    starts = [len(t) // tpb - 1 for t in gt]
+    dst = [np.array([4095 - i], dtype=np.int64) for i in range(len(gt))]
+    got = ci.get(gt, dst, pools.layout, starts)
+    for r, (t, g, bs) in enumerate(zip(gt, dst, starts)):
+        w = tier.get(t, g, bs)
+        assert (int(got.num_transferred[r]), got.cpu_blocks[r].tolist()) == (w.num_transferred, w.cpu_blocks.tolist())
+        pools.expect_h2d(w.gpu_blocks, w.cpu_blocks)
+    assert got.num_transferred.tolist() == [1, 1, 1]
+    assert pools.layers_match()
+    ci.close()
