@@ -233,14 +233,16 @@ class CpuCacheIndex:
         return MatchBatch(nm, nr, phys[:nb], blk)
 
     def put(self, token_ids: Sequence, gpu_block_ids: Sequence, layout: KVLayout,
-            mark_ready: bool = True) -> PutBatch:
+            mark_ready: bool = True, synchronous: bool = True) -> PutBatch:
         """Puts of the CPU tier for a batch of requests, in order
         (cache_engine.py:787-902): request r's full blocks are hashed, its
         cached prefix is skipped, pool blocks are taken for the rest, which
         are inserted (not ready), copied from the GPU blocks
         gpu_block_ids[r] (one per full block) and, with mark_ready, marked
         ready once the copy is done (the put callback).  Returns when the
-        copies are complete."""
+        copies are complete, or with synchronous=False as soon as the
+        decisions are known, the copies still running on the current
+        stream (wait on it before reusing the blocks)."""
         if len(token_ids) != len(gpu_block_ids):
             raise ValueError("one gpu block list per request")
         buf, offsets, ptr = _pack_tokens(token_ids)
@@ -253,10 +255,10 @@ class CpuCacheIndex:
         parts = [np.asarray(g.cpu() if isinstance(g, torch.Tensor) else g, dtype=np.int64).reshape(-1)
                  for g in gpu_block_ids]
         gids = np.concatenate(parts) if parts else np.zeros(0, dtype=np.int64)
-        return self.put_packed(ptr, offsets, gids, layout, mark_ready)
+        return self.put_packed(ptr, offsets, gids, layout, mark_ready, synchronous)
 
     def put_packed(self, token_ptr: int, seq_offsets: np.ndarray, gpu_block_ids: np.ndarray,
-                   layout: KVLayout, mark_ready: bool = True) -> PutBatch:
+                   layout: KVLayout, mark_ready: bool = True, synchronous: bool = True) -> PutBatch:
         """put over a packed batch: token_ptr addresses the int64 tokens of
         all sequences (host or device), seq_offsets (R+1, host) delimits
         them, gpu_block_ids holds one GPU block per full block of the batch,
@@ -276,29 +278,31 @@ class CpuCacheIndex:
         hashes = np.empty(max(nb, 1), dtype=np.uint64)
         d = layout.desc()
         check(_lib.load().fkv_cache_index_put(self._h, token_ptr, offsets.ctypes.data, R, gids.ctypes.data,
-                                              ctypes.byref(d), int(bool(mark_ready)), nsk.ctypes.data,
+                                              ctypes.byref(d), int(bool(mark_ready)), int(bool(synchronous)),
+                                              nsk.ctypes.data,
                                               ntr.ctypes.data, cpu.ctypes.data, hashes.ctypes.data,
                                               self._stream()),
               "CpuCacheIndex.put")
         return PutBatch(nsk, ntr, cpu[:nb], gids[:nb], hashes[:nb], blk)
 
     def get(self, token_ids: Sequence, gpu_block_ids: Sequence, layout: KVLayout,
-            block_starts: Optional[Sequence[int]] = None) -> GetBatch:
+            block_starts: Optional[Sequence[int]] = None, synchronous: bool = True) -> GetBatch:
         """Gets of the CPU tier for a batch of requests (cache_engine.py:
         412-548, SSD off): request r selects its full blocks from
         block_starts[r] (default 0) on and brings one GPU block per selected
         block; its ready cached blocks in that range are read into the
-        leading GPU blocks.  Returns when the copies are complete."""
+        leading GPU blocks.  Returns when the copies are complete (or, with
+        synchronous=False, once the decisions are known)."""
         if len(token_ids) != len(gpu_block_ids):
             raise ValueError("one gpu block list per request")
         buf, offsets, ptr = _pack_tokens(token_ids)
         parts = [np.asarray(g.cpu() if isinstance(g, torch.Tensor) else g, dtype=np.int64).reshape(-1)
                  for g in gpu_block_ids]
         gids = np.concatenate(parts) if parts else np.zeros(0, dtype=np.int64)
-        return self.get_packed(ptr, offsets, gids, layout, block_starts)
+        return self.get_packed(ptr, offsets, gids, layout, block_starts, synchronous)
 
     def get_packed(self, token_ptr: int, seq_offsets: np.ndarray, gpu_block_ids: np.ndarray, layout: KVLayout,
-                   block_starts: Optional[Sequence[int]] = None) -> GetBatch:
+                   block_starts: Optional[Sequence[int]] = None, synchronous: bool = True) -> GetBatch:
         """get over a packed batch (as put_packed; gpu_block_ids holds
         n_r - block_starts[r] GPU blocks per request)."""
         offsets = np.ascontiguousarray(seq_offsets, dtype=np.int64)
@@ -322,13 +326,14 @@ class CpuCacheIndex:
         cpu = np.full(max(ng, 1), -1, dtype=np.int64)
         d = layout.desc(host_to_device=True)
         check(_lib.load().fkv_cache_index_get(self._h, token_ptr, offsets.ctypes.data, R, starts.ctypes.data,
-                                              gbuf.ctypes.data, ctypes.byref(d), moved.ctypes.data,
+                                              gbuf.ctypes.data, ctypes.byref(d), int(bool(synchronous)),
+                                              moved.ctypes.data,
                                               cpu.ctypes.data, self._stream()),
               "CpuCacheIndex.get")
         return GetBatch(starts, moved, cpu[:ng], gids, goff)
 
     def get_requests(self, requests: Sequence[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]],
-                     layout: KVLayout) -> Tuple[List[torch.Tensor], GetBatch]:
+                     layout: KVLayout, synchronous: bool = True) -> Tuple[List[torch.Tensor], GetBatch]:
         """``GlobalCacheEngine.get(request_id, token_ids, token_mask,
         slot_mapping)`` for a batch (cache_engine.py:150-219, CPU tier):
         the mask selects a suffix of the full blocks that ends at the last
@@ -354,11 +359,12 @@ class CpuCacheIndex:
             toks.append(token_ids[:aligned].to(torch.int64).numpy())
             starts.append(bs)
             gids.append((slot_mapping[::tpb][:be - bs] // tpb).cpu().numpy().astype(np.int64))
-        res = self.get(toks, gids, layout, starts)
+        res = self.get(toks, gids, layout, starts, synchronous)
         return [res.return_mask(r, lens[r], tpb) for r in range(len(lens))], res
 
     def put_requests(self, requests: Sequence[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]],
-                     layout: KVLayout, mark_ready: bool = True) -> Tuple[List[torch.Tensor], PutBatch]:
+                     layout: KVLayout, mark_ready: bool = True,
+                     synchronous: bool = True) -> Tuple[List[torch.Tensor], PutBatch]:
         """``GlobalCacheEngine.put(request_id, token_ids, token_mask,
         slot_mapping)`` for a batch (cache_engine.py:550-615, CPU tier):
         tokens past the last full block are ignored, the mask must select a
@@ -391,7 +397,7 @@ class CpuCacheIndex:
                 continue
             toks.append(token_ids[:aligned].to(torch.int64))
             gids.append((slot_mapping[::tpb][:nfull] // tpb).cpu().numpy().astype(np.int64))
-        res = self.put(toks, gids, layout, mark_ready=mark_ready)
+        res = self.put(toks, gids, layout, mark_ready=mark_ready, synchronous=synchronous)
         masks = [res.return_mask(r, lens[r], tpb) for r in range(len(lens))]
         return masks, res
 

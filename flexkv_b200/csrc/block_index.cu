@@ -621,6 +621,7 @@ struct fkv_cache_index {
   int64_t *state = nullptr;      // device [kStateWords]
   char *pin = nullptr;           // page-locked bounce for uploads and results
   size_t pin_cap = 0;
+  cudaEvent_t decided = nullptr; // after a put's / get's results reached the bounce
   std::mutex mu;
 
   Table table() const {
@@ -776,6 +777,7 @@ int fkv_cache_index_create(int device, int64_t num_total_blocks, int tokens_per_
   if (e == cudaSuccess) e = cudaMalloc(&ci->free_mask, ci->mask_bytes);
   if (e == cudaSuccess) e = cudaMalloc(&ci->free_ids, 8 * num_total_blocks);
   if (e == cudaSuccess) e = cudaMalloc(&ci->state, 8 * kStateWords);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ci->decided, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaMemset(ci->keys, 0xff, 8 * ci->slots);
   if (e == cudaSuccess) e = cudaMemset(ci->flags, 0, 4 * ci->slots);
   if (e == cudaSuccess) {
@@ -803,6 +805,7 @@ void fkv_cache_index_destroy(fkv_cache_index *ci) {
     cudaFree(ci->free_mask);
     cudaFree(ci->free_ids);
     cudaFree(ci->state);
+    if (ci->decided) cudaEventDestroy(ci->decided);
     if (ci->pin) cudaFreeHost(ci->pin);
   }
   delete ci;
@@ -858,8 +861,8 @@ int fkv_cache_index_match(fkv_cache_index *ci, const int64_t *token_ids, const i
 
 int fkv_cache_index_put(fkv_cache_index *ci, const int64_t *token_ids, const int64_t *seq_offsets, int num_seqs,
                         const int64_t *gpu_block_ids, const fkv_transfer_desc *layout, int mark_ready,
-                        int64_t *num_skipped, int64_t *num_transferred, int64_t *cpu_block_ids,
-                        uint64_t *block_hashes, void *stream) {
+                        int synchronous, int64_t *num_skipped, int64_t *num_transferred,
+                        int64_t *cpu_block_ids, uint64_t *block_hashes, void *stream) {
   clear_error();
   if (!ci || !layout) return fail(FKV_ERR_INVALID_ARG, "null index or layout");
   if (num_seqs < 0 || (num_seqs > 0 && (!seq_offsets || !num_skipped || !num_transferred)))
@@ -957,6 +960,14 @@ int fkv_cache_index_put(fkv_cache_index *ci, const int64_t *token_ids, const int
                                                   reinterpret_cast<int64_t *>(b + o_slot), ci->state);
   FKV_CUDA(cudaGetLastError());
   note_launch(4);
+  // The decisions go back before the copy, so an asynchronous caller gets
+  // them as soon as they exist (the reference's put returns its graph and
+  // mask before the transfer runs).
+  FKV_CUDA(cudaMemcpyAsync(ci->pin, b + o_res, down_res, cudaMemcpyDeviceToHost, s));
+  FKV_CUDA(cudaMemcpyAsync(ci->pin + down_res, b + o_cpu, 8 * nb, cudaMemcpyDeviceToHost, s));
+  FKV_CUDA(cudaMemcpyAsync(ci->pin + down_res + 8 * nb, hashes, 8 * nb, cudaMemcpyDeviceToHost, s));
+  FKV_CUDA(cudaMemcpyAsync(ci->pin + down_res + 16 * nb, ci->state, 8 * kStateWords, cudaMemcpyDeviceToHost, s));
+  FKV_CUDA(cudaEventRecord(ci->decided, s));
   fkv_transfer_desc d = *layout;
   d.is_host_to_device = 0;
   if (int rc = transfer_enqueue_device_ids(d, reinterpret_cast<int64_t *>(b + o_d2hg),
@@ -968,11 +979,8 @@ int fkv_cache_index_put(fkv_cache_index *ci, const int64_t *token_ids, const int
     FKV_CUDA(cudaGetLastError());
     note_launch();
   }
-  FKV_CUDA(cudaMemcpyAsync(ci->pin, b + o_res, down_res, cudaMemcpyDeviceToHost, s));
-  FKV_CUDA(cudaMemcpyAsync(ci->pin + down_res, b + o_cpu, 8 * nb, cudaMemcpyDeviceToHost, s));
-  FKV_CUDA(cudaMemcpyAsync(ci->pin + down_res + 8 * nb, hashes, 8 * nb, cudaMemcpyDeviceToHost, s));
-  FKV_CUDA(cudaMemcpyAsync(ci->pin + down_res + 16 * nb, ci->state, 8 * kStateWords, cudaMemcpyDeviceToHost, s));
-  FKV_CUDA(cudaStreamSynchronize(s));
+  if (synchronous) FKV_CUDA(cudaStreamSynchronize(s));
+  else FKV_CUDA(cudaEventSynchronize(ci->decided));
   int64_t st[kStateWords];
   std::memcpy(st, ci->pin + down_res + 16 * nb, 8 * kStateWords);
   if (int rc = take_device_error(ci, s, st)) return rc;
@@ -988,7 +996,7 @@ int fkv_cache_index_put(fkv_cache_index *ci, const int64_t *token_ids, const int
 
 int fkv_cache_index_get(fkv_cache_index *ci, const int64_t *token_ids, const int64_t *seq_offsets, int num_seqs,
                         const int64_t *block_starts, const int64_t *gpu_block_ids, const fkv_transfer_desc *layout,
-                        int64_t *num_transferred, int64_t *cpu_block_ids, void *stream) {
+                        int synchronous, int64_t *num_transferred, int64_t *cpu_block_ids, void *stream) {
   clear_error();
   if (!ci || !layout) return fail(FKV_ERR_INVALID_ARG, "null index or layout");
   if (num_seqs < 0 || (num_seqs > 0 && (!seq_offsets || !num_transferred)))
@@ -1073,6 +1081,9 @@ int fkv_cache_index_get(fkv_cache_index *ci, const int64_t *token_ids, const int
                                     reinterpret_cast<int64_t *>(b + o_moved), d_cnt);
   FKV_CUDA(cudaGetLastError());
   note_launch(2);
+  FKV_CUDA(cudaMemcpyAsync(pin, b + o_moved, 8 * num_seqs, cudaMemcpyDeviceToHost, s));
+  if (ng) FKV_CUDA(cudaMemcpyAsync(pin + num_seqs, b + o_cpu, 8 * ng, cudaMemcpyDeviceToHost, s));
+  FKV_CUDA(cudaEventRecord(ci->decided, s));
   fkv_transfer_desc d = *layout;
   d.is_host_to_device = 1;
   if (ng > 0)
@@ -1080,9 +1091,8 @@ int fkv_cache_index_get(fkv_cache_index *ci, const int64_t *token_ids, const int
                                              reinterpret_cast<int64_t *>(b + o_h2dc), d_cnt, ng,
                                              ci->num_blocks - 1, s))
       return rc;
-  FKV_CUDA(cudaMemcpyAsync(pin, b + o_moved, 8 * num_seqs, cudaMemcpyDeviceToHost, s));
-  if (ng) FKV_CUDA(cudaMemcpyAsync(pin + num_seqs, b + o_cpu, 8 * ng, cudaMemcpyDeviceToHost, s));
-  FKV_CUDA(cudaStreamSynchronize(s));
+  if (synchronous) FKV_CUDA(cudaStreamSynchronize(s));
+  else FKV_CUDA(cudaEventSynchronize(ci->decided));
   std::memcpy(num_transferred, pin, 8 * num_seqs);
   if (cpu_block_ids && ng) std::memcpy(cpu_block_ids, pin + num_seqs, 8 * ng);
   return FKV_OK;

@@ -440,7 +440,12 @@ int fkv_ssd_last_stats(const fkv_ssd_ctx *ctx, int64_t *num_ios, int64_t *bytes)
  * seq_offsets on the host) and floor(len_s / tokens_per_block) blocks at
  * block offset blk_s (running sum of the previous sequences' blocks).  The
  * requests of a batch take effect in order, as consecutive puts do.  Every
- * call is synchronous on `stream` when it returns.
+ * call returns with its work done on `stream`, except the copies of a put
+ * or get called with synchronous = 0: those return once the decisions (the
+ * outputs) are known, with the copy -- and the put's ready marks -- still
+ * running on `stream`, as the reference's put/get return before their
+ * transfer graphs run.  The caller then waits on `stream` (an event recorded
+ * after the call) before it reuses the copied GPU blocks or pool blocks.
  *
  * Not done on the device: eviction.  When the pool is short a put comes back
  * empty, as the reference's does when take() finds nothing evictable; the
@@ -474,8 +479,9 @@ int fkv_cache_index_match(fkv_cache_index *ci, const int64_t *token_ids, const i
  * (optional, per block). */
 int fkv_cache_index_put(fkv_cache_index *ci, const int64_t *token_ids, const int64_t *seq_offsets,
                         int num_seqs, const int64_t *gpu_block_ids, const fkv_transfer_desc *layout,
-                        int mark_ready, int64_t *num_skipped, int64_t *num_transferred,
-                        int64_t *cpu_block_ids, uint64_t *block_hashes, void *stream);
+                        int mark_ready, int synchronous, int64_t *num_skipped,
+                        int64_t *num_transferred, int64_t *cpu_block_ids, uint64_t *block_hashes,
+                        void *stream);
 
 /* get of each sequence (CPU tier, cache_engine.py:150-219, 412-548, SSD
  * off): the mask selects full blocks [block_starts[s], n_s) (block_starts
@@ -489,7 +495,7 @@ int fkv_cache_index_put(fkv_cache_index *ci, const int64_t *token_ids, const int
  * The index and the pool do not change. */
 int fkv_cache_index_get(fkv_cache_index *ci, const int64_t *token_ids, const int64_t *seq_offsets,
                         int num_seqs, const int64_t *block_starts, const int64_t *gpu_block_ids,
-                        const fkv_transfer_desc *layout, int64_t *num_transferred,
+                        const fkv_transfer_desc *layout, int synchronous, int64_t *num_transferred,
                         int64_t *cpu_block_ids, void *stream);
 
 /* Mark cached blocks ready (ready != 0) or not, by block hash (host array);

@@ -120,7 +120,7 @@ int main(int argc, char **argv) {
     fkv_cache_index *ci = NULL;
     CHECK(fkv_cache_index_create(-1, NC, TPB, &ci));
     d.is_host_to_device = 0;
-    CHECK(fkv_cache_index_put(ci, seq, offs, 2, put_gpu, &d, 1, skipped, moved, cpu_of, NULL, NULL));
+    CHECK(fkv_cache_index_put(ci, seq, offs, 2, put_gpu, &d, 1, 1, skipped, moved, cpu_of, NULL, NULL));
     if (skipped[0] != 0 || moved[0] != NB || skipped[1] != 3 || moved[1] != 2) {
       fprintf(stderr, "put: skipped %lld/%lld moved %lld/%lld\n", (long long)skipped[0], (long long)skipped[1],
               (long long)moved[0], (long long)moved[1]);
@@ -136,7 +136,7 @@ int main(int argc, char **argv) {
     int64_t get_gpu[NB], got[1];
     for (int i = 0; i < NB; ++i) get_gpu[i] = 20 + i;
     d.is_host_to_device = 1;
-    CHECK(fkv_cache_index_get(ci, seq, offs, 1, NULL, get_gpu, &d, got, NULL, NULL));
+    CHECK(fkv_cache_index_get(ci, seq, offs, 1, NULL, get_gpu, &d, 1, got, NULL, NULL));
     if (got[0] != NB) {
       fprintf(stderr, "get: %lld blocks\n", (long long)got[0]);
       return 1;

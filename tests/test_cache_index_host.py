@@ -17,7 +17,7 @@ def index(tpb=4):
     ci.device = 0
     ci.calls = []
 
-    def put_packed(ptr, offsets, gids, layout, mark_ready=True):
+    def put_packed(ptr, offsets, gids, layout, mark_ready=True, synchronous=True):
         ci.calls.append(("put", offsets.copy(), np.asarray(gids).copy()))
         R = len(offsets) - 1
         blk = C._blk_off(offsets, tpb)
@@ -27,7 +27,7 @@ def index(tpb=4):
         sk = np.minimum(n, 1)
         return C.PutBatch(sk, n - sk, np.arange(nb), np.asarray(gids)[:nb], np.zeros(nb, np.uint64), blk)
 
-    def get_packed(ptr, offsets, gids, layout, block_starts=None):
+    def get_packed(ptr, offsets, gids, layout, block_starts=None, synchronous=True):
         ci.calls.append(("get", offsets.copy(), np.asarray(gids).copy(), list(block_starts)))
         R = len(offsets) - 1
         goff = np.zeros(R + 1, dtype=np.int64)

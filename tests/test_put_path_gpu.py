@@ -375,3 +375,38 @@ def test_edge_batches_match_the_oracle():
     assert got.num_transferred.tolist() == [1, 1, 1]
     assert pools.layers_match()
     ci.close()
+
+
+def test_asynchronous_put_and_get_return_the_decisions_first():
+    """synchronous=False returns once the decisions are known (the
+    reference's put/get return before their transfers run); the copies and
+    the ready marks finish on the stream, and the bytes equal the oracle's
+    once the stream has drained."""
+    tpb = 16
+    rng = np.random.default_rng(61)
+    pools = Pools(Case("async", 2, 1, 64, tpb, 2048, 2048), seed=67)
+    tier = CI.CpuTier(2048, tpb)
+    ci = CpuCacheIndex(2048, tpb)
+    seen = []
+    toks, gids = _requests(rng, 128, tpb, 24, 3000, seen, 0.5, 2048)
+    res = ci.put(toks, gids, pools.layout, synchronous=False)
+    want = [tier.put(t, g) for t, g in zip(toks, gids)]
+    for r, w in enumerate(want):
+        assert (int(res.num_skipped[r]), res.cpu_blocks[r].tolist()) == (w.num_skipped, w.cpu_blocks.tolist())
+        pools.expect_d2h(w.gpu_blocks, w.cpu_blocks)
+        tier.complete(w)
+    torch.cuda.current_stream().synchronize()
+    assert pools.pool_matches()
+    assert ci.stats()["total_ready_blocks"] == tier.tree.total_ready()
+    gt = [t for t in seen if len(t) >= tpb][:64]
+    perm = rng.permutation(2048).astype(np.int64)
+    cuts = np.cumsum([0] + [len(t) // tpb for t in gt])
+    dst = [perm[cuts[i]:cuts[i + 1]] for i in range(len(gt))]
+    got = ci.get(gt, dst, pools.layout, synchronous=False)
+    for r, (t, g) in enumerate(zip(gt, dst)):
+        w = tier.get(t, g)
+        assert got.cpu_blocks[r].tolist() == w.cpu_blocks.tolist()
+        pools.expect_h2d(w.gpu_blocks, w.cpu_blocks)
+    torch.cuda.current_stream().synchronize()
+    assert pools.layers_match()
+    ci.close()
