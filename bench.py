@@ -697,7 +697,9 @@ def measure_put_path(S, reps: int = 3):
       transfer.cu (oracle/_ref, transfer_sms=8, ids pinned per op,
       synchronous) to copy, then the put's completion callback.
     control only: the second put batch again -- every block cached, nothing
-      copied -- so the time is hashing, matching and deciding."""
+      copied -- so the time is hashing, matching and deciding.
+    layer-wise get: the same get in layer groups (layer_granularity), timed
+      to the first group's event (when a prefill could start) and the last."""
     from oracle import cache_index as CI
     from oracle import oracle as O
     from flexkv_b200.cache_index import CpuCacheIndex, KVLayout
@@ -716,6 +718,9 @@ def measure_put_path(S, reps: int = 3):
         raise RuntimeError("get batch larger than the GPU pool")
     ggids = [perm[cuts[i]:cuts[i + 1]] for i in range(len(gtoks))]
     ours, ctl, ours_get, ref, ref_ctl, ref_get, moved, got_blocks = [], [], [], [], [], [], [], []
+    L = len(S.layers)
+    G = next(g for g in range(max(1, L // 8), L + 1) if L % g == 0)  # layer groups of the layer-wise get
+    lw_first, lw_all = [], []
     ref_lib = O.ref_lib() if O.reference_available() else None
     ptrs = S.ptrs.pin_memory()
     stream = torch.cuda.current_stream().cuda_stream
@@ -745,12 +750,24 @@ def measure_put_path(S, reps: int = 3):
             t0 = time.perf_counter()
             gres = ci.get(gtoks, ggids, layout)
             tg = time.perf_counter() - t0
+            evs = [torch.cuda.Event() for _ in range(L // G)]
+            for e in evs:
+                e.record()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            ci.get(gtoks, ggids, layout, synchronous=False, layer_granularity=G, group_events=evs)
+            evs[0].synchronize()
+            t_first = time.perf_counter() - t0
+            evs[-1].synchronize()
+            t_lw = time.perf_counter() - t0
         finally:
             ci.close()
         if rep:
             ours.append(sum(ts))
             ctl.append(tc)
             ours_get.append(tg)
+            lw_first.append(t_first)
+            lw_all.append(t_lw)
             moved.append(blocks)
             got_blocks.append(int(gres.num_transferred.sum()))
         if ref_lib is None:
@@ -795,6 +812,9 @@ def measure_put_path(S, reps: int = 3):
                  "control_us_per_request": round(med(ctl) / n_req * 1e6, 2)},
         "ours_get": {"ms": round(med(ours_get) * 1e3, 2),
                      "GBps": round(got_blocks[-1] * bb / med(ours_get) / 1e9, 2)},
+        "ours_get_layerwise": {"layer_granularity": G, "groups": L // G,
+                               "first_group_ms": round(med(lw_first) * 1e3, 2),
+                               "all_groups_ms": round(med(lw_all) * 1e3, 2)},
         "how": "wall clock, median of %d repetitions on a fresh index" % reps,
     }
     if ref:

@@ -197,8 +197,8 @@ _SIGNATURES = {
         c_int, [c_vp, c_vp, c_vp, c_int, c_vp, ctypes.POINTER(TransferDesc), c_int, c_int, c_vp, c_vp,
                 c_vp, c_vp, c_vp]),
     "fkv_cache_index_get": (
-        c_int, [c_vp, c_vp, c_vp, c_int, c_vp, c_vp, ctypes.POINTER(TransferDesc), c_int, c_vp, c_vp,
-                c_vp]),
+        c_int, [c_vp, c_vp, c_vp, c_int, c_vp, c_vp, ctypes.POINTER(TransferDesc), c_int, c_vp, c_int, c_vp,
+                c_vp, c_vp]),
     "fkv_cache_index_set_ready": (c_int, [c_vp, c_vp, c_i64, c_int, P_i64, c_vp]),
     "fkv_cache_index_remove": (c_int, [c_vp, c_vp, c_i64, c_vp, c_vp]),
     "fkv_cache_index_recycle": (c_int, [c_vp, c_vp, c_i64, c_vp]),

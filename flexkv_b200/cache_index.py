@@ -286,23 +286,29 @@ class CpuCacheIndex:
         return PutBatch(nsk, ntr, cpu[:nb], gids[:nb], hashes[:nb], blk)
 
     def get(self, token_ids: Sequence, gpu_block_ids: Sequence, layout: KVLayout,
-            block_starts: Optional[Sequence[int]] = None, synchronous: bool = True) -> GetBatch:
+            block_starts: Optional[Sequence[int]] = None, synchronous: bool = True,
+            layer_granularity: int = -1, group_events: Optional[Sequence] = None) -> GetBatch:
         """Gets of the CPU tier for a batch of requests (cache_engine.py:
         412-548, SSD off): request r selects its full blocks from
         block_starts[r] (default 0) on and brings one GPU block per selected
         block; its ready cached blocks in that range are read into the
         leading GPU blocks.  Returns when the copies are complete (or, with
-        synchronous=False, once the decisions are known)."""
+        synchronous=False, once the decisions are known).  layer_granularity
+        copies the layers in groups of that many, in order, and records
+        group_events[i] (torch.cuda.Event) after group i, for a prefill
+        that starts on the first layers while later ones load."""
         if len(token_ids) != len(gpu_block_ids):
             raise ValueError("one gpu block list per request")
         buf, offsets, ptr = _pack_tokens(token_ids)
         parts = [np.asarray(g.cpu() if isinstance(g, torch.Tensor) else g, dtype=np.int64).reshape(-1)
                  for g in gpu_block_ids]
         gids = np.concatenate(parts) if parts else np.zeros(0, dtype=np.int64)
-        return self.get_packed(ptr, offsets, gids, layout, block_starts, synchronous)
+        return self.get_packed(ptr, offsets, gids, layout, block_starts, synchronous, layer_granularity,
+                               group_events)
 
     def get_packed(self, token_ptr: int, seq_offsets: np.ndarray, gpu_block_ids: np.ndarray, layout: KVLayout,
-                   block_starts: Optional[Sequence[int]] = None, synchronous: bool = True) -> GetBatch:
+                   block_starts: Optional[Sequence[int]] = None, synchronous: bool = True,
+                   layer_granularity: int = -1, group_events: Optional[Sequence] = None) -> GetBatch:
         """get over a packed batch (as put_packed; gpu_block_ids holds
         n_r - block_starts[r] GPU blocks per request)."""
         offsets = np.ascontiguousarray(seq_offsets, dtype=np.int64)
@@ -325,15 +331,24 @@ class CpuCacheIndex:
         moved = np.zeros(R, dtype=np.int64)
         cpu = np.full(max(ng, 1), -1, dtype=np.int64)
         d = layout.desc(host_to_device=True)
+        ev = None
+        if group_events is not None:
+            handles = []
+            for e in group_events:
+                if not e.cuda_event:  # torch creates the CUDA event on its first record
+                    e.record()
+                handles.append(e.cuda_event)
+            ev = (ctypes.c_void_p * len(handles))(*handles)
         check(_lib.load().fkv_cache_index_get(self._h, token_ptr, offsets.ctypes.data, R, starts.ctypes.data,
-                                              gbuf.ctypes.data, ctypes.byref(d), int(bool(synchronous)),
-                                              moved.ctypes.data,
+                                              gbuf.ctypes.data, ctypes.byref(d), int(layer_granularity), ev,
+                                              int(bool(synchronous)), moved.ctypes.data,
                                               cpu.ctypes.data, self._stream()),
               "CpuCacheIndex.get")
         return GetBatch(starts, moved, cpu[:ng], gids, goff)
 
     def get_requests(self, requests: Sequence[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]],
-                     layout: KVLayout, synchronous: bool = True) -> Tuple[List[torch.Tensor], GetBatch]:
+                     layout: KVLayout, synchronous: bool = True, layer_granularity: int = -1,
+                     group_events: Optional[Sequence] = None) -> Tuple[List[torch.Tensor], GetBatch]:
         """``GlobalCacheEngine.get(request_id, token_ids, token_mask,
         slot_mapping)`` for a batch (cache_engine.py:150-219, CPU tier):
         the mask selects a suffix of the full blocks that ends at the last
@@ -359,7 +374,7 @@ class CpuCacheIndex:
             toks.append(token_ids[:aligned].to(torch.int64).numpy())
             starts.append(bs)
             gids.append((slot_mapping[::tpb][:be - bs] // tpb).cpu().numpy().astype(np.int64))
-        res = self.get(toks, gids, layout, starts, synchronous)
+        res = self.get(toks, gids, layout, starts, synchronous, layer_granularity, group_events)
         return [res.return_mask(r, lens[r], tpb) for r in range(len(lens))], res
 
     def put_requests(self, requests: Sequence[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]],

@@ -996,7 +996,8 @@ int fkv_cache_index_put(fkv_cache_index *ci, const int64_t *token_ids, const int
 
 int fkv_cache_index_get(fkv_cache_index *ci, const int64_t *token_ids, const int64_t *seq_offsets, int num_seqs,
                         const int64_t *block_starts, const int64_t *gpu_block_ids, const fkv_transfer_desc *layout,
-                        int synchronous, int64_t *num_transferred, int64_t *cpu_block_ids, void *stream) {
+                        int layer_granularity, void *const *group_events, int synchronous,
+                        int64_t *num_transferred, int64_t *cpu_block_ids, void *stream) {
   clear_error();
   if (!ci || !layout) return fail(FKV_ERR_INVALID_ARG, "null index or layout");
   if (num_seqs < 0 || (num_seqs > 0 && (!seq_offsets || !num_transferred)))
@@ -1024,6 +1025,10 @@ int fkv_cache_index_get(fkv_cache_index *ci, const int64_t *token_ids, const int
   if (!token_ids || !gpu_block_ids) return fail(FKV_ERR_INVALID_ARG, "null token ids or gpu block ids");
   if (nb >= (1ll << 29)) return fail(FKV_ERR_INVALID_ARG, "too many blocks in one batch (limit 2^29)");
   if (!layout->is_host_to_device) return fail(FKV_ERR_INVALID_ARG, "the get path copies host to device");
+  const int L = layout->num_layers;
+  const int G = layer_granularity > 0 ? layer_granularity : L;
+  if (L > 0 && (G > L || L % G != 0))  // transfer_pattern.py:377
+    return fail(FKV_ERR_INVALID_ARG, "layer_granularity must divide the number of layers");
   if (int rc = transfer_check_device_ids(*layout, ng, ci->num_blocks - 1)) return rc;
   std::vector<int64_t> gids((size_t)ng);
   int gdev = 0, gd = -1;
@@ -1084,13 +1089,22 @@ int fkv_cache_index_get(fkv_cache_index *ci, const int64_t *token_ids, const int
   FKV_CUDA(cudaMemcpyAsync(pin, b + o_moved, 8 * num_seqs, cudaMemcpyDeviceToHost, s));
   if (ng) FKV_CUDA(cudaMemcpyAsync(pin + num_seqs, b + o_cpu, 8 * ng, cudaMemcpyDeviceToHost, s));
   FKV_CUDA(cudaEventRecord(ci->decided, s));
-  fkv_transfer_desc d = *layout;
-  d.is_host_to_device = 1;
-  if (ng > 0)
-    if (int rc = transfer_enqueue_device_ids(d, reinterpret_cast<int64_t *>(b + o_h2dg),
-                                             reinterpret_cast<int64_t *>(b + o_h2dc), d_cnt, ng,
-                                             ci->num_blocks - 1, s))
-      return rc;
+  // One copy per layer group, in order (convert_read_graph_to_layer_wise_graph,
+  // transfer_pattern.py:370-428: group i after group i-1); the caller's event
+  // for group i marks its layers as loaded (wait_at_layer_group).
+  {
+    fkv_transfer_desc d = *layout;
+    d.is_host_to_device = 1;
+    if (ng > 0) {
+      if (int rc = transfer_enqueue_device_ids(d, reinterpret_cast<int64_t *>(b + o_h2dg),
+                                               reinterpret_cast<int64_t *>(b + o_h2dc), d_cnt, ng,
+                                               ci->num_blocks - 1, s, G, group_events))
+        return rc;
+    } else if (group_events) {
+      for (int g0 = 0; g0 < L; g0 += G)
+        if (group_events[g0 / G]) FKV_CUDA(cudaEventRecord((cudaEvent_t)group_events[g0 / G], s));
+    }
+  }
   if (synchronous) FKV_CUDA(cudaStreamSynchronize(s));
   else FKV_CUDA(cudaEventSynchronize(ci->decided));
   std::memcpy(num_transferred, pin, 8 * num_seqs);

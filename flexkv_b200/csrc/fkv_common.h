@@ -78,9 +78,13 @@ size_t transfer_stage_bytes(const fkv_transfer_desc &d);
 // layout and direction; its id arrays and num_blocks are not used.  The
 // producer of the lists guarantees the GPU ids are in range; cpu ids are at
 // most max_cpu_id, checked here against d.cpu_pool_bytes when that is set.
+// layer_granularity > 0 splits the layers into groups of that many (it must
+// divide them), copied one launch per group in order; group_events[g]
+// (optional cudaEvent_t handles) is recorded after group g.
 int transfer_enqueue_device_ids(const fkv_transfer_desc &d, const int64_t *gpu_ids_dev,
                                 const int64_t *cpu_ids_dev, const int64_t *n_dev, int64_t n_max,
-                                int64_t max_cpu_id, cudaStream_t s);
+                                int64_t max_cpu_id, cudaStream_t s, int layer_granularity = 0,
+                                void *const *group_events = nullptr);
 // The checks transfer_enqueue_device_ids makes before it launches, alone:
 // callers that change state before the copy run them first.
 int transfer_check_device_ids(const fkv_transfer_desc &d, int64_t n_max, int64_t max_cpu_id);

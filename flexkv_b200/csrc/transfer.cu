@@ -697,7 +697,8 @@ int transfer_check_device_ids(const fkv_transfer_desc &d, int64_t n_max, int64_t
 
 int transfer_enqueue_device_ids(const fkv_transfer_desc &d, const int64_t *gpu_ids_dev,
                                 const int64_t *cpu_ids_dev, const int64_t *n_dev, int64_t n_max,
-                                int64_t max_cpu_id, cudaStream_t s) {
+                                int64_t max_cpu_id, cudaStream_t s, int layer_granularity,
+                                void *const *group_events) {
   HostPlan hp;
   if (int rc = device_ids_plan(d, n_max, max_cpu_id, hp)) return rc;
   if (n_max <= 0 || d.num_layers == 0 || d.chunk_size_in_bytes < 16) return FKV_OK;
@@ -722,10 +723,12 @@ int transfer_enqueue_device_ids(const fkv_transfer_desc &d, const int64_t *gpu_i
   }
   int sms = d.transfer_sms > 0 ? d.transfer_sms : env_int("FKV_TRANSFER_SMS", kDefaultSms);
   sms = std::min(sms, ctx->num_sms);
+  const int64_t G = layer_granularity > 0 ? layer_granularity : L;
+  if (L % G != 0) return fail(FKV_ERR_INVALID_ARG, "layer_granularity must divide the number of layers");
   const int64_t warps_per_cta = kThreads / 32;
-  int64_t grid = std::min<int64_t>((int64_t)sms * std::max(occ, 1), (L * KV * n_max + warps_per_cta - 1) / warps_per_cta);
+  int64_t grid = std::min<int64_t>((int64_t)sms * std::max(occ, 1), (G * KV * n_max + warps_per_cta - 1) / warps_per_cta);
   grid = std::max<int64_t>(grid, 1);
-  // Layer pointer table: staged, uploaded on s, freed on s after the kernel.
+  // Layer pointer table: staged once, uploaded on s, freed on s after the kernels.
   const size_t tb = 8 * (size_t)L;
   char *stage = nullptr;
   if (int rc = acquire_staging(ctx, tb, &stage)) return rc;
@@ -738,22 +741,34 @@ int transfer_enqueue_device_ids(const fkv_transfer_desc &d, const int64_t *gpu_i
     return fail_cuda(e, "cudaMemcpyAsync(layer table)");
   }
   if (int rc = release_staging(ctx, s)) return rc;
-  CopyParams p{};
-  p.layer_ptrs = reinterpret_cast<char *const *>(dev_table);
-  p.gpu_ids = gpu_ids_dev;
-  p.cpu_ids = cpu_ids_dev;
-  p.cpu_base = hp.cpu_dev_base;
-  p.gpu_kv_stride = hp.gkv;
-  p.gpu_block_stride = hp.gbs;
-  p.cpu_layer_stride = hp.cls;
-  p.cpu_kv_stride = hp.ckv;
-  p.cpu_block_stride = hp.cbs;
-  p.n_vec = hp.copy_bytes / 16;
-  const uint32_t kvd = (uint32_t)KV, nl = (uint32_t)L, nm = (uint32_t)n_max;
-  void *args[] = {&p, const_cast<int64_t **>(&n_dev), (void *)&kvd, (void *)&nl, (void *)&nm};
-  e = cudaLaunchKernel(k, dim3((unsigned)grid), dim3(kThreads), args, 0, s);
-  int rc = e == cudaSuccess ? FKV_OK : fail_cuda(e, "cudaLaunchKernel(kv_copy_devn_kernel)");
-  if (rc == FKV_OK) note_launch();
+  // One launch per group of G layers, in order; group_events[g] (optional)
+  // is recorded after group g.
+  int rc = FKV_OK;
+  for (int64_t g0 = 0; g0 < L && rc == FKV_OK; g0 += G) {
+    CopyParams p{};
+    p.layer_ptrs = reinterpret_cast<char *const *>(dev_table) + g0;
+    p.gpu_ids = gpu_ids_dev;
+    p.cpu_ids = cpu_ids_dev;
+    p.cpu_base = hp.cpu_dev_base + g0 * hp.cls;
+    p.gpu_kv_stride = hp.gkv;
+    p.gpu_block_stride = hp.gbs;
+    p.cpu_layer_stride = hp.cls;
+    p.cpu_kv_stride = hp.ckv;
+    p.cpu_block_stride = hp.cbs;
+    p.n_vec = hp.copy_bytes / 16;
+    const uint32_t kvd = (uint32_t)KV, nl = (uint32_t)G, nm = (uint32_t)n_max;
+    void *args[] = {&p, const_cast<int64_t **>(&n_dev), (void *)&kvd, (void *)&nl, (void *)&nm};
+    e = cudaLaunchKernel(k, dim3((unsigned)grid), dim3(kThreads), args, 0, s);
+    if (e != cudaSuccess) {
+      rc = fail_cuda(e, "cudaLaunchKernel(kv_copy_devn_kernel)");
+      break;
+    }
+    note_launch();
+    if (group_events && group_events[g0 / G]) {
+      e = cudaEventRecord((cudaEvent_t)group_events[g0 / G], s);
+      if (e != cudaSuccess) rc = fail_cuda(e, "cudaEventRecord(layer group)");
+    }
+  }
   int rf = scratch_free(dev_table, s);
   return rc != FKV_OK ? rc : rf;
 }

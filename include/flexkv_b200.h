@@ -492,10 +492,16 @@ int fkv_cache_index_put(fkv_cache_index *ci, const int64_t *token_ids, const int
  * fkv_cache_index_put).  Out: num_transferred[s] blocks read (the return
  * mask covers blocks [block_starts[s], +num_transferred[s])); cpu_block_ids
  * (optional, one per GPU entry): the pool block read into it, -1 if none.
- * The index and the pool do not change. */
+ * The index and the pool do not change.  layer_granularity > 0 copies the
+ * layers in groups of that many, in order (it must divide the number of
+ * layers, as convert_read_graph_to_layer_wise_graph requires,
+ * transfer_pattern.py:370-428); group_events (optional, one cudaEvent_t per
+ * group) are recorded on `stream` after each group, for the caller's
+ * wait_at_layer_group (kvmanager.py:480). */
 int fkv_cache_index_get(fkv_cache_index *ci, const int64_t *token_ids, const int64_t *seq_offsets,
                         int num_seqs, const int64_t *block_starts, const int64_t *gpu_block_ids,
-                        const fkv_transfer_desc *layout, int synchronous, int64_t *num_transferred,
+                        const fkv_transfer_desc *layout, int layer_granularity,
+                        void *const *group_events, int synchronous, int64_t *num_transferred,
                         int64_t *cpu_block_ids, void *stream);
 
 /* Mark cached blocks ready (ready != 0) or not, by block hash (host array);

@@ -136,7 +136,7 @@ int main(int argc, char **argv) {
     int64_t get_gpu[NB], got[1];
     for (int i = 0; i < NB; ++i) get_gpu[i] = 20 + i;
     d.is_host_to_device = 1;
-    CHECK(fkv_cache_index_get(ci, seq, offs, 1, NULL, get_gpu, &d, 1, got, NULL, NULL));
+    CHECK(fkv_cache_index_get(ci, seq, offs, 1, NULL, get_gpu, &d, 0, NULL, 1, got, NULL, NULL));
     if (got[0] != NB) {
       fprintf(stderr, "get: %lld blocks\n", (long long)got[0]);
       return 1;

@@ -27,7 +27,8 @@ def index(tpb=4):
         sk = np.minimum(n, 1)
         return C.PutBatch(sk, n - sk, np.arange(nb), np.asarray(gids)[:nb], np.zeros(nb, np.uint64), blk)
 
-    def get_packed(ptr, offsets, gids, layout, block_starts=None, synchronous=True):
+    def get_packed(ptr, offsets, gids, layout, block_starts=None, synchronous=True, layer_granularity=-1,
+                   group_events=None):
         ci.calls.append(("get", offsets.copy(), np.asarray(gids).copy(), list(block_starts)))
         R = len(offsets) - 1
         goff = np.zeros(R + 1, dtype=np.int64)

@@ -410,3 +410,44 @@ def test_asynchronous_put_and_get_return_the_decisions_first():
     torch.cuda.current_stream().synchronize()
     assert pools.layers_match()
     ci.close()
+
+
+def test_layerwise_get_completes_group_by_group():
+    """layer_granularity: the layers are read in groups, in order, and the
+    event of group i marks those layers as loaded (the reference's layer-wise
+    read graph, transfer_pattern.py:370-428, waited on by
+    wait_at_layer_group); a granularity that does not divide the layers is
+    refused as the reference asserts."""
+    tpb = 16
+    rng = np.random.default_rng(71)
+    case = Case("layers", 8, 1, 64, tpb, 1024, 1024)
+    pools = Pools(case, seed=73)
+    tier = CI.CpuTier(1024, tpb)
+    ci = CpuCacheIndex(1024, tpb)
+    seen = []
+    toks, gids = _requests(rng, 64, tpb, 16, 3000, seen, 0.5, 1024)
+    ci.put(toks, gids, pools.layout)
+    for t, g in zip(toks, gids):
+        tier.complete(tier.put(t, g))
+    gt = [t for t in toks if len(t) >= tpb][:32]
+    perm = rng.permutation(1024).astype(np.int64)
+    cuts = np.cumsum([0] + [len(t) // tpb for t in gt])
+    dst = [perm[cuts[i]:cuts[i + 1]] for i in range(len(gt))]
+    # expected GPU images: the puts copied D2H (host images of the pool follow the device pool)
+    pools.cpu_img[:] = pools.cpu.numpy()
+    for t, g in zip(gt, dst):
+        w = tier.get(t, g)
+        pools.expect_h2d(w.gpu_blocks, w.cpu_blocks)
+    events = [torch.cuda.Event() for _ in range(4)]
+    got = ci.get(gt, dst, pools.layout, synchronous=False, layer_granularity=2, group_events=events)
+    assert int(got.num_transferred.sum()) == int(sum(len(t) // tpb for t in gt))
+    for gi, ev in enumerate(events):
+        ev.synchronize()
+        for l in (2 * gi, 2 * gi + 1):
+            assert np.array_equal(pools.layers[l].cpu().numpy(), pools.gpu_imgs[l]), f"layer {l} after group {gi}"
+    torch.cuda.current_stream().synchronize()
+    assert pools.layers_match()
+    with pytest.raises(FlexKVError) as e:
+        ci.get(gt[:1], dst[:1], pools.layout, layer_granularity=3)
+    assert e.value.code == FKV_ERR_INVALID_ARG
+    ci.close()
