@@ -15,7 +15,12 @@ Restates, in this module's own structure:
     evict (every cached block still locked or not ready, or the caller has
     already made room);
   * the put callback: _transfer_callback -> CacheEngine.cleanup (:904-925,
-    :83-85), which unlocks the inserted node and marks it ready.
+    :83-85), which unlocks the inserted node and marks it ready;
+  * the CPU-tier get: GlobalCacheEngine.get (:150-219) and _get_impl_local
+    (:412-548) with the SSD tier off;
+  * both with the SSD tier on (TwoTier): the put's D2H into new CPU blocks
+    and H2DISK of the blocks the SSD tier lacks, and the get's legs, when
+    neither tier's take() evicts.
 
 Pinned by tests/golden/put_path.json, which tests/golden/make_put_golden.py
 produced by running the reference's own GlobalCacheEngine.
@@ -268,3 +273,87 @@ class CpuTier:
         if f == 0:
             return empty
         return PutResult(block_start, f, gpu_blocks[:f].copy(), np.asarray(ready, dtype=np.int64))
+
+
+@dataclass
+class TwoTierPut:
+    num_skipped: int
+    num_transferred: int
+    gpu_blocks: np.ndarray        # D2H sources
+    cpu_blocks: np.ndarray        # D2H destinations (new CPU blocks)
+    h2disk_cpu: np.ndarray        # H2DISK sources (the reference's cpu_new[-frag2:])
+    ssd_blocks: np.ndarray        # H2DISK destinations (new SSD blocks)
+    cpu_node: Optional[Node] = None
+    cpu_size: int = 0
+    ssd_node: Optional[Node] = None
+    ssd_size: int = 0
+
+
+class TwoTier:
+    """GlobalCacheEngine with the CPU and SSD tiers (cache_engine.py:787-902
+    for puts, :412-548 for gets), when neither tier's take() evicts: every
+    block still locked or not ready, or pools large enough."""
+
+    def __init__(self, cpu_blocks: int, ssd_blocks: int, tokens_per_block: int):
+        self.cpu = CpuTier(cpu_blocks, tokens_per_block)
+        self.ssd = CpuTier(ssd_blocks, tokens_per_block)
+        self.tpb = tokens_per_block
+
+    def put(self, token_ids: np.ndarray, gpu_blocks: np.ndarray) -> TwoTierPut:
+        h = self.cpu.hashes(token_ids)
+        n = len(h)
+        gpu_blocks = np.asarray(gpu_blocks, dtype=np.int64)[:n]
+        z = np.zeros(0, np.int64)
+        empty = TwoTierPut(0, 0, z, z, z, z)
+        cm, sm = self.cpu.tree.match(h), self.ssd.tree.match(h)
+        skipped = min(cm.num_matched, n)
+        frag12 = n - skipped
+        if frag12 == 0:
+            return empty
+        frag2 = n - min(sm.num_matched, n)
+        cpu_new = self.cpu.pool.allocate(min(frag12, self.cpu.pool.num_free))
+        ssd_new = self.ssd.pool.allocate(min(frag2, self.ssd.pool.num_free))
+        if len(cpu_new) < frag12 or len(ssd_new) < frag2:
+            self.cpu.pool.recycle(cpu_new)
+            self.ssd.pool.recycle(ssd_new)
+            return empty
+        h2disk_cpu = cpu_new[-frag2:] if frag2 > 0 else z
+        cnode = self.cpu.tree.insert(h, cpu_new, ready=False, m=cm)
+        cnode.locks += 1
+        snode = None
+        if len(ssd_new):
+            snode = self.ssd.tree.insert(h, ssd_new, ready=False, m=sm)
+            snode.locks += 1
+        return TwoTierPut(skipped, frag12, gpu_blocks[skipped:].copy(), cpu_new, h2disk_cpu.copy(), ssd_new,
+                          cnode, cnode.size, snode, snode.size if snode else 0)
+
+    def complete(self, r: TwoTierPut) -> None:
+        """The put callback (cache_engine.py:904-916): both tiers' nodes."""
+        for tier, node, size in ((self.cpu, r.cpu_node, r.cpu_size), (self.ssd, r.ssd_node, r.ssd_size)):
+            if node is not None:
+                node.locks -= 1
+                tier.tree.set_ready(node, size)
+
+    def get(self, token_ids: np.ndarray, gpu_blocks: np.ndarray, block_start: int = 0):
+        """(num_transferred, [(kind, src_blocks, dst_blocks)...]) as the
+        reference's _get_impl_local builds them; with nothing evicted the SSD
+        tier never holds a ready block the CPU tier lacks, so the DISK2H leg
+        stays empty and this equals CpuTier.get."""
+        h = self.cpu.hashes(token_ids)
+        n = len(h)
+        if n == 0:
+            return 0, []
+        cm, sm = self.cpu.tree.match(h), self.ssd.tree.match(h)
+        cpu_ready = cm.blocks[:cm.num_ready][block_start:n]
+        ssd_ready = sm.blocks[:sm.num_ready][block_start:n]
+        frag12 = max(len(cpu_ready), len(ssd_ready))
+        frag1 = len(cpu_ready)
+        frag2 = max(len(ssd_ready) - len(cpu_ready), 0)
+        if frag12 == 0:
+            return 0, []
+        gpu_blocks = np.asarray(gpu_blocks, dtype=np.int64)
+        ops = []
+        if frag2 > 0:
+            ops.append(("DISK2H", np.asarray(ssd_ready[-frag2:], np.int64), None))
+        ops.append(("H2D", np.asarray(cpu_ready[:frag1], np.int64), gpu_blocks[:frag1].copy()))
+        return frag12, ops

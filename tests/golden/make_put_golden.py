@@ -90,16 +90,28 @@ def make_requests(rng, n_batches, per_batch, tpb, max_blocks, vocab, gpu_blocks,
     return batches, seen
 
 
+def ops_of(graph, TransferType):
+    """The graph's transfer ops as (type, src ids, dst ids), in op order."""
+    out = []
+    for op in graph._op_map.values():
+        if op.transfer_type == TransferType.VIRTUAL:
+            continue
+        out.append([op.transfer_type.name, op.src_descriptor.physical_block_ids.tolist(),
+                    op.dst_descriptor.physical_block_ids.tolist()])
+    return out
+
+
 def run_scenario(torch, refmods, name, seed, tpb, num_cpu_blocks, n_batches, per_batch,
-                 max_blocks, complete_each_batch, share=0.6, vocab=40):
+                 max_blocks, complete_each_batch, share=0.6, vocab=40, num_ssd_blocks=0):
     GlobalCacheEngine, CacheConfig, ModelConfig, SequenceMeta, DeviceType, TransferType = refmods
     rng = np.random.default_rng(seed)
     batches, seen = make_requests(rng, n_batches, per_batch, tpb, max_blocks, vocab, 256, share)
-    cc = CacheConfig(tokens_per_block=tpb, enable_cpu=True, enable_ssd=False, enable_remote=False,
-                     num_cpu_blocks=num_cpu_blocks)
+    cc = CacheConfig(tokens_per_block=tpb, enable_cpu=True, enable_ssd=num_ssd_blocks > 0,
+                     enable_remote=False, num_cpu_blocks=num_cpu_blocks,
+                     num_ssd_blocks=max(num_ssd_blocks, 1))
     mc = ModelConfig(num_layers=2, num_kv_heads=1, head_size=8)
     eng = GlobalCacheEngine(cc, mc)
-    out = {"name": name, "tpb": tpb, "num_cpu_blocks": num_cpu_blocks,
+    out = {"name": name, "tpb": tpb, "num_cpu_blocks": num_cpu_blocks, "num_ssd_blocks": num_ssd_blocks,
            "complete_each_batch": complete_each_batch, "batches": [], "results": [],
            "probes": [], "gets": [], "num_free": [], "total_cached": [], "total_ready": []}
     rid = 0
@@ -125,7 +137,7 @@ def run_scenario(torch, refmods, name, seed, tpb, num_cpu_blocks, n_batches, per
                     gpu_ids = op.src_descriptor.physical_block_ids.tolist()
                     cpu_ids = op.dst_descriptor.physical_block_ids.tolist()
             res.append({"skipped": skipped, "transferred": transferred,
-                        "gpu_blocks": gpu_ids, "cpu_blocks": cpu_ids})
+                        "gpu_blocks": gpu_ids, "cpu_blocks": cpu_ids, "ops": ops_of(graph, TransferType)})
         if complete_each_batch:
             for cb in callbacks:
                 cb()
@@ -164,8 +176,12 @@ def run_scenario(torch, refmods, name, seed, tpb, num_cpu_blocks, n_batches, per
             cb()
             gets.append({"tokens": tok.tolist(), "block_start": bs, "gpu_blocks": g.tolist(),
                          "mask_start": int(idx[0]) // tpb if len(idx) else 0, "transferred": len(idx) // tpb,
-                         "copied_gpu_blocks": gpu_ids, "copied_cpu_blocks": cpu_ids})
+                         "copied_gpu_blocks": gpu_ids, "copied_cpu_blocks": cpu_ids,
+                         "ops": ops_of(graph, TransferType)})
         out["gets"].append(gets)
+        if num_ssd_blocks:
+            out.setdefault("ssd_num_free", []).append(int(eng.ssd_cache_engine.mempool.num_free_blocks))
+            out.setdefault("ssd_total_cached", []).append(int(eng.ssd_cache_engine.index.total_cached_blocks()))
         out["num_free"].append(int(eng.cpu_cache_engine.mempool.num_free_blocks))
         out["total_cached"].append(int(eng.cpu_cache_engine.index.total_cached_blocks()))
         out["total_ready"].append(int(eng.cpu_cache_engine.index.total_ready_blocks()))
@@ -192,6 +208,11 @@ def main():
         run_scenario(torch, mods, "in_batch_sharing_tpb2", 12, 2, 512, 3, 16, 12, True, share=0.8),
         run_scenario(torch, mods, "pool_full", 13, 4, 48, 4, 10, 8, False),
         run_scenario(torch, mods, "callbacks_deferred", 14, 8, 256, 3, 10, 6, False, share=0.7),
+        # the SSD tier on: puts copy D2H into new CPU blocks and H2DISK the blocks the SSD tier lacks
+        run_scenario(torch, mods, "ssd_two_tier", 15, 4, 1024, 3, 12, 10, True, num_ssd_blocks=2048),
+        # an SSD pool that runs out (callbacks deferred: nothing evictable): puts come back empty
+        # and give their CPU blocks back
+        run_scenario(torch, mods, "ssd_pool_full", 16, 4, 512, 3, 10, 8, False, num_ssd_blocks=40),
     ]
     with open(os.path.join(HERE, "put_path.json"), "w") as f:
         json.dump({"source": "reference GlobalCacheEngine.put / CacheEngine.match, CPU tier only",

@@ -20,6 +20,9 @@ def scenarios():
 
 def replay(sc):
     """Run a golden scenario through the oracle; yield (kind, got, want)."""
+    if sc.get("num_ssd_blocks", 0):
+        yield from replay_two_tier(sc)
+        return
     tier = CI.CpuTier(sc["num_cpu_blocks"], sc["tpb"])
     for b, batch in enumerate(sc["batches"]):
         results = []
@@ -43,6 +46,40 @@ def replay(sc):
                 (g["mask_start"], g["transferred"], g["copied_gpu_blocks"], g["copied_cpu_blocks"])
         yield "totals", (tier.pool.num_free, tier.tree.total_blocks(), tier.tree.total_ready()), \
             (sc["num_free"][b], sc["total_cached"][b], sc["total_ready"][b])
+
+
+def replay_two_tier(sc):
+    """The scenarios with the SSD tier on: each put's D2H and H2DISK ops,
+    each get's ops, and both tiers' totals."""
+    tt = CI.TwoTier(sc["num_cpu_blocks"], sc["num_ssd_blocks"], sc["tpb"])
+    for b, batch in enumerate(sc["batches"]):
+        results = []
+        for req, want in zip(batch, sc["results"][b]):
+            r = tt.put(np.array(req["tokens"], dtype=np.int64), np.array(req["gpu_blocks"], dtype=np.int64))
+            results.append(r)
+            ops = []
+            if r.num_transferred:
+                ops.append(["D2H", r.gpu_blocks.tolist(), r.cpu_blocks.tolist()])
+                if len(r.ssd_blocks):
+                    ops.append(["H2DISK", r.h2disk_cpu.tolist(), r.ssd_blocks.tolist()])
+            yield "put", (r.num_skipped, r.num_transferred, ops), (want["skipped"], want["transferred"], want["ops"])
+        if sc["complete_each_batch"]:
+            for r in results:
+                tt.complete(r)
+        for p in sc["probes"][b]:
+            m = tt.cpu.match(np.array(p["tokens"], dtype=np.int64))
+            yield "probe", (m.num_matched, m.num_ready, m.blocks[:m.num_matched]), \
+                (p["num_matched"], p["num_ready"], p["blocks"])
+        for g in sc["gets"][b]:
+            n, ops = tt.get(np.array(g["tokens"], dtype=np.int64), np.array(g["gpu_blocks"], dtype=np.int64),
+                            g["block_start"])
+            got = [[k, src.tolist(), dst.tolist() if dst is not None else None] for k, src, dst in ops]
+            want_ops = [[k, src, dst] for k, src, dst in g["ops"]]
+            yield "get", (n, got), (g["transferred"], want_ops)
+        yield "totals", (tt.cpu.pool.num_free, tt.cpu.tree.total_blocks(), tt.cpu.tree.total_ready(),
+                         tt.ssd.pool.num_free, tt.ssd.tree.total_blocks()), \
+            (sc["num_free"][b], sc["total_cached"][b], sc["total_ready"][b], sc["ssd_num_free"][b],
+             sc["ssd_total_cached"][b])
 
 
 @pytest.mark.parametrize("name", [s["name"] for s in scenarios()])

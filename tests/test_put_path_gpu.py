@@ -66,7 +66,7 @@ class Pools:
         return all(np.array_equal(t.cpu().numpy(), w) for t, w in zip(self.layers, self.gpu_imgs))
 
 
-@pytest.mark.parametrize("name", list(golden()))
+@pytest.mark.parametrize("name", [n for n, sc in golden().items() if not sc.get("num_ssd_blocks")])
 def test_device_put_path_matches_the_reference(name):
     sc = golden()[name]
     tpb = sc["tpb"]
