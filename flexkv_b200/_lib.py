@@ -196,6 +196,9 @@ _SIGNATURES = {
     "fkv_cache_index_put": (
         c_int, [c_vp, c_vp, c_vp, c_int, c_vp, ctypes.POINTER(TransferDesc), c_int, c_int, c_vp, c_vp,
                 c_vp, c_vp, c_vp]),
+    "fkv_cache_index_put2": (
+        c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_vp, ctypes.POINTER(TransferDesc), c_int, c_vp, c_vp, c_vp,
+                c_vp, c_vp, c_vp, c_vp]),
     "fkv_cache_index_get": (
         c_int, [c_vp, c_vp, c_vp, c_int, c_vp, c_vp, ctypes.POINTER(TransferDesc), c_int, c_vp, c_int, c_vp,
                 c_vp, c_vp]),

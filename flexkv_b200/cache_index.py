@@ -164,6 +164,46 @@ class GetBatch:
         return m
 
 
+class TwoTierPutBatch(PutBatch):
+    """A put with the SSD tier on: PutBatch plus, per block, the new SSD
+    block (-1 if the SSD tier already held it or the put was empty)."""
+
+    def __init__(self, num_skipped, num_transferred, num_to_ssd, cpu_flat, gpu_flat, ssd_flat, hashes_flat,
+                 blk_off):
+        super().__init__(num_skipped, num_transferred, cpu_flat, gpu_flat, hashes_flat, blk_off)
+        self.num_to_ssd = num_to_ssd
+        self.ssd_flat = ssd_flat
+
+    def _to_ssd(self, flat) -> List[np.ndarray]:
+        o = self.blk_off
+        return [flat[o[r + 1] - int(f):o[r + 1]] for r, f in enumerate(self.num_to_ssd)]
+
+    @property
+    def ssd_blocks(self) -> List[np.ndarray]:
+        """Per request: the new SSD blocks (the H2DISK destinations)."""
+        return self._to_ssd(self.ssd_flat)
+
+    @property
+    def h2disk_cpu_blocks(self) -> List[np.ndarray]:
+        """Per request: the CPU blocks written to them (the H2DISK sources)."""
+        return self._to_ssd(self.cpu_flat)
+
+
+@dataclass
+class SsdTier:
+    """The SSD tier of a two-tier put: its index, its SSD context and the
+    arguments of c_ext.transfer_kv_blocks_ssd (worker.py:512-575)."""
+
+    index: "CpuCacheIndex"
+    ioctx: object              # c_ext.SSDIOCTX
+    strides: object            # flexkv_b200.ssd.SsdStrides
+    num_layers: int
+    num_blocks_per_file: int
+    round_robin: int = 1
+    threads_per_device: int = 16
+    is_mla: bool = False
+
+
 def _pack_tokens(token_ids: Sequence) -> Tuple[object, np.ndarray, int]:
     """Concatenate a batch of token sequences (int64; numpy, host or CUDA
     tensors) and give the token offsets.  Returns (buffer kept alive,
@@ -376,6 +416,52 @@ class CpuCacheIndex:
             gids.append((slot_mapping[::tpb][:be - bs] // tpb).cpu().numpy().astype(np.int64))
         res = self.get(toks, gids, layout, starts, synchronous, layer_granularity, group_events)
         return [res.return_mask(r, lens[r], tpb) for r in range(len(lens))], res
+
+    def put_two_tier(self, ssd: SsdTier, token_ids: Sequence, gpu_block_ids: Sequence, layout: KVLayout,
+                     mark_ready: bool = True) -> TwoTierPutBatch:
+        """Puts with the SSD tier on (cache_engine.py:787-902): the decisions
+        of both tiers on the device (this index is the CPU tier's), the D2H
+        copy, then the H2DISK leg through the SSD tier for the blocks the SSD
+        tier lacked, and with mark_ready both tiers' blocks marked ready (the
+        put callback).  Returns when the SSD writes are done."""
+        from . import c_ext
+        if len(token_ids) != len(gpu_block_ids):
+            raise ValueError("one gpu block list per request")
+        buf, offsets, ptr = _pack_tokens(token_ids)
+        nblk = (offsets[1:] - offsets[:-1]) // self.tokens_per_block
+        parts = [np.asarray(g.cpu() if isinstance(g, torch.Tensor) else g, dtype=np.int64).reshape(-1)
+                 for g in gpu_block_ids]
+        if any(len(g) != n for g, n in zip(parts, nblk)):
+            raise ValueError("one gpu block per full block")
+        gids = np.ascontiguousarray(np.concatenate(parts) if parts else np.zeros(0, np.int64))
+        R = len(offsets) - 1
+        blk = _blk_off(offsets, self.tokens_per_block)
+        nb = int(blk[-1])
+        gbuf = gids if nb else np.zeros(1, dtype=np.int64)
+        nsk, ntr, nss = (np.zeros(R, dtype=np.int64) for _ in range(3))
+        cpu = np.full(max(nb, 1), -1, dtype=np.int64)
+        ssd_ids = np.full(max(nb, 1), -1, dtype=np.int64)
+        hashes = np.zeros(max(nb, 1), dtype=np.uint64)
+        d = layout.desc()
+        check(_lib.load().fkv_cache_index_put2(self._h, ssd.index._h, ptr, offsets.ctypes.data, R, gbuf.ctypes.data,
+                                               ctypes.byref(d), int(bool(mark_ready)), nsk.ctypes.data,
+                                               ntr.ctypes.data, nss.ctypes.data, cpu.ctypes.data,
+                                               ssd_ids.ctypes.data, hashes.ctypes.data, self._stream()),
+              "CpuCacheIndex.put_two_tier")
+        res = TwoTierPutBatch(nsk, ntr, nss, cpu[:nb], gids[:nb], ssd_ids[:nb], hashes[:nb], blk)
+        sel = np.flatnonzero(ssd_ids[:nb] >= 0)
+        if len(sel):
+            st = ssd.strides
+            c_ext.transfer_kv_blocks_ssd(
+                ssd.ioctx, list(range(ssd.num_layers)), layout.cpu_tensor.data_ptr(),
+                np.ascontiguousarray(ssd_ids[sel]), np.ascontiguousarray(cpu[sel]),
+                st.cpu_layer_stride_in_bytes, st.cpu_kv_stride_in_bytes, st.ssd_layer_stride_in_bytes,
+                st.ssd_kv_stride_in_bytes, st.chunk_size_in_bytes, st.block_stride_in_bytes, False,
+                ssd.num_blocks_per_file, ssd.round_robin, ssd.threads_per_device, ssd.is_mla,
+                cpu_pool_bytes=layout.cpu_tensor.numel() * layout.cpu_tensor.element_size())
+            if mark_ready:
+                ssd.index.set_ready(hashes[sel])
+        return res
 
     def put_requests(self, requests: Sequence[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]],
                      layout: KVLayout, mark_ready: bool = True,

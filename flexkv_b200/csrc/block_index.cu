@@ -357,6 +357,135 @@ __global__ void __launch_bounds__(kDecideThreads) put_decide_fast_kernel(
   }
 }
 
+// Per block: present in a tier's index before the call, and the pool block
+// it holds there (-1 if absent).
+__global__ void tier_lookup_kernel(Table t, const uint64_t *hashes, int64_t nb, uint8_t *present, int64_t *phys) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nb; i += stride) {
+    const int64_t s = find(t, hashes[i]);
+    present[i] = s >= 0 ? 1 : 0;
+    if (phys) phys[i] = s >= 0 ? t.vals[s] : -1;
+  }
+}
+
+// One tier's pool in the two-tier decide step.
+struct PoolRef {
+  uint8_t *mask;
+  int64_t mask_bytes;
+  int64_t *free_ids;
+  int64_t *state;
+};
+
+// The two-tier put decisions (cache_engine.py:787-902 with the SSD tier on),
+// one warp, requests in order.  Per request: m_c / m_s leading blocks
+// present in the CPU / SSD tier (before the call, or inserted there by an
+// earlier request of the batch); k = n - m_c blocks go D2H into new CPU
+// blocks; f2 = n - m_s blocks go CPU -> SSD into new SSD blocks (the block's
+// CPU copy: new for j >= m_c, the cached one below); both takes must succeed
+// or the request comes back empty with both allocations given back
+// (cache_engine.py:838-852).  res[4r..4r+3] = skipped, moved D2H, moved to
+// SSD, outcome.
+__global__ void __launch_bounds__(32) put2_decide_kernel(
+    int num_req, const int64_t *blk_off, const uint8_t *before_c, const uint8_t *before_s, const int64_t *phys_c,
+    const int32_t *lslot, int32_t *ins_c, int32_t *ins_s, int64_t *slot_cpu, const int64_t *gpu_ids, PoolRef pc,
+    PoolRef ps, int64_t *res, int64_t *cpu_out, int64_t *ssd_out, int64_t *d2h_gpu, int64_t *d2h_cpu,
+    int64_t *new_c, int64_t *new_s, int64_t *counts) {
+  const int lane = threadIdx.x;
+  if (pc.state[kErr] != kErrNone || ps.state[kErr] != kErrNone) {  // an earlier step failed
+    if (lane == 0) counts[0] = counts[1] = 0;
+    return;
+  }
+  int64_t free_c = pc.state[kNumFree], len_c = pc.state[kListLen], off_c = pc.state[kOffset];
+  int64_t free_s = ps.state[kNumFree], len_s = ps.state[kListLen], off_s = ps.state[kOffset];
+  int64_t cnt_c = 0, cnt_s = 0;
+  for (int r = 0; r < num_req; ++r) {
+    const int64_t o = blk_off[r], n = blk_off[r + 1] - o;
+    int64_t m_c = n, m_s = n;
+    bool found_c = false, found_s = false;
+    for (int64_t jb = 0; jb < n && !(found_c && found_s); jb += 32) {
+      const int64_t j = jb + lane;
+      bool miss_c = false, miss_s = false;
+      if (j < n) {
+        const int32_t sl = lslot[o + j];
+        miss_c = !(before_c[o + j] || (sl >= 0 && ins_c[sl] < r));
+        miss_s = !(before_s[o + j] || (sl >= 0 && ins_s[sl] < r));
+      }
+      const unsigned bc = __ballot_sync(0xffffffffu, miss_c);
+      const unsigned bs = __ballot_sync(0xffffffffu, miss_s);
+      if (!found_c && bc) { m_c = jb + __ffs(bc) - 1; found_c = true; }
+      if (!found_s && bs) { m_s = jb + __ffs(bs) - 1; found_s = true; }
+    }
+    const int64_t k = n - m_c, f2 = n - m_s;
+    int64_t *rr = res + 4 * (int64_t)r;
+    if (k == 0) {  // the CPU tier holds every block: nothing moves (cache_engine.py:819-820)
+      if (lane == 0) { rr[0] = 0; rr[1] = 0; rr[2] = 0; rr[3] = kPutEmpty; }
+      continue;
+    }
+    int64_t a = k < free_c ? k : free_c;
+    if (a > len_c - off_c) {
+      len_c = rebuild_free_ids(pc.mask, pc.mask_bytes, pc.free_ids, lane);
+      off_c = 0;
+    }
+    if (a > len_c - off_c) a = len_c - off_c;
+    int64_t b = f2 < free_s ? f2 : free_s;
+    if (b > len_s - off_s) {
+      len_s = rebuild_free_ids(ps.mask, ps.mask_bytes, ps.free_ids, lane);
+      off_s = 0;
+    }
+    if (b > len_s - off_s) b = len_s - off_s;
+    if (a < k || b < f2) {  // allocate then recycle both: masks and counts unchanged
+      off_c += a;
+      off_s += b;
+      if (lane == 0) { rr[0] = 0; rr[1] = 0; rr[2] = 0; rr[3] = kPutNoSpace; }
+      continue;
+    }
+    for (int64_t t = lane; t < k; t += 32) {
+      const int64_t i = o + m_c + t, c = pc.free_ids[off_c + t];
+      pc.mask[c] = 0;
+      cpu_out[i] = c;
+      d2h_gpu[cnt_c + t] = gpu_ids[i];
+      d2h_cpu[cnt_c + t] = c;
+      new_c[cnt_c + t] = i;
+      const int32_t sl = lslot[i];
+      if (sl >= 0) {
+        ins_c[sl] = r;
+        slot_cpu[sl] = c;
+      }
+    }
+    __syncwarp();
+    for (int64_t t = lane; t < f2; t += 32) {
+      const int64_t j = m_s + t, i = o + j, sid = ps.free_ids[off_s + t];
+      ps.mask[sid] = 0;
+      ssd_out[i] = sid;
+      if (j < m_c) {  // already on the CPU tier: its cached block is the H2DISK source
+        const int32_t sl = lslot[i];
+        cpu_out[i] = before_c[i] ? phys_c[i] : (sl >= 0 ? slot_cpu[sl] : -1);
+      }
+      new_s[cnt_s + t] = i;
+      const int32_t sl = lslot[i];
+      if (sl >= 0) ins_s[sl] = r;
+    }
+    off_c += k;
+    free_c -= k;
+    cnt_c += k;
+    off_s += f2;
+    free_s -= f2;
+    cnt_s += f2;
+    if (lane == 0) { rr[0] = m_c; rr[1] = k; rr[2] = f2; rr[3] = kPutDone; }
+    __syncwarp();
+  }
+  if (lane == 0) {
+    pc.state[kNumFree] = free_c;
+    pc.state[kListLen] = len_c;
+    pc.state[kOffset] = off_c;
+    ps.state[kNumFree] = free_s;
+    ps.state[kListLen] = len_s;
+    ps.state[kOffset] = off_s;
+    counts[0] = cnt_c;
+    counts[1] = cnt_s;
+  }
+}
+
 // Insert the decided blocks, not ready (radixtree.py:202-256 with
 // is_ready=False, as _put_impl_local does).
 __global__ void put_insert_kernel(Table t, const uint64_t *hashes, const int64_t *new_blk, const int64_t *cpu_out,
@@ -991,6 +1120,136 @@ int fkv_cache_index_put(fkv_cache_index *ci, const int64_t *token_ids, const int
   }
   if (cpu_block_ids) std::memcpy(cpu_block_ids, ci->pin + down_res, 8 * nb);
   if (block_hashes) std::memcpy(block_hashes, ci->pin + down_res + 8 * nb, 8 * nb);
+  return FKV_OK;
+}
+
+int fkv_cache_index_put2(fkv_cache_index *cpu, fkv_cache_index *ssd, const int64_t *token_ids,
+                         const int64_t *seq_offsets, int num_seqs, const int64_t *gpu_block_ids,
+                         const fkv_transfer_desc *layout, int mark_ready, int64_t *num_skipped,
+                         int64_t *num_transferred, int64_t *num_to_ssd, int64_t *cpu_block_ids,
+                         int64_t *ssd_block_ids, uint64_t *block_hashes, void *stream) {
+  clear_error();
+  if (!cpu || !ssd || !layout || cpu == ssd) return fail(FKV_ERR_INVALID_ARG, "need two distinct indexes and a layout");
+  if (cpu->device != ssd->device || cpu->tpb != ssd->tpb)
+    return fail(FKV_ERR_INVALID_ARG, "the CPU and SSD indexes must share the device and tokens_per_block");
+  if (num_seqs < 0 || (num_seqs > 0 && (!seq_offsets || !num_skipped || !num_transferred || !num_to_ssd)))
+    return fail(FKV_ERR_INVALID_ARG, "bad batch description");
+  if (num_seqs == 0) return FKV_OK;
+  std::scoped_lock lk(cpu->mu, ssd->mu);
+  DeviceGuard g(cpu->device);
+  cudaStream_t s = (cudaStream_t)stream;
+  std::vector<int64_t> blk;
+  if (int rc = batch_offsets(seq_offsets, num_seqs, cpu->tpb, blk)) return rc;
+  const int64_t nb = blk[num_seqs];
+  for (int r = 0; r < num_seqs; ++r) num_skipped[r] = num_transferred[r] = num_to_ssd[r] = 0;
+  if (nb == 0) return FKV_OK;
+  if (!token_ids || !gpu_block_ids) return fail(FKV_ERR_INVALID_ARG, "null token ids or gpu block ids");
+  if (nb >= (1ll << 29)) return fail(FKV_ERR_INVALID_ARG, "too many blocks in one batch (limit 2^29)");
+  if (layout->is_host_to_device) return fail(FKV_ERR_INVALID_ARG, "the put path copies device to host");
+  if (int rc = transfer_check_device_ids(*layout, nb, cpu->num_blocks - 1)) return rc;
+  std::vector<int64_t> gids((size_t)nb);
+  int gdev = 0, gd = -1;
+  pointer_is_device(gpu_block_ids, &gdev, &gd);
+  if (gdev) FKV_CUDA(cudaMemcpy(gids.data(), gpu_block_ids, 8 * nb, cudaMemcpyDeviceToHost));
+  else std::memcpy(gids.data(), gpu_block_ids, 8 * nb);
+  const int64_t gbs = (layout->gpu_block_stride_in_bytes / 8) * 8;
+  const int64_t gkv = (layout->gpu_kv_stride_in_bytes / 8) * 8;
+  const int64_t gpu_extent = (layout->is_mla ? 0 : gkv) + (layout->chunk_size_in_bytes / 16) * 16;
+  for (int64_t i = 0; i < nb; ++i) {
+    const int64_t gi = gids[i];
+    if (gi < 0 || gi >= (1ll << 31))
+      return fail(FKV_ERR_OUT_OF_RANGE, "gpu block id out of [0, 2^31) at index " + std::to_string(i));
+    if (layout->gpu_layer_bytes > 0 && gi * gbs + gpu_extent > layout->gpu_layer_bytes)
+      return fail(FKV_ERR_OUT_OF_RANGE, "gpu block id " + std::to_string(gi) + " at index " +
+                                            std::to_string(i) + " addresses past the gpu layer");
+  }
+  const uint64_t lslots = pow2_at_least(2 * (uint64_t)nb);
+  size_t off = 0;
+  auto carve = [&](size_t bytes) { const size_t at = off; off = al16(off + bytes); return at; };
+  const size_t o_hash = carve(8 * nb), o_bc = carve(nb), o_bs = carve(nb), o_phys = carve(8 * nb),
+               o_lslot = carve(4 * nb), o_lkeys = carve(8 * lslots), o_insc = carve(4 * lslots),
+               o_inss = carve(4 * lslots), o_scpu = carve(8 * lslots), o_off = carve(8 * (num_seqs + 1)),
+               o_gid = carve(8 * nb), o_res = carve(32 * (size_t)num_seqs), o_cpu = carve(8 * nb),
+               o_ssd = carve(8 * nb), o_d2hg = carve(8 * nb), o_d2hc = carve(8 * nb), o_newc = carve(8 * nb),
+               o_news = carve(8 * nb), o_slotc = carve(8 * nb), o_slots = carve(8 * nb), o_cnt = carve(16);
+  Scratch sc, tok;
+  sc.s = s;
+  if (int rc = scratch_alloc(cpu->device, off, s, (void **)&sc.base)) return rc;
+  char *b = sc.base;
+  auto I64 = [&](size_t o) { return reinterpret_cast<int64_t *>(b + o); };
+  uint64_t *hashes = reinterpret_cast<uint64_t *>(b + o_hash);
+  int64_t *counts = I64(o_cnt);
+  if (int rc = hash_batch(cpu, token_ids, seq_offsets, num_seqs, hashes, s, tok)) return rc;
+  const size_t up_off = 8 * (num_seqs + 1);
+  const size_t down_res = 32 * (size_t)num_seqs, down = down_res + 24 * nb + 16 * kStateWords;
+  if (int rc = ensure_pin(cpu, std::max(up_off + 8 * nb, down))) return rc;
+  std::memcpy(cpu->pin, blk.data(), up_off);
+  std::memcpy(cpu->pin + up_off, gids.data(), 8 * nb);
+  FKV_CUDA(cudaMemcpyAsync(b + o_off, cpu->pin, up_off, cudaMemcpyHostToDevice, s));
+  FKV_CUDA(cudaMemcpyAsync(b + o_gid, cpu->pin + up_off, 8 * nb, cudaMemcpyHostToDevice, s));
+  FKV_CUDA(cudaMemsetAsync(b + o_lkeys, 0xff, 8 * lslots, s));
+  FKV_CUDA(cudaMemsetAsync(b + o_insc, 0x7f, 4 * lslots, s));
+  FKV_CUDA(cudaMemsetAsync(b + o_inss, 0x7f, 4 * lslots, s));
+  FKV_CUDA(cudaMemsetAsync(b + o_cpu, 0xff, 8 * nb, s));
+  FKV_CUDA(cudaMemsetAsync(b + o_ssd, 0xff, 8 * nb, s));
+  FKV_CUDA(cudaMemsetAsync(counts, 0, 16, s));
+  const Table tc = cpu->table(), ts = ssd->table();
+  put_lookup_kernel<<<grid_for(nb), 256, 0, s>>>(tc, hashes, nb, reinterpret_cast<uint8_t *>(b + o_bc),
+                                                  reinterpret_cast<uint64_t *>(b + o_lkeys), lslots - 1,
+                                                  64 - log2u(lslots), reinterpret_cast<int32_t *>(b + o_lslot),
+                                                  cpu->state);
+  FKV_CUDA(cudaGetLastError());
+  tier_lookup_kernel<<<grid_for(nb), 256, 0, s>>>(tc, hashes, nb, reinterpret_cast<uint8_t *>(b + o_bc), I64(o_phys));
+  FKV_CUDA(cudaGetLastError());
+  tier_lookup_kernel<<<grid_for(nb), 256, 0, s>>>(ts, hashes, nb, reinterpret_cast<uint8_t *>(b + o_bs), nullptr);
+  FKV_CUDA(cudaGetLastError());
+  const PoolRef pc{cpu->free_mask, cpu->mask_bytes, cpu->free_ids, cpu->state};
+  const PoolRef ps{ssd->free_mask, ssd->mask_bytes, ssd->free_ids, ssd->state};
+  put2_decide_kernel<<<1, 32, 0, s>>>(num_seqs, I64(o_off), reinterpret_cast<uint8_t *>(b + o_bc),
+                                      reinterpret_cast<uint8_t *>(b + o_bs), I64(o_phys),
+                                      reinterpret_cast<int32_t *>(b + o_lslot), reinterpret_cast<int32_t *>(b + o_insc),
+                                      reinterpret_cast<int32_t *>(b + o_inss), I64(o_scpu), I64(o_gid), pc, ps,
+                                      I64(o_res), I64(o_cpu), I64(o_ssd), I64(o_d2hg), I64(o_d2hc), I64(o_newc),
+                                      I64(o_news), counts);
+  FKV_CUDA(cudaGetLastError());
+  put_insert_kernel<<<grid_for(nb), 256, 0, s>>>(tc, hashes, I64(o_newc), I64(o_cpu), counts, I64(o_slotc), cpu->state);
+  FKV_CUDA(cudaGetLastError());
+  put_insert_kernel<<<grid_for(nb), 256, 0, s>>>(ts, hashes, I64(o_news), I64(o_ssd), counts + 1, I64(o_slots),
+                                                  ssd->state);
+  FKV_CUDA(cudaGetLastError());
+  note_launch(6);
+  char *pin = cpu->pin;
+  FKV_CUDA(cudaMemcpyAsync(pin, b + o_res, down_res, cudaMemcpyDeviceToHost, s));
+  FKV_CUDA(cudaMemcpyAsync(pin + down_res, b + o_cpu, 8 * nb, cudaMemcpyDeviceToHost, s));
+  FKV_CUDA(cudaMemcpyAsync(pin + down_res + 8 * nb, b + o_ssd, 8 * nb, cudaMemcpyDeviceToHost, s));
+  FKV_CUDA(cudaMemcpyAsync(pin + down_res + 16 * nb, hashes, 8 * nb, cudaMemcpyDeviceToHost, s));
+  FKV_CUDA(cudaMemcpyAsync(pin + down_res + 24 * nb, cpu->state, 8 * kStateWords, cudaMemcpyDeviceToHost, s));
+  FKV_CUDA(cudaMemcpyAsync(pin + down_res + 24 * nb + 8 * kStateWords, ssd->state, 8 * kStateWords,
+                           cudaMemcpyDeviceToHost, s));
+  fkv_transfer_desc d = *layout;
+  d.is_host_to_device = 0;
+  if (int rc = transfer_enqueue_device_ids(d, I64(o_d2hg), I64(o_d2hc), counts, nb, cpu->num_blocks - 1, s))
+    return rc;
+  if (mark_ready) {
+    mark_slots_ready_kernel<<<grid_for(nb), 256, 0, s>>>(tc, I64(o_slotc), counts);
+    FKV_CUDA(cudaGetLastError());
+    note_launch();
+  }
+  FKV_CUDA(cudaStreamSynchronize(s));
+  int64_t st_c[kStateWords], st_s[kStateWords];
+  std::memcpy(st_c, pin + down_res + 24 * nb, 8 * kStateWords);
+  std::memcpy(st_s, pin + down_res + 24 * nb + 8 * kStateWords, 8 * kStateWords);
+  if (int rc = take_device_error(cpu, s, st_c)) return rc;
+  if (int rc = take_device_error(ssd, s, st_s)) return rc;
+  const int64_t *res = reinterpret_cast<const int64_t *>(pin);
+  for (int r = 0; r < num_seqs; ++r) {
+    num_skipped[r] = res[4 * r];
+    num_transferred[r] = res[4 * r + 1];
+    num_to_ssd[r] = res[4 * r + 2];
+  }
+  if (cpu_block_ids) std::memcpy(cpu_block_ids, pin + down_res, 8 * nb);
+  if (ssd_block_ids) std::memcpy(ssd_block_ids, pin + down_res + 8 * nb, 8 * nb);
+  if (block_hashes) std::memcpy(block_hashes, pin + down_res + 16 * nb, 8 * nb);
   return FKV_OK;
 }
 

@@ -483,6 +483,27 @@ int fkv_cache_index_put(fkv_cache_index *ci, const int64_t *token_ids, const int
                         int64_t *num_transferred, int64_t *cpu_block_ids, uint64_t *block_hashes,
                         void *stream);
 
+/* put of each sequence with the SSD tier on (cache_engine.py:787-902):
+ * `cpu` and `ssd` are the two tiers' indexes (same device and
+ * tokens_per_block).  Per sequence: m_c / m_s leading blocks cached in the
+ * CPU / SSD tier; the n - m_c others are copied D2H into new CPU blocks
+ * (inserted, ready after the copy when mark_ready); the n - m_s blocks the
+ * SSD tier lacks get new SSD blocks (inserted, not ready).  Both takes must
+ * succeed, else the put is empty and gives both allocations back.  Out:
+ * num_skipped (m_c), num_transferred (D2H blocks), num_to_ssd (SSD blocks);
+ * per block of the batch: cpu_block_ids (the CPU block holding it when it
+ * is copied or goes to the SSD tier, else -1), ssd_block_ids (its new SSD
+ * block, else -1), block_hashes.  The caller then writes each
+ * (cpu_block_ids[i] -> ssd_block_ids[i]) pair to the SSD tier
+ * (fkv_transfer_kv_blocks_ssd) and marks those blocks ready in `ssd`
+ * (fkv_cache_index_set_ready), the H2DISK op and callback of the reference's
+ * put graph.  Synchronous. */
+int fkv_cache_index_put2(fkv_cache_index *cpu, fkv_cache_index *ssd, const int64_t *token_ids,
+                         const int64_t *seq_offsets, int num_seqs, const int64_t *gpu_block_ids,
+                         const fkv_transfer_desc *layout, int mark_ready, int64_t *num_skipped,
+                         int64_t *num_transferred, int64_t *num_to_ssd, int64_t *cpu_block_ids,
+                         int64_t *ssd_block_ids, uint64_t *block_hashes, void *stream);
+
 /* get of each sequence (CPU tier, cache_engine.py:150-219, 412-548, SSD
  * off): the mask selects full blocks [block_starts[s], n_s) (block_starts
  * NULL: all from 0); of the sequence's first num_ready matched blocks, those

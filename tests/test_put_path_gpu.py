@@ -451,3 +451,70 @@ def test_layerwise_get_completes_group_by_group():
         ci.get(gt[:1], dst[:1], pools.layout, layer_granularity=3)
     assert e.value.code == FKV_ERR_INVALID_ARG
     ci.close()
+
+
+@pytest.mark.parametrize("name", [n for n, sc in golden().items() if sc.get("num_ssd_blocks")])
+def test_two_tier_put_matches_the_reference(tmp_path, name):
+    """Puts with the SSD tier on (cache_engine.py:787-902), from the
+    reference's own GlobalCacheEngine run with its SSD tier: each put's D2H
+    and H2DISK block lists, the gets' H2D lists, both tiers' totals, and the
+    bytes on the SSD (read back from the files, compared with the CPU blocks
+    they were written from)."""
+    from flexkv_b200.cache_index import SsdTier
+    from flexkv_b200.layout import KVCacheLayout, KVCacheLayoutType
+    from flexkv_b200.ssd import SsdStrides, allocate_ssd_files
+    sc = golden()[name]
+    tpb, n_cpu, n_ssd = sc["tpb"], sc["num_cpu_blocks"], sc["num_ssd_blocks"]
+    case = Case("golden", 2, 1, 8, tpb, 256, n_cpu)
+    pools = Pools(case)
+    cpu_layout = case.cpu_layout_obj()
+    ssd_layout = KVCacheLayout(KVCacheLayoutType.LAYERWISE, 2, n_ssd, tpb, 1, 8, False)
+    files, per_file = allocate_ssd_files(ssd_layout, 2, str(tmp_path / "ssd"), max_blocks_per_file=n_ssd)
+    ioctx = c_ext.SSDIOCTX(files, len(files), 0, 0)
+    strides = SsdStrides.of(cpu_layout, ssd_layout, sum(len(v) for v in files.values()), 2)
+    ci, si = CpuCacheIndex(n_cpu, tpb), CpuCacheIndex(n_ssd, tpb)
+    ssd = SsdTier(si, ioctx, strides, 2, per_file)
+    written = []
+    for b, batch in enumerate(sc["batches"]):
+        toks = [np.array(q["tokens"], dtype=np.int64) for q in batch]
+        gids = [np.array(q["gpu_blocks"], dtype=np.int64) for q in batch]
+        res = ci.put_two_tier(ssd, toks, gids, pools.layout, mark_ready=sc["complete_each_batch"])
+        for r, want in enumerate(sc["results"][b]):
+            ops = []
+            if int(res.num_transferred[r]):
+                ops.append(["D2H", res.gpu_blocks[r].tolist(), res.cpu_blocks[r].tolist()])
+                if int(res.num_to_ssd[r]):
+                    ops.append(["H2DISK", res.h2disk_cpu_blocks[r].tolist(), res.ssd_blocks[r].tolist()])
+                    written += list(zip(res.h2disk_cpu_blocks[r].tolist(), res.ssd_blocks[r].tolist()))
+            assert (int(res.num_skipped[r]), int(res.num_transferred[r]), ops) == \
+                (want["skipped"], want["transferred"], want["ops"]), f"batch {b} put {r}"
+        for i, gq in enumerate(sc["gets"][b]):
+            got = ci.get([np.array(gq["tokens"], dtype=np.int64)], [np.array(gq["gpu_blocks"], dtype=np.int64)],
+                         pools.layout, [gq["block_start"]])
+            ops = [["H2D", got.cpu_blocks[0].tolist(), got.gpu_blocks[0].tolist()]] if int(got.num_transferred[0]) else []
+            assert ops == gq["ops"], f"batch {b} get {i}"
+        sc_c, sc_s = ci.stats(), si.stats()
+        assert (sc_c["num_free_blocks"], sc_c["total_cached_blocks"], sc_c["total_ready_blocks"],
+                sc_s["num_free_blocks"], sc_s["total_cached_blocks"]) == \
+            (sc["num_free"][b], sc["total_cached"][b], sc["total_ready"][b], sc["ssd_num_free"][b],
+             sc["ssd_total_cached"][b])
+    assert written
+    # the SSD holds what the CPU blocks held: read it back into a second pool at the same CPU blocks
+    back = torch.zeros_like(pools.cpu).pin_memory()
+    cids = np.array([c for c, _ in written], dtype=np.int64)
+    sids = np.array([s_ for _, s_ in written], dtype=np.int64)
+    c_ext.transfer_kv_blocks_ssd(ioctx, [0, 1], back.data_ptr(), sids, cids, strides.cpu_layer_stride_in_bytes,
+                                 strides.cpu_kv_stride_in_bytes, strides.ssd_layer_stride_in_bytes,
+                                 strides.ssd_kv_stride_in_bytes, strides.chunk_size_in_bytes,
+                                 strides.block_stride_in_bytes, True, per_file,
+                                 cpu_pool_bytes=back.numel() * back.element_size())
+    st = case.strides()
+    a, w = pools.cpu.numpy(), back.numpy()
+    for c in cids.tolist():
+        for l in range(2):
+            for k in range(2):
+                o = l * st["cpu_layer"] + k * st["cpu_kv"] + c * st["cpu_block"]
+                assert np.array_equal(a[o:o + st["cpu_chunk"]], w[o:o + st["cpu_chunk"]]), (c, l, k)
+    ioctx.close()
+    ci.close()
+    si.close()
