@@ -93,3 +93,61 @@ def random_history(seed, n_ops, tpb, pool_blocks):
 @pytest.mark.parametrize("seed,tpb,pool", [(1, 2, 4000), (2, 4, 4000), (3, 1, 4000), (4, 4, 120), (5, 2, 60)])
 def test_tree_walk_equals_leading_present_blocks(seed, tpb, pool):
     random_history(seed, 300, tpb, pool)
+
+
+class FlatTwoTier:
+    """Both tiers as flat maps, with the two-tier put rule: D2H the blocks
+    the CPU tier lacks, H2DISK the ones the SSD tier lacks, both takes or
+    neither."""
+
+    def __init__(self, n_cpu, n_ssd, tpb):
+        self.c = FlatModel(n_cpu, tpb)
+        self.s = FlatModel(n_ssd, tpb)
+
+    def put(self, tok):
+        h = self.c.hashes(tok)
+        n = len(h)
+        m_c = self.c.match(h)[0]
+        m_s = self.s.match(h)[0]
+        k, f2 = n - m_c, n - m_s
+        if k == 0:
+            return (0, 0, [], []), [], []
+        got_c = self.c.pool.allocate(min(k, self.c.pool.num_free))
+        got_s = self.s.pool.allocate(min(f2, self.s.pool.num_free))
+        if len(got_c) < k or len(got_s) < f2:
+            self.c.pool.recycle(got_c)
+            self.s.pool.recycle(got_s)
+            return (0, 0, [], []), [], []
+        for x, c in zip(h[m_c:], got_c.tolist()):
+            self.c.map[x] = [c, False]
+        for x, c in zip(h[m_s:], got_s.tolist()):
+            self.s.map[x] = [c, False]
+        return (m_c, k, got_c.tolist(), got_s.tolist()), h[m_c:], h[m_s:]
+
+
+@pytest.mark.parametrize("seed,n_cpu,n_ssd", [(7, 3000, 5000), (8, 200, 5000), (9, 3000, 150)])
+def test_two_tier_tree_walks_equal_flat_maps(seed, n_cpu, n_ssd):
+    tpb = 2
+    rng = np.random.default_rng(seed)
+    tt = CI.TwoTier(n_cpu, n_ssd, tpb)
+    flat = FlatTwoTier(n_cpu, n_ssd, tpb)
+    seen, pending = [], []
+    for step in range(300):
+        if seen and rng.random() < 0.6:
+            base = seen[rng.integers(len(seen))]
+            tok = np.concatenate([base[:int(rng.integers(0, len(base) + 1))],
+                                  rng.integers(0, 20, int(rng.integers(0, 8 * tpb)))]).astype(np.int64)
+        else:
+            tok = rng.integers(0, 20, int(rng.integers(0, 12 * tpb))).astype(np.int64)
+        seen.append(tok)
+        r = tt.put(tok, np.arange(len(tok) // tpb))
+        got, ins_c, ins_s = flat.put(tok)
+        assert (r.num_skipped, r.num_transferred, r.cpu_blocks.tolist(), r.ssd_blocks.tolist()) == got, step
+        pending.append((r, ins_c, ins_s))
+        while pending and rng.random() < 0.5:
+            r2, c2, s2 = pending.pop(int(rng.integers(len(pending))))
+            tt.complete(r2)
+            flat.c.complete(c2)
+            flat.s.complete(s2)
+    assert (tt.cpu.pool.num_free, tt.ssd.pool.num_free) == (flat.c.pool.num_free, flat.s.pool.num_free)
+    assert (tt.cpu.tree.total_blocks(), tt.ssd.tree.total_blocks()) == (len(flat.c.map), len(flat.s.map))
