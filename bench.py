@@ -18,15 +18,19 @@ cfg4_qwen2_7b (Qwen2-7B shape, 256 requests of U[1,32] scattered blocks per
 step, mixed get/put, directions overlapped), cfg3_llama3_70b_tp (Llama-3-70B,
 one TP group of --tp ranks driven from one process).
 
-  value  — device-timed GB/s (CUDA events on the launch streams) of plans
-           prepared before the timed region (ids validated, coalesced and
-           resident on the device).
+  value  — device-timed GB/s (CUDA events on the call streams) of every op
+           made through the reference-facing call,
+           c_ext.transfer_kv_blocks, with pinned host id tensors: one
+           synchronous call per op as FlexKV's worker makes it (per-direction
+           streams when the workload overlaps directions), so id validation,
+           coalescing and the id-table upload are inside the timed region.
+           plan_replay beside it runs the same ops from TransferPlans built
+           beforehand, and brackets the SM kernel for the roofline.
   e2e    — GB/s through the public API that replaces FlexKV's
            TransferEngine (flexkv_b200.engine.TransferEngine: one graph per
            op, host id tensors, wall clock; H2D and D2H ops in flight
-           together); per_op_calls beside it is one synchronous
-           c_ext.transfer_kv_blocks call per op, the reference worker's
-           pattern.
+           together); per_op_calls beside it is the wall clock of the value
+           leg.
   extras — link peaks measured live (each rank alone, and all ranks at
            once when N > 1), the duplex rate, and at N = 1 on cfg2 the
            XXH64 hashing, small-op latency, CPU-tier put path (device index
@@ -34,13 +38,18 @@ one TP group of --tp ranks driven from one process).
            SSD-tier measurements.
   --impl reference — the reference's own transfer.cu built from its source
            (oracle/_ref) driven the way its worker drives it: one op at a
-           time, transfer_sms=8, pinned id tensors, synchronous.
+           time, transfer_sms=8, pinned id tensors, synchronous, on pools
+           built the stock way (one flat host tensor, Portable
+           cudaHostRegister); nothing of flexkv_b200 is loaded.
   --hash-only / --ssd-only / --put-only — only that measurement, one JSON
            line (--put-only on the --config shape).
 
 Multi-GPU (torchrun): every rank runs the same per-GPU workload on its own
 GPU and pools (data parallel, no collective on the data path); value is the
-bytes of all ranks over the max-over-ranks time (weak scaling).
+bytes of all ranks over the max-over-ranks time (weak scaling).  The line
+adds each rank's H2D and D2H rates (per_rank) and the box's per-direction
+sums against N x the single-GPU link peak and against the peak measured
+with every rank copying at once (box).
 """
 from __future__ import annotations
 
@@ -244,66 +253,125 @@ def mem_available_bytes() -> int:
     return 0
 
 
+def kv_strides(kind: str, L: int, N: int, tpb: int, H: int, D: int, mla: bool) -> dict:
+    """Element strides of FlexKV's KVCacheLayout (flexkv/common/storage.py:
+    59-149) for a pool of N blocks: LAYERWISE [L, kv, N, tpb, H, D] or
+    BLOCKWISE [N, L, kv, tpb, H, D].  Plain arithmetic, so the reference arm
+    needs nothing of flexkv_b200."""
+    kv = 1 if mla else 2
+    chunk = tpb * H * D
+    if kind == "LAYERWISE":
+        st = {"layer": kv * N * chunk, "kv": N * chunk, "block": chunk}
+    else:
+        st = {"layer": kv * chunk, "kv": chunk, "block": L * kv * chunk}
+    st.update(chunk=chunk, total=L * kv * N * chunk, kv_dim=kv)
+    return st
+
+
+def stock_host_register(t: torch.Tensor) -> None:
+    """Page-lock a host tensor the way FlexKV's worker does: one plain
+    cudaHostRegister with flag 1 (Portable), no huge-page advice
+    (flexkv/transfer/worker.py:35-41)."""
+    rc = torch.cuda.cudart().cudaHostRegister(t.data_ptr(), t.numel() * t.element_size(), 1)
+    if int(getattr(rc, "value", rc)) != 0:
+        raise RuntimeError(f"cudaHostRegister failed with error code {rc}")
+
+
+def stock_host_unregister(t: torch.Tensor) -> None:
+    torch.cuda.cudart().cudaHostUnregister(t.data_ptr())
+
+
+def fit_cpu_blocks(cfg: dict, ws: int, block_bytes: int, override: int = 0) -> int:
+    """The configuration's host pool, scaled down to 55 % of the box's
+    available RAM shared by the ws ranks (and never below two batches)."""
+    if override:
+        return override
+    fit = int(0.55 * mem_available_bytes() / max(ws, 1) / block_bytes)
+    min_blocks = 2 * cfg.get("batch", cfg.get("requests", 1) * cfg.get("max_req_blocks", 1))
+    return cfg["cpu_blocks"] if fit >= cfg["cpu_blocks"] else max(fit, min_blocks)
+
+
 class Setup:
-    """Pools, layouts and per-step ops of one rank."""
+    """Pools, strides and per-step ops of one rank.
+
+    stock=False: the host pool is page-locked by flexkv_b200
+    (c_ext.cudaHostRegister with huge-page advice).  stock=True (the
+    reference arm): the pool is one flat torch tensor, as FlexKV's
+    CPUAllocator.allocate makes it (flexkv/storage/allocator.py:93-113),
+    registered with the worker's plain Portable cudaHostRegister; nothing of
+    flexkv_b200 is imported."""
 
     def __init__(self, cfg: dict, layout: str, ws: int, local: int, cpu_blocks_override: int = 0,
-                 gpu_alloc: str = "per-layer"):
-        from flexkv_b200 import c_ext
-        from flexkv_b200.layout import KVCacheLayout, KVCacheLayoutType
+                 gpu_alloc: str = "per-layer", stock: bool = False):
         self.cfg = cfg
+        self.stock = stock
         self.mla = cfg.get("mla", False)
         self.kv = 1 if self.mla else 2
         L, H, D, tpb = cfg["layers"], cfg["heads"], cfg["head_dim"], cfg["tpb"]
-        self.chunk = tpb * H * D * 2
-        self.block_bytes = L * self.kv * self.chunk
-        cpu_blocks = cfg["cpu_blocks"]
-        fit = int(0.55 * mem_available_bytes() / max(ws, 1) / self.block_bytes)
-        min_blocks = 2 * cfg.get("batch", cfg.get("requests", 1) * cfg.get("max_req_blocks", 1))
-        if cpu_blocks_override:
-            cpu_blocks = cpu_blocks_override
-        elif fit < cpu_blocks:
-            cpu_blocks = max(fit, min_blocks)
-        self.cpu_blocks = cpu_blocks
-        self.gpu_layout = KVCacheLayout(KVCacheLayoutType.LAYERWISE, L, cfg["gpu_blocks"], tpb, H, D,
-                                        self.mla)
-        self.cpu_layout = KVCacheLayout(KVCacheLayoutType[layout], L, cpu_blocks, tpb, H, D, self.mla)
-        per = self.gpu_layout.div_layer(L)
         e = 2
-        self.g_kv, self.g_blk = per.get_kv_stride() * e, per.get_block_stride() * e
-        self.c_kv = self.cpu_layout.get_kv_stride() * e
-        self.c_layer = self.cpu_layout.get_layer_stride() * e
-        self.c_blk = self.cpu_layout.get_block_stride() * e
-        self.gpu_layer_bytes = per.get_total_elements() * e
+        self.chunk = tpb * H * D * e
+        self.block_bytes = L * self.kv * self.chunk
+        self.cpu_blocks = cpu_blocks = fit_cpu_blocks(cfg, ws, self.block_bytes, cpu_blocks_override)
+        self.layout = layout
+        g = kv_strides("LAYERWISE", 1, cfg["gpu_blocks"], tpb, H, D, self.mla)  # one layer
+        c = kv_strides(layout, L, cpu_blocks, tpb, H, D, self.mla)
+        self.g_kv, self.g_blk = g["kv"] * e, g["block"] * e
+        self.c_kv, self.c_layer, self.c_blk = c["kv"] * e, c["layer"] * e, c["block"] * e
+        self.gpu_layer_bytes = g["total"] * e
+        layer_shape = (self.kv, cfg["gpu_blocks"], tpb, H, D)
         dev = torch.device(f"cuda:{local}")
         t0 = time.time()
         self.layers = []
         self.gpu_alloc = gpu_alloc
         if gpu_alloc == "contiguous":
             # One allocation viewed as per-layer [kv, N, tpb, H, D] tensors.
-            self._gpu_base = torch.empty((L,) + tuple(per.kv_shape), dtype=torch.bfloat16, device=dev)
+            self._gpu_base = torch.empty((L,) + layer_shape, dtype=torch.bfloat16, device=dev)
             self._gpu_base.normal_()
             self.layers = [self._gpu_base[l] for l in range(L)]
         else:
             for _ in range(L):
-                t = torch.empty(per.kv_shape, dtype=torch.bfloat16, device=dev)
+                t = torch.empty(layer_shape, dtype=torch.bfloat16, device=dev)
                 t.normal_()
                 self.layers.append(t)
         self.ptrs = torch.tensor([t.data_ptr() for t in self.layers], dtype=torch.int64)
         t1 = time.time()
-        cpu_bytes = self.cpu_layout.get_total_elements() * e
+        cpu_bytes = c["total"] * e
         self.cpu = torch.empty(cpu_bytes // 2, dtype=torch.bfloat16)
-        c_ext.cudaHostRegister(self.cpu, advise_hugepages=True)
+        if stock:
+            stock_host_register(self.cpu)
+        else:
+            from flexkv_b200 import c_ext
+            c_ext.cudaHostRegister(self.cpu, advise_hugepages=True)
         t2 = time.time()
         log(f"[rank{local}] gpu pool {L}x{self.gpu_layer_bytes / 2**30:.2f} GiB in {t1 - t0:.1f}s, "
-            f"cpu pool {cpu_bytes / 2**30:.1f} GiB registered in {t2 - t1:.1f}s")
+            f"cpu pool {cpu_bytes / 2**30:.1f} GiB registered in {t2 - t1:.1f}s"
+            + (" (stock: flat tensor, Portable cudaHostRegister)" if stock else ""))
         self.steps = rank_steps(cfg, cpu_blocks, local)
         self.step_bytes = {d: sum(len(g) for g, c, h in self.steps[0] if h == (d == "h2d")) * self.block_bytes
                            for d in ("h2d", "d2h")}
 
+    @property
+    def gpu_layout(self):
+        """flexkv_b200's KVCacheLayout of the GPU pool (our arm only)."""
+        from flexkv_b200.layout import KVCacheLayout, KVCacheLayoutType
+        c = self.cfg
+        return KVCacheLayout(KVCacheLayoutType.LAYERWISE, c["layers"], c["gpu_blocks"], c["tpb"], c["heads"],
+                             c["head_dim"], self.mla)
+
+    @property
+    def cpu_layout(self):
+        """flexkv_b200's KVCacheLayout of the host pool (our arm only)."""
+        from flexkv_b200.layout import KVCacheLayout, KVCacheLayoutType
+        c = self.cfg
+        return KVCacheLayout(KVCacheLayoutType[self.layout], c["layers"], self.cpu_blocks, c["tpb"], c["heads"],
+                             c["head_dim"], self.mla)
+
     def close(self):
-        from flexkv_b200 import c_ext
-        c_ext.cudaHostUnregister(self.cpu)
+        if self.stock:
+            stock_host_unregister(self.cpu)
+        else:
+            from flexkv_b200 import c_ext
+            c_ext.cudaHostUnregister(self.cpu)
 
 
 def mode_kwargs(args):
@@ -912,7 +980,27 @@ def measure_engine(S, args, K, W, ws):
     return dt
 
 
+def gather_over_ranks(ws, xs):
+    """Every rank's list of floats (same length on all ranks), rank-major;
+    timing plumbing only, never data."""
+    if ws == 1:
+        return [list(xs)]
+    import torch.distributed as dist
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor(list(xs), dtype=torch.float64, device=dev)
+    out = [torch.empty_like(t) for _ in range(ws)]
+    dist.all_gather(out, t)
+    return [o.cpu().tolist() for o in out]
+
+
 def run_ours(args, ws, rank, local, cfg, layout, with_hash):
+    """value: every op through the reference-facing call
+    (c_ext.transfer_kv_blocks with host id tensors, one synchronous call per
+    op as FlexKV's worker makes it; per-direction streams when the workload
+    overlaps directions), device-timed with CUDA events on the call's
+    stream.  plan_replay: the same ops as TransferPlans built before the
+    timed region (it also brackets the SM kernel alone for the roofline).
+    e2e: the same steps through flexkv_b200.engine.TransferEngine."""
     from flexkv_b200 import c_ext
     S = Setup(cfg, layout, ws, local, args.cpu_blocks, args.gpu_alloc)
     kw, use_ce = mode_kwargs(args)
@@ -921,6 +1009,8 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
                                  S.cpu, S.c_kv, S.c_layer, S.c_blk, S.chunk, 0, args.transfer_sms,
                                  h2d, use_ce, S.mla, gpu_layer_bytes=S.gpu_layer_bytes, **kw)
               for g, c, h2d in ops] for ops in S.steps]
+    host_ops = [[(torch.from_numpy(g).pin_memory(), torch.from_numpy(c).pin_memory(), h)
+                 for g, c, h in ops] for ops in S.steps]
     stream = torch.cuda.current_stream()
     side = torch.cuda.Stream()
     # Concurrent workloads: each direction alternates over two streams (as
@@ -936,16 +1026,27 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
             e.record(stream)
         return evs
 
-    def run_step(k, rec=None):
-        """Enqueue step k; rec collects events for timing (None = untimed)."""
-        ops, ps = S.steps[k % len(S.steps)], plans[k % len(plans)]
+    def new_rec(k, kernels):
+        nops = len(S.steps[(W + k) % len(S.steps)])
+        e = new_events(4 + 2 * nops + (2 * nops if kernels else 0))
+        rec = {"start": e[0], "end": e[1], "end_main": e[2], "end_side": e[3],
+               "op": [(e[4 + 2 * i], e[5 + 2 * i]) for i in range(nops)]}
+        if kernels:
+            b = 4 + 2 * nops
+            rec["k"] = [(e[b + 2 * i], e[b + 2 * i + 1]) for i in range(nops)]
+        return rec
+
+    def run_step(k, rec=None, via_plans=False):
+        """Enqueue step k through the per-op call (or the prebuilt plans);
+        rec collects events for timing (None = untimed)."""
+        ops, ps, hops = S.steps[k % len(S.steps)], plans[k % len(plans)], host_ops[k % len(host_ops)]
         start = rec["start"] if rec is not None else torch.cuda.Event()
         start.record(stream)
         if conc:
             for q in pool_h[1:] + pool_d:
                 q.wait_event(start)
         nh = nd = 0
-        for i, ((g, c, h2d), p) in enumerate(zip(ops, ps)):
+        for i, (g, c, h2d) in enumerate(hops):
             if not conc:
                 st = stream
             elif h2d:
@@ -954,10 +1055,16 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
                 st, nd = pool_d[nd % 2], nd + 1
             if rec is not None and not conc:
                 rec["op"][i][0].record(st)
-            if rec is not None and track_kernels:
-                p.execute(stream=st, kernel_events=(rec["k"][i][0], rec["k"][i][1]))
+            if via_plans:
+                if rec is not None and "k" in rec:
+                    ps[i].execute(stream=st, kernel_events=(rec["k"][i][0], rec["k"][i][1]))
+                else:
+                    ps[i].execute(stream=st)
             else:
-                p.execute(stream=st)
+                with torch.cuda.stream(st):
+                    c_ext.transfer_kv_blocks(g, S.ptrs, S.g_kv, S.g_blk, c, S.cpu, S.c_kv, S.c_layer, S.c_blk,
+                                             S.chunk, 0, args.transfer_sms, h2d, use_ce, S.mla,
+                                             synchronous=not conc, gpu_layer_bytes=S.gpu_layer_bytes, **kw)
             if rec is not None and not conc:
                 rec["op"][i][1].record(st)
         if conc:
@@ -974,68 +1081,81 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
         if rec is not None:
             rec["end"].record(stream)
 
+    def dir_times(recs):
+        """Per-direction device ms of each timed step."""
+        out = {"h2d": [], "d2h": []}
+        for k, rec in enumerate(recs):
+            ops = S.steps[(W + k) % len(S.steps)]
+            if conc:
+                out["h2d"].append(rec["start"].elapsed_time(rec["end_main"]))
+                out["d2h"].append(rec["start"].elapsed_time(rec["end_side"]))
+            else:
+                for d in ("h2d", "d2h"):
+                    out[d].append(sum(rec["op"][i][0].elapsed_time(rec["op"][i][1])
+                                      for i, op in enumerate(ops) if op[2] == (d == "h2d")))
+        return out
+
+    sb = S.step_bytes
+    step_total = sb["h2d"] + sb["d2h"]
+
+    def rates(dms):
+        return {d: (sb[d] / (statistics.mean(dms[d]) / 1e3) / 1e9 if sb[d] and statistics.mean(dms[d]) > 0
+                    else 0.0) for d in ("h2d", "d2h")}
+
     for k in range(W):
         run_step(k)
+        run_step(k, via_plans=True)
     torch.cuda.synchronize()
-    recs = []
-    for k in range(K):
-        nops = len(S.steps[(W + k) % len(S.steps)])
-        e = new_events(4 + 2 * nops + (2 * nops if track_kernels else 0))
-        rec = {"start": e[0], "end": e[1], "end_main": e[2], "end_side": e[3],
-               "op": [(e[4 + 2 * i], e[5 + 2 * i]) for i in range(nops)]}
-        if track_kernels:
-            b = 4 + 2 * nops
-            rec["k"] = [(e[b + 2 * i], e[b + 2 * i + 1]) for i in range(nops)]
-        recs.append(rec)
+    recs = [new_rec(k, False) for k in range(K)]
+    precs = [new_rec(k, track_kernels) for k in range(K)]
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
     with sampler:
+        # value: the per-op call path, host id tensors, device-timed
         barrier(ws)
         launches0 = c_ext.kernel_launch_count()
+        w0 = time.perf_counter()
         for k in range(K):
             run_step(W + k, recs[k])
         torch.cuda.synchronize()
+        calls_wall_s = time.perf_counter() - w0
         launches = c_ext.kernel_launch_count() - launches0
         barrier(ws)
         elapsed_ms = recs[0]["start"].elapsed_time(recs[-1]["end"])
-        # e2e through the reference-facing call with host id tensors
-        host_ops = [[(torch.from_numpy(g).pin_memory(), torch.from_numpy(c).pin_memory(), h)
-                     for g, c, h in ops] for ops in S.steps]
-
-        def e2e_step(k):
-            for g, c, h2d in host_ops[k % len(host_ops)]:
-                st = stream if (h2d or not conc) else side
-                with torch.cuda.stream(st):
-                    c_ext.transfer_kv_blocks(g, S.ptrs, S.g_kv, S.g_blk, c, S.cpu, S.c_kv,
-                                             S.c_layer, S.c_blk, S.chunk, 0, args.transfer_sms, h2d,
-                                             use_ce, S.mla, synchronous=not conc, **kw)
-            if conc:
-                torch.cuda.synchronize()
-
-        for k in range(W):
-            e2e_step(k)
+        # plan replay: the same ops from TransferPlans built before timing
         barrier(ws)
-        w0 = time.perf_counter()
         for k in range(K):
-            e2e_step(W + k)
+            run_step(W + k, precs[k], via_plans=True)
         torch.cuda.synchronize()
-        e2e_s = time.perf_counter() - w0
         barrier(ws)
-        # The same steps through the TransferEngine: one single-op graph per
-        # op, all submitted, then polled until every graph has finished.
+        plan_ms = precs[0]["start"].elapsed_time(precs[-1]["end"])
+        # e2e: the same steps through the TransferEngine, one single-op
+        # graph per op, all submitted, then polled until every graph ended.
         e2e_engine_s = measure_engine(S, args, K, W, ws)
     clocks = sampler.summary()
+    dir_ms = dir_times(recs)
+    rate = rates(dir_ms)
+    plan_rate = rates(dir_times(precs))
+    kern_ms = {"h2d": [], "d2h": []}
+    if track_kernels:
+        for k, rec in enumerate(precs):
+            for i, op in enumerate(S.steps[(W + k) % len(S.steps)]):
+                kern_ms["h2d" if op[2] else "d2h"].append(rec["k"][i][0].elapsed_time(rec["k"][i][1]))
+
     extras = {}
+    lp_alone = lp_conc = None
     if not args.no_extras:
         for r in range(ws):  # one rank at a time: each GPU's own link
             if r == rank:
-                extras["link_peak_measured"] = measure_link_peaks(S, stream)
+                lp_alone = measure_link_peaks(S, stream)
             barrier(ws)
         if ws > 1:  # every rank at once: the host side shared by all links
-            lpc = measure_link_peaks(S, stream, sync=lambda: barrier(ws))
-            lpc["how"] = ("contiguous cudaMemcpyAsync from each rank's pinned pool with every rank copying "
-                          "at once (rank 0's rates), median of 3")
-            extras["link_peak_concurrent"] = lpc
+            lp_conc = measure_link_peaks(S, stream, sync=lambda: barrier(ws))
+        extras["link_peak_measured"] = dict(lp_alone)
+        if lp_conc is not None:
+            extras["link_peak_concurrent"] = dict(
+                lp_conc, how="contiguous cudaMemcpyAsync from each rank's pinned pool with every rank "
+                             "copying at once (rank 0's rates), median of 3")
         if not conc and cfg["kind"] == "batch":
             ts = []  # the same steps with both directions in flight together
             for k in range(max(K, 3)):
@@ -1052,8 +1172,7 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
                 b.record(stream)
                 torch.cuda.synchronize()
                 ts.append(a.elapsed_time(b))
-            extras["duplex"] = {"value": round(sum(S.step_bytes.values()) / statistics.median(ts) / 1e6, 2),
-                                "unit": "GB/s",
+            extras["duplex"] = {"value": round(step_total / statistics.median(ts) / 1e6, 2), "unit": "GB/s",
                                 "how": "the same steps with the H2D and the D2H batch in flight together on two streams"}
         if with_hash and rank == 0 and ws == 1:
             extras["hash"] = measure_hash()
@@ -1072,74 +1191,64 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
             except Exception as e:  # noqa: BLE001
                 extras["ssd"] = {"error": f"{type(e).__name__}: {e}"}
 
-    # Per-direction rates.
-    dir_ms = {"h2d": [], "d2h": []}
-    kern_ms = {"h2d": [], "d2h": []}
-    for k, rec in enumerate(recs):
-        ops = S.steps[(W + k) % len(S.steps)]
-        if conc:
-            dir_ms["h2d"].append(rec["start"].elapsed_time(rec["end_main"]))
-            dir_ms["d2h"].append(rec["start"].elapsed_time(rec["end_side"]))
-        else:
-            for d in ("h2d", "d2h"):
-                dir_ms[d].append(sum(rec["op"][i][0].elapsed_time(rec["op"][i][1])
-                                     for i, op in enumerate(ops) if op[2] == (d == "h2d")))
-        if track_kernels:
-            for i, op in enumerate(ops):
-                kern_ms["h2d" if op[2] else "d2h"].append(rec["k"][i][0].elapsed_time(rec["k"][i][1]))
-    sb = S.step_bytes
-    rate = {d: sb[d] / (statistics.mean(dir_ms[d]) / 1e3) / 1e9 for d in ("h2d", "d2h")
-            if sb[d] and statistics.mean(dir_ms[d]) > 0}
-    step_total = sb["h2d"] + sb["d2h"]
+    # Every rank's figures, for the per-GPU and box-level lines.
+    keys = ("h2d", "d2h", "duplex_total")
+    mine = [rate["h2d"], rate["d2h"]]
+    mine += [float(lp_alone[k]) if lp_alone else 0.0 for k in keys]
+    mine += [float(lp_conc[k]) if lp_conc else 0.0 for k in keys]
+    allr = gather_over_ranks(ws, mine)
     max_elapsed = max_over_ranks(ws, elapsed_ms)
-    max_e2e = max_over_ranks(ws, e2e_s)
+    max_plan = max_over_ranks(ws, plan_ms)
+    max_calls_wall = max_over_ranks(ws, calls_wall_s)
     max_e2e_engine = max_over_ranks(ws, e2e_engine_s)
     total_bytes = sum_over_ranks(ws, float(K * step_total))
     value = total_bytes / (max_elapsed / 1e3) / 1e9
-    e2e_calls = total_bytes / max_e2e / 1e9
     e2e_engine = total_bytes / max_e2e_engine / 1e9
-    # Headline e2e: the public API that replaces FlexKV's TransferEngine
-    # (flexkv_b200.engine.TransferEngine, which keeps an H2D and a D2H op in
-    # flight together); the rate of one synchronous transfer_kv_blocks call
-    # per op (the reference worker's pattern) is reported beside it.
-    e2e = e2e_engine
     out = None
     if rank == 0:
-        lpc = extras.get("link_peak_concurrent")  # all ranks run at once in the timed region
-        lp = lpc or extras.get("link_peak_measured")
+        per_rank = [{"rank": r, "h2d": round(x[0], 2), "d2h": round(x[1], 2),
+                     "link_alone": {k: x[2 + i] for i, k in enumerate(keys)} if lp_alone else None,
+                     "link_concurrent": {k: x[5 + i] for i, k in enumerate(keys)} if lp_conc else None}
+                    for r, x in enumerate(allr)]
+        box_dir = {d: round(sum(x[i] for x in allr), 2) for i, d in enumerate(("h2d", "d2h"))}
+        sum_alone = {k: round(sum(x[2 + i] for x in allr), 2) for i, k in enumerate(keys)} if lp_alone else None
+        sum_conc = {k: round(sum(x[5 + i] for x in allr), 2) for i, k in enumerate(keys)} if lp_conc else None
+        # The roofline denominator: each GPU's link measured alone (the
+        # single-GPU peak), summed over the ranks; at N > 1 the peak with
+        # every rank copying at once is reported beside it.
+        lp = lp_alone
         if conc:
             ach = step_total / (elapsed_ms / K / 1e3) / 1e9
             peak = lp["duplex_total"] if lp else 2 * PCIE_GEN5_X16_GBS
             roof = {"bound": "pcie", "kernel": "transfer step, both directions in flight "
-                    "(kv_copy_kernel + copy-engine runs)", "achieved": round(ach, 2), "peak": peak,
+                    "(kv_copy_kernel + copy-engine runs), rank 0", "achieved": round(ach, 2), "peak": peak,
                     "unit": "GB/s", "frac": round(ach / peak, 4),
                     "traffic": int(sb["h2d"] * TRAFFIC_RATIO["h2d"] + sb["d2h"] * TRAFFIC_RATIO["d2h"]),
                     "traffic_unit": "DRAM bytes per step",
-                    "peak_source": (("measured live: contiguous cudaMemcpyAsync both ways at once on the "
-                                     "same pinned pool" + (", every rank copying at once" if lpc else "") +
-                                     " (MEASURED_PEAKS.json has no host-link figure)") if lp else
-                                    "nominal 2 x PCIe Gen5 x16"),
+                    "peak_source": ("measured live: contiguous cudaMemcpyAsync both ways at once on the same "
+                                    "pinned pool, this GPU alone (MEASURED_PEAKS.json has no host-link figure)"
+                                    if lp else "nominal 2 x PCIe Gen5 x16"),
                     "nominal_peak": 2 * PCIE_GEN5_X16_GBS,
                     "frac_of_nominal": round(ach / (2 * PCIE_GEN5_X16_GBS), 4)}
         else:
             head = min(rate, key=rate.get)
             peak = lp[head] if lp else PCIE_GEN5_X16_GBS
             nops_head = len([o for o in S.steps[0] if o[2] == (head == "h2d")])
-            roof = {"bound": "pcie", "kernel": f"transfer op {head.upper()} (kv_copy_kernel + copy-engine runs)",
-                    "achieved": round(rate[head], 2), "peak": peak, "unit": "GB/s",
+            roof = {"bound": "pcie", "kernel": f"transfer op {head.upper()} (kv_copy_kernel + copy-engine runs), "
+                    "rank 0", "achieved": round(rate[head], 2), "peak": peak, "unit": "GB/s",
                     "frac": round(rate[head] / peak, 4),
                     "traffic": int(sb[head] * TRAFFIC_RATIO[head] / max(nops_head, 1)),
                     "traffic_unit": "DRAM bytes per op",
-                    "peak_source": (("measured live: one contiguous cudaMemcpyAsync of up to 2 GiB on the "
-                                     "same pinned pool" + (", every rank copying at once" if lpc else "") +
-                                     " (MEASURED_PEAKS.json has no host-link figure)") if lp else
-                                    "nominal PCIe Gen5 x16 (no live measurement in this run)"),
+                    "peak_source": ("measured live: one contiguous cudaMemcpyAsync of up to 2 GiB on the same "
+                                    "pinned pool, this GPU alone (MEASURED_PEAKS.json has no host-link figure)"
+                                    if lp else "nominal PCIe Gen5 x16 (no live measurement in this run)"),
                     "nominal_peak": PCIE_GEN5_X16_GBS,
                     "frac_of_nominal": round(rate[head] / PCIE_GEN5_X16_GBS, 4),
                     "per_direction": {d: {"achieved": round(rate[d], 2),
                                           "peak": (lp[d] if lp else PCIE_GEN5_X16_GBS),
-                                          "frac": round(rate[d] / (lp[d] if lp else PCIE_GEN5_X16_GBS), 4)}
-                                      for d in rate}}
+                                          "frac": round(rate[d] / (lp[d] if lp else PCIE_GEN5_X16_GBS), 4),
+                                          "frac_of_nominal": round(rate[d] / PCIE_GEN5_X16_GBS, 4)}
+                                      for d in rate if rate[d] > 0}}
         if track_kernels:
             st0 = {("h2d" if op[2] else "d2h"): p.stats() for op, p in zip(S.steps[0], plans[0])}
             roof["sm_kernel"] = {
@@ -1147,6 +1256,24 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
                     "avg_launch_ms": round(statistics.mean(kern_ms[d]), 3),
                     "achieved_alongside_copy_engines": round(st0[d]["sm_bytes"] / statistics.mean(kern_ms[d]) / 1e6, 2)}
                 for d in st0 if kern_ms[d] and statistics.mean(kern_ms[d]) > 0}
+        box = {"per_direction_gbs": box_dir, "gpus": ws,
+               "how": "sum over ranks of each rank's per-direction rate (device-timed, every rank running)"}
+        if sum_alone:
+            if conc:
+                box["frac_of_n_x_single_gpu_peak"] = round(value / sum_alone["duplex_total"], 4)
+            else:
+                box["frac_of_n_x_single_gpu_peak"] = {d: round(box_dir[d] / sum_alone[d], 4) for d in box_dir
+                                                      if sum_alone[d] > 0}
+            box["n_x_single_gpu_peak"] = sum_alone
+        if sum_conc:
+            if conc:
+                box["frac_of_concurrent_peak"] = round(value / sum_conc["duplex_total"], 4)
+            else:
+                box["frac_of_concurrent_peak"] = {d: round(box_dir[d] / sum_conc[d], 4) for d in box_dir
+                                                  if sum_conc[d] > 0}
+            box["concurrent_peak"] = sum_conc
+        box["frac_of_n_x_nominal"] = ({d: round(box_dir[d] / (PCIE_GEN5_X16_GBS * ws), 4) for d in box_dir}
+                                      if not conc else round(value / (2 * PCIE_GEN5_X16_GBS * ws), 4))
         nids = sum(len(g) for g, c, h in S.steps[0])
         out = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": ws, "steps": K,
@@ -1160,20 +1287,29 @@ def run_ours(args, ws, rank, local, cfg, layout, with_hash):
                        "ops_per_step": len(S.steps[0]), "step_bytes": sb,
                        "gpu_pool_blocks": cfg["gpu_blocks"], "cpu_pool_blocks": S.cpu_blocks,
                        "cpu_pool_blocks_requested": cfg["cpu_blocks"],
+                       "cpu_pool_note": ("full size" if S.cpu_blocks >= cfg["cpu_blocks"] else
+                                         "scaled to 55% of the box's available RAM over the ranks"),
                        "transfer_sms": args.transfer_sms, "parallelism": f"dp{ws} (independent)",
-                       "l2": "inputs larger than L2, no flush"},
-            "per_direction_gbs": {d: round(v, 2) for d, v in rate.items()},
+                       "l2": "inputs larger than L2, no flush",
+                       "value_path": "c_ext.transfer_kv_blocks per op, pinned host id tensors, device-timed"},
+            "per_direction_gbs": {d: round(v, 2) for d, v in rate.items() if v > 0},
             "blocks_per_s": round(value * 1e9 / S.block_bytes, 1),
             "box_roofline_frac": round(value / (PCIE_GEN5_X16_GBS * ws * (2 if conc else 1)), 4),
+            "box": box,
+            "per_rank": per_rank,
             "roofline": roof,
-            "e2e": {"value": round(e2e, 3), "unit": "GB/s",
+            "plan_replay": {"value": round(total_bytes / (max_plan / 1e3) / 1e9, 3), "unit": "GB/s",
+                            "per_direction_gbs": {d: round(v, 2) for d, v in plan_rate.items() if v > 0},
+                            "how": "the same ops from c_ext.TransferPlan objects built before the timed region"},
+            "e2e": {"value": round(e2e_engine, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": int(sb["h2d"] + 16 * nids + 8 * cfg["layers"] * len(S.steps[0])),
                     "d2h_bytes_per_step": int(sb["d2h"]),
                     "how": "flexkv_b200.engine.TransferEngine: one graph per op, submit + poll, host id "
                            "tensors, wall clock (H2D and D2H ops on their own streams)",
-                    "per_op_calls": round(e2e_calls, 3),
-                    "per_op_calls_how": "flexkv_b200.c_ext.transfer_kv_blocks, one synchronous call per op "
-                                        "(async per direction when the workload overlaps directions)"},
+                    "per_op_calls": round(total_bytes / max_calls_wall / 1e9, 3),
+                    "per_op_calls_how": "wall clock of the value leg: flexkv_b200.c_ext.transfer_kv_blocks, one "
+                                        "synchronous call per op (async per direction when the workload "
+                                        "overlaps directions)"},
             "gpu_launches": int(launches), "clocks": clocks,
         }
         out.update(extras)
@@ -1187,52 +1323,70 @@ class TPSetup:
     """A tensor-parallel group of R GPUs in one process:
     rank r holds heads/R of every layer on cuda:r, and moves its slice to
     byte offset r*gpu_chunk of every chunk of one shared BLOCKWISE host pool
-    that holds all heads."""
+    that holds all heads.  stock=True registers the pool as FlexKV's worker
+    does (Setup's docstring) and imports nothing of flexkv_b200."""
 
-    def __init__(self, cfg: dict, R: int, cpu_blocks_override: int = 0):
-        from flexkv_b200 import c_ext
-        from flexkv_b200.layout import KVCacheLayout, KVCacheLayoutType
-        self.cfg, self.R = cfg, R
+    def __init__(self, cfg: dict, R: int, cpu_blocks_override: int = 0, stock: bool = False):
+        self.cfg, self.R, self.stock = cfg, R, stock
         L, H, D, tpb = cfg["layers"], cfg["heads"], cfg["head_dim"], cfg["tpb"]
         if H % R:
             raise ValueError(f"{H} KV heads do not divide over {R} ranks")
-        full = KVCacheLayout(KVCacheLayoutType.LAYERWISE, L, cfg["gpu_blocks"], tpb, H, D)
-        self.gpu_layout = full.div_head(R)
-        per = self.gpu_layout.div_layer(L)
         e = 2
-        self.g_kv, self.g_blk = per.get_kv_stride() * e, per.get_block_stride() * e
-        self.g_chunk = per.get_chunk_size() * e
-        self.gpu_layer_bytes = per.get_total_elements() * e
+        g = kv_strides("LAYERWISE", 1, cfg["gpu_blocks"], tpb, H // R, D, False)  # one layer, H/R heads
+        self.g_kv, self.g_blk = g["kv"] * e, g["block"] * e
+        self.g_chunk = g["chunk"] * e
+        self.gpu_layer_bytes = g["total"] * e
         self.block_bytes = L * 2 * tpb * H * D * e  # all heads: the host chunk
         fit = int(0.55 * mem_available_bytes() / self.block_bytes)
         cpu_blocks = cpu_blocks_override or min(cfg["cpu_blocks"], max(fit, 2 * cfg["batch"]))
         self.cpu_blocks = cpu_blocks
-        self.cpu_layout = KVCacheLayout(KVCacheLayoutType.BLOCKWISE, L, cpu_blocks, tpb, H, D)
-        self.c_kv = self.cpu_layout.get_kv_stride() * e
-        self.c_layer = self.cpu_layout.get_layer_stride() * e
-        self.c_blk = self.cpu_layout.get_block_stride() * e
-        self.c_chunk = self.cpu_layout.get_chunk_size() * e
+        c = kv_strides("BLOCKWISE", L, cpu_blocks, tpb, H, D, False)
+        self.c_kv, self.c_layer, self.c_blk = c["kv"] * e, c["layer"] * e, c["block"] * e
+        self.c_chunk = c["chunk"] * e
         self.layers = []
         for r in range(R):
             dev = torch.device(f"cuda:{r}")
-            base = torch.empty((L,) + tuple(per.kv_shape), dtype=torch.bfloat16, device=dev)
+            base = torch.empty((L, 2, cfg["gpu_blocks"], tpb, H // R, D), dtype=torch.bfloat16, device=dev)
             base.normal_()
             self.layers.append([base[l] for l in range(L)])
-        self.cpu = torch.empty(self.cpu_layout.get_total_elements(), dtype=torch.bfloat16)
-        c_ext.cudaHostRegister(self.cpu, advise_hugepages=True)
-        log(f"[tp{R}] gpu pool {L} layers x {R} ranks, cpu pool {self.cpu.numel() * 2 / 2**30:.1f} GiB")
+        self.cpu = torch.empty(c["total"], dtype=torch.bfloat16)
+        if stock:
+            stock_host_register(self.cpu)
+        else:
+            from flexkv_b200 import c_ext
+            c_ext.cudaHostRegister(self.cpu, advise_hugepages=True)
+        log(f"[tp{R}] gpu pool {L} layers x {R} ranks, cpu pool {self.cpu.numel() * 2 / 2**30:.1f} GiB"
+            + (" (stock registration)" if stock else ""))
         self.steps = []
         for s_ in range(4):
             ops = []
             for j, h2d in enumerate((True, False)):
-                g, c = make_batch(cfg["batch"], cfg["gpu_blocks"], cpu_blocks, 10 * s_ + j, 0.0, 1)
-                ops.append((g, c, h2d))
+                g_, c_ = make_batch(cfg["batch"], cfg["gpu_blocks"], cpu_blocks, 10 * s_ + j, 0.0, 1)
+                ops.append((g_, c_, h2d))
             self.steps.append(ops)
         self.step_bytes = {"h2d": cfg["batch"] * self.block_bytes, "d2h": cfg["batch"] * self.block_bytes}
 
+    @property
+    def gpu_layout(self):
+        """flexkv_b200's KVCacheLayout of one rank's GPU pool (our arm only)."""
+        from flexkv_b200.layout import KVCacheLayout, KVCacheLayoutType
+        c = self.cfg
+        return KVCacheLayout(KVCacheLayoutType.LAYERWISE, c["layers"], c["gpu_blocks"], c["tpb"], c["heads"],
+                             c["head_dim"]).div_head(self.R)
+
+    @property
+    def cpu_layout(self):
+        from flexkv_b200.layout import KVCacheLayout, KVCacheLayoutType
+        c = self.cfg
+        return KVCacheLayout(KVCacheLayoutType.BLOCKWISE, c["layers"], self.cpu_blocks, c["tpb"], c["heads"],
+                             c["head_dim"])
+
     def close(self):
-        from flexkv_b200 import c_ext
-        c_ext.cudaHostUnregister(self.cpu)
+        if self.stock:
+            stock_host_unregister(self.cpu)
+        else:
+            from flexkv_b200 import c_ext
+            c_ext.cudaHostUnregister(self.cpu)
 
 
 def run_tp(args, cfg, R):
@@ -1358,7 +1512,7 @@ def run_tp_reference(args, cfg, R):
     from oracle import oracle as O
     if not O.reference_available():
         return {"impl": "reference", "unavailable": "oracle/_ref/libref_transfer.so not built"}, None
-    S = TPSetup(cfg, R, args.cpu_blocks)
+    S = TPSetup(cfg, R, args.cpu_blocks, stock=True)
     ref = O.ref_lib()
     ptrs = [torch.tensor([t.data_ptr() for t in S.layers[r]], dtype=torch.int64).pin_memory() for r in range(R)]
     host_ops = [[(torch.from_numpy(g).pin_memory(), torch.from_numpy(c).pin_memory(), h)
@@ -1441,7 +1595,7 @@ def run_reference(args, ws, rank, local, cfg, layout):
     if not O.reference_available():
         return {"impl": "reference", "unavailable": "oracle/_ref/libref_transfer.so not built "
                 "(needs the reference tree at build time)"}, None
-    S = Setup(cfg, layout, 1, local, args.cpu_blocks, args.gpu_alloc)
+    S = Setup(cfg, layout, 1, local, args.cpu_blocks, args.gpu_alloc, stock=True)
     ref = O.ref_lib()
     ptrs = S.ptrs.pin_memory()
     host_ops = [[(torch.from_numpy(g).pin_memory(), torch.from_numpy(c).pin_memory(), h)

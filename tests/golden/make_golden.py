@@ -201,8 +201,11 @@ def run_transfer_case(spec: dict) -> dict:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("FLEXKV_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("FLEXKV_REFERENCE"),
+                    help="the reference tree (default: $FLEXKV_REFERENCE)")
     a = ap.parse_args()
+    if not a.reference or not os.path.isdir(a.reference):
+        ap.error("the reference tree is needed: pass --reference or set FLEXKV_REFERENCE")
     with open(os.path.join(HERE, "layouts.json"), "w") as f:
         json.dump(make_layouts(a.reference), f, indent=1)
     with open(os.path.join(HERE, "hash.json"), "w") as f:
