@@ -152,6 +152,67 @@ def ref_lib() -> ctypes.CDLL:
     return _ref
 
 
+REF_SSD_SO = os.path.join(HERE, "_ref", "libref_ssd.so")
+_ref_ssd = None
+
+
+def reference_ssd_available() -> bool:
+    return os.path.exists(REF_SSD_SO)
+
+
+def ref_ssd_lib() -> ctypes.CDLL:
+    """The reference's own SSD tier (csrc/transfer_ssd.cpp), built into
+    oracle/_ref/libref_ssd.so by oracle/Makefile (ref_ssd_shim.cpp)."""
+    global _ref_ssd
+    if _ref_ssd is None:
+        if not reference_ssd_available():
+            raise FileNotFoundError(f"{REF_SSD_SO} not built (needs FLEXKV_REFERENCE at build time)")
+        L = ctypes.CDLL(REF_SSD_SO)
+        L.ref_ssd_ctx_create.restype = _c_int
+        L.ref_ssd_ctx_create.argtypes = [_vp, _c_int, _c_int, ctypes.POINTER(_vp)]
+        L.ref_ssd_ctx_destroy.restype = None
+        L.ref_ssd_ctx_destroy.argtypes = [_vp]
+        L.ref_ssd_transfer.restype = _c_int
+        L.ref_ssd_transfer.argtypes = [
+            _vp, _c_int, _c_int, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+            _c_int, _c_int, _c_int, _c_int, _c_int]
+        _ref_ssd = L
+    return _ref_ssd
+
+
+class RefSSDContext:
+    """flexkv::SSDIOCTX of the reference (thread-pool path): files[d] lists
+    the file paths of SSD device d, every device with as many files."""
+
+    def __init__(self, files: dict):
+        nd, nf = len(files), len(files[0])
+        paths = [str(files[d][f]).encode() for d in range(nd) for f in range(nf)]
+        arr = (ctypes.c_char_p * len(paths))(*paths)
+        h = _vp()
+        if ref_ssd_lib().ref_ssd_ctx_create(ctypes.cast(arr, _vp), nd, nf, ctypes.byref(h)) != 0:
+            raise RuntimeError("reference SSDIOCTX failed to open its files")
+        self._h = h
+
+    def transfer(self, start_layer: int, num_layers: int, cpu_ptr: int, ssd_block_ids: np.ndarray,
+                 cpu_block_ids: np.ndarray, cpu_layer_stride: int, cpu_kv_stride: int, ssd_layer_stride: int,
+                 ssd_kv_stride: int, chunk: int, block_stride: int, is_read: bool, num_blocks_per_file: int,
+                 round_robin: int = 1, threads_per_device: int = 16, is_mla: bool = False) -> None:
+        s = np.ascontiguousarray(ssd_block_ids, dtype=np.int64)
+        c = np.ascontiguousarray(cpu_block_ids, dtype=np.int64)
+        rc = ref_ssd_lib().ref_ssd_transfer(
+            self._h, int(start_layer), int(num_layers), _vp(int(cpu_ptr)), _ptr(s), _ptr(c), len(s),
+            int(cpu_layer_stride), int(cpu_kv_stride), int(ssd_layer_stride), int(ssd_kv_stride), int(chunk),
+            int(block_stride), int(bool(is_read)), int(num_blocks_per_file), int(round_robin),
+            int(threads_per_device), int(bool(is_mla)))
+        if rc != 0:
+            raise RuntimeError("reference transfer_kv_blocks_ssd threw")
+
+    def close(self) -> None:
+        if self._h:
+            ref_ssd_lib().ref_ssd_ctx_destroy(self._h)
+            self._h = None
+
+
 def ssd_transfer(files: List[List[np.ndarray]], start_layer: int, num_layers: int, cpu: np.ndarray,
                  ssd_block_ids: np.ndarray, cpu_block_ids: np.ndarray, cpu_layer_stride: int,
                  cpu_kv_stride: int, ssd_layer_stride: int, ssd_kv_stride: int, chunk: int,
