@@ -162,6 +162,7 @@ _SIGNATURES = {
     "fkv_hasher_destroy": (None, [c_vp]),
     "fkv_hasher_reset": (c_int, [c_vp, c_vp]),
     "fkv_hasher_update": (c_int, [c_vp, c_vp, c_i64, c_vp]),
+    "fkv_hasher_update_bounded": (c_int, [c_vp, c_vp, c_i64, c_u64, c_i64, c_vp]),
     "fkv_hasher_digest": (c_int, [c_vp, P_u64, c_vp]),
     "fkv_gen_hashes": (c_int, [c_vp, c_vp, c_i64, c_int, c_vp, c_i64, c_vp]),
     "fkv_gen_hashes_batched": (c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp]),

@@ -423,7 +423,9 @@ class CpuCacheIndex:
         of both tiers on the device (this index is the CPU tier's), the D2H
         copy, then the H2DISK leg through the SSD tier for the blocks the SSD
         tier lacked, and with mark_ready both tiers' blocks marked ready (the
-        put callback).  Returns when the SSD writes are done."""
+        put callback).  Returns when the SSD writes are done.  If the SSD
+        writes fail, the SSD tier's new entries are removed and their blocks
+        recycled before the error propagates; the CPU tier keeps its part."""
         from . import c_ext
         if len(token_ids) != len(gpu_block_ids):
             raise ValueError("one gpu block list per request")
@@ -452,13 +454,22 @@ class CpuCacheIndex:
         sel = np.flatnonzero(ssd_ids[:nb] >= 0)
         if len(sel):
             st = ssd.strides
-            c_ext.transfer_kv_blocks_ssd(
-                ssd.ioctx, list(range(ssd.num_layers)), layout.cpu_tensor.data_ptr(),
-                np.ascontiguousarray(ssd_ids[sel]), np.ascontiguousarray(cpu[sel]),
-                st.cpu_layer_stride_in_bytes, st.cpu_kv_stride_in_bytes, st.ssd_layer_stride_in_bytes,
-                st.ssd_kv_stride_in_bytes, st.chunk_size_in_bytes, st.block_stride_in_bytes, False,
-                ssd.num_blocks_per_file, ssd.round_robin, ssd.threads_per_device, ssd.is_mla,
-                cpu_pool_bytes=layout.cpu_tensor.numel() * layout.cpu_tensor.element_size())
+            try:
+                c_ext.transfer_kv_blocks_ssd(
+                    ssd.ioctx, list(range(ssd.num_layers)), layout.cpu_tensor.data_ptr(),
+                    np.ascontiguousarray(ssd_ids[sel]), np.ascontiguousarray(cpu[sel]),
+                    st.cpu_layer_stride_in_bytes, st.cpu_kv_stride_in_bytes, st.ssd_layer_stride_in_bytes,
+                    st.ssd_kv_stride_in_bytes, st.chunk_size_in_bytes, st.block_stride_in_bytes, False,
+                    ssd.num_blocks_per_file, ssd.round_robin, ssd.threads_per_device, ssd.is_mla,
+                    cpu_pool_bytes=layout.cpu_tensor.numel() * layout.cpu_tensor.element_size())
+            except Exception:
+                # The SSD tier never received these blocks: take its new
+                # entries out again and give their SSD blocks back, so no
+                # entry points at a block that was never written.  The CPU
+                # tier's part of the put (D2H, ready marks) stands.
+                held = ssd.index.remove(hashes[sel])
+                ssd.index.recycle(held[held >= 0])
+                raise
             if mark_ready:
                 ssd.index.set_ready(hashes[sel])
         return res

@@ -60,7 +60,7 @@ enum : int {
 enum ErrCode : int64_t { kErrNone = 0, kErrFull = 1, kErrReserved = 2, kErrCollision = 3, kErrRecycleFree = 4 };
 
 // put outcome per request (res[3r+2])
-enum : int64_t { kPutEmpty = 0, kPutDone = 1, kPutNoSpace = 2 };
+enum : int64_t { kPutEmpty = 0, kPutDone = 1, kPutNoSpace = 2, kPutSourceNotReady = 3 };
 
 struct Table {
   uint64_t *keys;
@@ -357,14 +357,16 @@ __global__ void __launch_bounds__(kDecideThreads) put_decide_fast_kernel(
   }
 }
 
-// Per block: present in a tier's index before the call, and the pool block
-// it holds there (-1 if absent).
-__global__ void tier_lookup_kernel(Table t, const uint64_t *hashes, int64_t nb, uint8_t *present, int64_t *phys) {
+// Per block: present in a tier's index before the call, the pool block it
+// holds there (-1 if absent) and whether that block is ready.
+__global__ void tier_lookup_kernel(Table t, const uint64_t *hashes, int64_t nb, uint8_t *present, int64_t *phys,
+                                   uint8_t *ready) {
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nb; i += stride) {
     const int64_t s = find(t, hashes[i]);
     present[i] = s >= 0 ? 1 : 0;
     if (phys) phys[i] = s >= 0 ? t.vals[s] : -1;
+    if (ready) ready[i] = (s >= 0 && (t.flags[s] & kReadyBit)) ? 1 : 0;
   }
 }
 
@@ -383,11 +385,15 @@ struct PoolRef {
 // blocks; f2 = n - m_s blocks go CPU -> SSD into new SSD blocks (the block's
 // CPU copy: new for j >= m_c, the cached one below); both takes must succeed
 // or the request comes back empty with both allocations given back
-// (cache_engine.py:838-852).  res[4r..4r+3] = skipped, moved D2H, moved to
-// SSD, outcome.
+// (cache_engine.py:838-852).  When the SSD tier is behind the CPU tier
+// (m_s < m_c, only after a caller evicted from the SSD tier alone), a block
+// below m_c goes to the SSD tier from its cached CPU block; if one of those
+// cached blocks is not ready (its own D2H may still be in flight), the
+// request is refused: it comes back empty and allocates nothing.
+// res[4r..4r+3] = skipped, moved D2H, moved to SSD, outcome.
 __global__ void __launch_bounds__(32) put2_decide_kernel(
     int num_req, const int64_t *blk_off, const uint8_t *before_c, const uint8_t *before_s, const int64_t *phys_c,
-    const int32_t *lslot, int32_t *ins_c, int32_t *ins_s, int64_t *slot_cpu, const int64_t *gpu_ids, PoolRef pc,
+    const uint8_t *ready_c, const int32_t *lslot, int32_t *ins_c, int32_t *ins_s, int64_t *slot_cpu, const int64_t *gpu_ids, PoolRef pc,
     PoolRef ps, int64_t *res, int64_t *cpu_out, int64_t *ssd_out, int64_t *d2h_gpu, int64_t *d2h_cpu,
     int64_t *new_c, int64_t *new_s, int64_t *counts) {
   const int lane = threadIdx.x;
@@ -419,6 +425,16 @@ __global__ void __launch_bounds__(32) put2_decide_kernel(
     int64_t *rr = res + 4 * (int64_t)r;
     if (k == 0) {  // the CPU tier holds every block: nothing moves (cache_engine.py:819-820)
       if (lane == 0) { rr[0] = 0; rr[1] = 0; rr[2] = 0; rr[3] = kPutEmpty; }
+      continue;
+    }
+    bool unready = false;  // an H2DISK source cached before the call but not ready
+    for (int64_t jb = m_s; jb < m_c && !unready; jb += 32) {
+      const int64_t j = jb + lane;
+      const bool bad = j < m_c && before_c[o + j] && !ready_c[o + j];
+      unready = __ballot_sync(0xffffffffu, bad) != 0u;
+    }
+    if (unready) {
+      if (lane == 0) { rr[0] = 0; rr[1] = 0; rr[2] = 0; rr[3] = kPutSourceNotReady; }
       continue;
     }
     int64_t a = k < free_c ? k : free_c;
@@ -1167,7 +1183,7 @@ int fkv_cache_index_put2(fkv_cache_index *cpu, fkv_cache_index *ssd, const int64
   size_t off = 0;
   auto carve = [&](size_t bytes) { const size_t at = off; off = al16(off + bytes); return at; };
   const size_t o_hash = carve(8 * nb), o_bc = carve(nb), o_bs = carve(nb), o_phys = carve(8 * nb),
-               o_lslot = carve(4 * nb), o_lkeys = carve(8 * lslots), o_insc = carve(4 * lslots),
+               o_rdy = carve(nb), o_lslot = carve(4 * nb), o_lkeys = carve(8 * lslots), o_insc = carve(4 * lslots),
                o_inss = carve(4 * lslots), o_scpu = carve(8 * lslots), o_off = carve(8 * (num_seqs + 1)),
                o_gid = carve(8 * nb), o_res = carve(32 * (size_t)num_seqs), o_cpu = carve(8 * nb),
                o_ssd = carve(8 * nb), o_d2hg = carve(8 * nb), o_d2hc = carve(8 * nb), o_newc = carve(8 * nb),
@@ -1199,15 +1215,17 @@ int fkv_cache_index_put2(fkv_cache_index *cpu, fkv_cache_index *ssd, const int64
                                                   64 - log2u(lslots), reinterpret_cast<int32_t *>(b + o_lslot),
                                                   cpu->state);
   FKV_CUDA(cudaGetLastError());
-  tier_lookup_kernel<<<grid_for(nb), 256, 0, s>>>(tc, hashes, nb, reinterpret_cast<uint8_t *>(b + o_bc), I64(o_phys));
+  tier_lookup_kernel<<<grid_for(nb), 256, 0, s>>>(tc, hashes, nb, reinterpret_cast<uint8_t *>(b + o_bc), I64(o_phys),
+                                                   reinterpret_cast<uint8_t *>(b + o_rdy));
   FKV_CUDA(cudaGetLastError());
-  tier_lookup_kernel<<<grid_for(nb), 256, 0, s>>>(ts, hashes, nb, reinterpret_cast<uint8_t *>(b + o_bs), nullptr);
+  tier_lookup_kernel<<<grid_for(nb), 256, 0, s>>>(ts, hashes, nb, reinterpret_cast<uint8_t *>(b + o_bs), nullptr,
+                                                   nullptr);
   FKV_CUDA(cudaGetLastError());
   const PoolRef pc{cpu->free_mask, cpu->mask_bytes, cpu->free_ids, cpu->state};
   const PoolRef ps{ssd->free_mask, ssd->mask_bytes, ssd->free_ids, ssd->state};
   put2_decide_kernel<<<1, 32, 0, s>>>(num_seqs, I64(o_off), reinterpret_cast<uint8_t *>(b + o_bc),
                                       reinterpret_cast<uint8_t *>(b + o_bs), I64(o_phys),
-                                      reinterpret_cast<int32_t *>(b + o_lslot), reinterpret_cast<int32_t *>(b + o_insc),
+                                      reinterpret_cast<uint8_t *>(b + o_rdy), reinterpret_cast<int32_t *>(b + o_lslot), reinterpret_cast<int32_t *>(b + o_insc),
                                       reinterpret_cast<int32_t *>(b + o_inss), I64(o_scpu), I64(o_gid), pc, ps,
                                       I64(o_res), I64(o_cpu), I64(o_ssd), I64(o_d2hg), I64(o_d2hc), I64(o_newc),
                                       I64(o_news), counts);

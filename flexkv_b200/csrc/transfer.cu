@@ -206,17 +206,28 @@ int variant_index(int unroll, int pf256) {
   return u + (pf256 ? 3 : 0);
 }
 
+// Per-device caches below hold this many devices; a larger ordinal is
+// refused rather than aliased onto another device's entry.
+constexpr int kMaxDevices = 64;
+
+int check_device(int device) {
+  if (device < 0 || device >= kMaxDevices)
+    return fail(FKV_ERR_INVALID_ARG, "device ordinal " + std::to_string(device) + " is outside [0, 64)");
+  return FKV_OK;
+}
+
 // Occupancy (CTAs per SM) of each kernel variant, cached per device.
 struct OccCache {
   std::mutex mu;
-  int max_pitch[64] = {0};
-  int occ[64][2][kNumVariants] = {{{0}}};
+  int max_pitch[kMaxDevices] = {0};
+  int occ[kMaxDevices][2][kNumVariants] = {{{0}}};
 };
 OccCache g_occ;
 
 int ctas_per_sm(int device, bool h2d, int variant, int *out) {
+  if (int rc = check_device(device)) return rc;
   std::lock_guard<std::mutex> lk(g_occ.mu);
-  int d = device & 63;
+  const int d = device;
   int &v = g_occ.occ[d][h2d ? 1 : 0][variant];
   if (v == 0) {
     const void *k = h2d ? kernel_ptr<true>(variant) : kernel_ptr<false>(variant);
@@ -229,8 +240,9 @@ int ctas_per_sm(int device, bool h2d, int variant, int *out) {
 }
 
 int max_pitch(int device, int *out) {
+  if (int rc = check_device(device)) return rc;
   std::lock_guard<std::mutex> lk(g_occ.mu);
-  int d = device & 63;
+  const int d = device;
   if (g_occ.max_pitch[d] == 0) {
     int mp = 0;
     FKV_CUDA(cudaDeviceGetAttribute(&mp, cudaDevAttrMaxPitch, device));
@@ -709,17 +721,18 @@ int transfer_enqueue_device_ids(const fkv_transfer_desc &d, const int64_t *gpu_i
   ThreadDeviceCtx *ctx = nullptr;
   if (int rc = get_ctx(device, &ctx)) return rc;
   const void *k = hp.h2d ? (const void *)kv_copy_devn_kernel<true> : (const void *)kv_copy_devn_kernel<false>;
-  static int occ_cache[64][2] = {{0}};  // CTAs per SM, per device and direction
+  if (int rc = check_device(device)) return rc;
+  static int occ_cache[kMaxDevices][2] = {{0}};  // CTAs per SM, per device and direction
   int occ = 0;
   {
     std::lock_guard<std::mutex> lk(g_occ.mu);
-    occ = occ_cache[device & 63][hp.h2d ? 1 : 0];
+    occ = occ_cache[device][hp.h2d ? 1 : 0];
   }
   if (occ == 0) {
     FKV_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, kThreads, 0));
     occ = std::max(occ, 1);
     std::lock_guard<std::mutex> lk(g_occ.mu);
-    occ_cache[device & 63][hp.h2d ? 1 : 0] = occ;
+    occ_cache[device][hp.h2d ? 1 : 0] = occ;
   }
   int sms = d.transfer_sms > 0 ? d.transfer_sms : env_int("FKV_TRANSFER_SMS", kDefaultSms);
   sms = std::min(sms, ctx->num_sms);
@@ -970,11 +983,12 @@ static __device__ __align__(256) int64_t g_noalloc_table[kNoAllocWords];
 
 // Device address of g_noalloc_table per device, resolved once per device.
 std::mutex g_noalloc_mu;
-int64_t *g_noalloc_addr[64] = {nullptr};
+int64_t *g_noalloc_addr[kMaxDevices] = {nullptr};
 
 int noalloc_table(int device, int64_t **out) {
+  if (int rc = check_device(device)) return rc;
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  int64_t *&p = g_noalloc_addr[device & 63];
+  int64_t *&p = g_noalloc_addr[device];
   if (p == nullptr) {
     void *addr = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_table);

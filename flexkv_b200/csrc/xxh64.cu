@@ -347,12 +347,12 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 // Wait for the phase of the given parity to complete; false (and the
-// caller's error word set) if it does not within kWaitLimitNs.
-__device__ __noinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *err) {
+// caller's error word set) if it does not within limit_ns.
+__device__ __noinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *err, uint64_t limit_ns) {
   if (mbar_try_wait(b, parity)) return true;
   const uint64_t t0 = global_ns();
   while (!mbar_try_wait(b, parity)) {
-    if (global_ns() - t0 > kWaitLimitNs) {
+    if (global_ns() - t0 > limit_ns) {
       *err = FKV_ERR_TIMEOUT;
       return false;
     }
@@ -361,10 +361,13 @@ __device__ __noinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile in
 }
 
 // The two-warp chain over K stripes of aligned data.  Returns false on a
-// timed-out hand-off (error word set).
+// timed-out hand-off (error word set).  Every hand-off wait gives up after
+// limit_ns.  max_tiles >= 0 makes the producer stop after that many tiles
+// (a diagnostic that lets the chain warp's wait run out); -1 = all tiles.
 template <int SPB, bool SNAP>
 __device__ bool chain_fused(const uint64_t *data64, bool al16, int64_t K, uint64_t *smem, uint64_t *bars,
-                            int warp, int lane, uint64_t &v, uint64_t *snaps, volatile int *err) {
+                            int warp, int lane, uint64_t &v, uint64_t *snaps, volatile int *err,
+                            uint64_t limit_ns, int64_t max_tiles) {
   uint64_t *prod = smem;                   // [2][kProdSlot]
   uint64_t *snap = smem + 2 * kProdSlot;   // [2][kSnapSlot]
   uint64_t *full = bars, *empty = bars + 2;
@@ -373,9 +376,10 @@ __device__ bool chain_fused(const uint64_t *data64, bool al16, int64_t K, uint64
   auto tile_stripes = [&](int64_t t) { return (int)(K - 256 * t < 256 ? K - 256 * t : 256); };
   if (warp == 1) {
     for (int64_t t = 0; t < T; ++t) {
+      if (max_tiles >= 0 && t >= max_tiles) return true;  // stopped on purpose: the chain's wait runs out
       const int sl = (int)(t & 1);
       if (t >= 2) {  // slot sl held tile t-2 (a full tile): wait for the chain, drain its snapshots
-        if (!mbar_wait(&empty[sl], (uint32_t)(((t >> 1) - 1) & 1), err)) return false;
+        if (!mbar_wait(&empty[sl], (uint32_t)(((t >> 1) - 1) & 1), err, limit_ns)) return false;
         if (SNAP) {
           uint64_t *dst = snaps + 4 * (t - 2) * kBlocksPerTile;
           for (int k = lane; k < 4 * kBlocksPerTile; k += 32) dst[k] = snap[sl * kSnapSlot + k];
@@ -386,7 +390,7 @@ __device__ bool chain_fused(const uint64_t *data64, bool al16, int64_t K, uint64
     }
     for (int64_t t = T >= 2 ? T - 2 : 0; t < T; ++t) {  // the last one or two tiles
       const int sl = (int)(t & 1);
-      if (!mbar_wait(&empty[sl], (uint32_t)((t >> 1) & 1), err)) return false;
+      if (!mbar_wait(&empty[sl], (uint32_t)((t >> 1) & 1), err, limit_ns)) return false;
       if (SNAP) {
         uint64_t *dst = snaps + 4 * t * kBlocksPerTile;
         const int n = 4 * (tile_stripes(t) / SPB);
@@ -396,7 +400,7 @@ __device__ bool chain_fused(const uint64_t *data64, bool al16, int64_t K, uint64
   } else if (lane < 4) {
     for (int64_t t = 0; t < T; ++t) {
       const int sl = (int)(t & 1);
-      if (!mbar_wait(&full[sl], (uint32_t)((t >> 1) & 1), err)) return false;
+      if (!mbar_wait(&full[sl], (uint32_t)((t >> 1) & 1), err, limit_ns)) return false;
       chain_tile_fused<SPB, SNAP>(prod + sl * kProdSlot + lane * kProdStride, tile_stripes(t), v,
                                   snap + sl * kSnapSlot + lane);
       mbar_arrive(&empty[sl]);
@@ -427,11 +431,13 @@ __device__ __forceinline__ void chain_tile_generic(const uint64_t *buf, int kt, 
 // data and blocks of 1, 2, 4 or 8 whole stripes (every gen_hashes call
 // with tpb a multiple of 4 tokens, and every update of aligned data) the
 // two warps run the fused path; otherwise warp 0 runs alone.  err is a
-// host-visible word set to FKV_ERR_TIMEOUT if a hand-off wait ran out.
+// host-visible word set to FKV_ERR_TIMEOUT if a hand-off wait ran out
+// (each gives up after limit_ns); max_tiles caps the producer (see
+// chain_fused), -1 in every product call.
 __global__ void __launch_bounds__(64) xxh_chain_kernel(const XxhState *in, XxhState *out,
                                                        const uint8_t *data, int64_t len,
                                                        int64_t bb, int64_t nb, uint64_t *snaps,
-                                                       int *err) {
+                                                       int *err, uint64_t limit_ns, int64_t max_tiles) {
   __shared__ __align__(16) uint64_t smem[kChainSmemWords];
   __shared__ __align__(8) uint64_t bars[4];  // full[2], empty[2]
   const int warp = threadIdx.x >> 5;
@@ -460,11 +466,11 @@ __global__ void __launch_bounds__(64) xxh_chain_kernel(const XxhState *in, XxhSt
     const bool al16 = (reinterpret_cast<uintptr_t>(data) & 15) == 0;
     volatile int *e = err;
     bool ok;
-    if (snaps == nullptr) ok = chain_fused<1, false>(data64, al16, K, smem, bars, warp, lane, v, snaps, e);
-    else if (spb == 1) ok = chain_fused<1, true>(data64, al16, K, smem, bars, warp, lane, v, snaps, e);
-    else if (spb == 2) ok = chain_fused<2, true>(data64, al16, K, smem, bars, warp, lane, v, snaps, e);
-    else if (spb == 4) ok = chain_fused<4, true>(data64, al16, K, smem, bars, warp, lane, v, snaps, e);
-    else ok = chain_fused<8, true>(data64, al16, K, smem, bars, warp, lane, v, snaps, e);
+    if (snaps == nullptr) ok = chain_fused<1, false>(data64, al16, K, smem, bars, warp, lane, v, snaps, e, limit_ns, max_tiles);
+    else if (spb == 1) ok = chain_fused<1, true>(data64, al16, K, smem, bars, warp, lane, v, snaps, e, limit_ns, max_tiles);
+    else if (spb == 2) ok = chain_fused<2, true>(data64, al16, K, smem, bars, warp, lane, v, snaps, e, limit_ns, max_tiles);
+    else if (spb == 4) ok = chain_fused<4, true>(data64, al16, K, smem, bars, warp, lane, v, snaps, e, limit_ns, max_tiles);
+    else ok = chain_fused<8, true>(data64, al16, K, smem, bars, warp, lane, v, snaps, e, limit_ns, max_tiles);
     if (!ok || warp != 0) return;
   } else {
     if (warp != 0) return;
@@ -687,10 +693,10 @@ int device_view(const void *p, int64_t bytes, int device, cudaStream_t s, DevBuf
 }
 
 int run_chain(fkv_hasher *h, const uint8_t *data_dev, int64_t len, int64_t bb, int64_t nb,
-              uint64_t *snaps, cudaStream_t s) {
+              uint64_t *snaps, cudaStream_t s, uint64_t limit_ns = kWaitLimitNs, int64_t max_tiles = -1) {
   XxhState *in = h->states + h->cur;
   XxhState *out = h->states + (h->cur ^ 1);
-  xxh_chain_kernel<<<1, 64, 0, s>>>(in, out, data_dev, len, bb, nb, snaps, h->err_dev);
+  xxh_chain_kernel<<<1, 64, 0, s>>>(in, out, data_dev, len, bb, nb, snaps, h->err_dev, limit_ns, max_tiles);
   FKV_CUDA(cudaGetLastError());
   note_launch();
   return FKV_OK;
@@ -701,7 +707,7 @@ int check_chain(fkv_hasher *h) {
   if (*h->err_host == 0) return FKV_OK;
   const int code = *h->err_host;
   *h->err_host = 0;
-  return fail(code, "hash chain kernel: a producer/consumer hand-off wait timed out; the hasher state is invalid");
+  return fail(code, "hash chain kernel: a producer/consumer hand-off wait timed out; the update did not complete");
 }
 
 }  // namespace
@@ -782,6 +788,29 @@ int fkv_hasher_update(fkv_hasher *h, const void *data, int64_t size, void *strea
     FKV_CUDA(cudaStreamSynchronize(s));
     return check_chain(h);
   }
+  return FKV_OK;
+}
+
+int fkv_hasher_update_bounded(fkv_hasher *h, const void *data, int64_t size, uint64_t wait_limit_ns,
+                              int64_t producer_tiles, void *stream) {
+  clear_error();
+  if (!h) return fail(FKV_ERR_INVALID_ARG, "null hasher");
+  if (size < 0 || (size > 0 && !data)) return fail(FKV_ERR_INVALID_ARG, "bad update buffer");
+  if (wait_limit_ns == 0 || wait_limit_ns > kWaitLimitNs)
+    return fail(FKV_ERR_INVALID_ARG, "wait_limit_ns must lie in (0, 2 s]");
+  if (producer_tiles < -1) return fail(FKV_ERR_INVALID_ARG, "producer_tiles must be -1 or non-negative");
+  if (size == 0) return FKV_OK;
+  DeviceGuard g;
+  if (int rc = g.enter(h->device)) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  DevBuf tmp;
+  const void *dv = nullptr;
+  bool was_host = false;
+  if (int rc = device_view(data, size, h->device, s, tmp, &dv, &was_host)) return rc;
+  if (int rc = run_chain(h, (const uint8_t *)dv, size, 0, 0, nullptr, s, wait_limit_ns, producer_tiles)) return rc;
+  FKV_CUDA(cudaStreamSynchronize(s));
+  if (int rc = check_chain(h)) return rc;  // timed out: the state before the call stays live
+  h->cur ^= 1;
   return FKV_OK;
 }
 

@@ -317,6 +317,19 @@ int fkv_hasher_reset(fkv_hasher *h, void *stream);
 /* data may be host or device memory; returns after the state is updated. */
 int fkv_hasher_update(fkv_hasher *h, const void *data, int64_t size,
                       void *stream);
+/* Diagnostic form of fkv_hasher_update (no counterpart in the reference):
+ * every producer/consumer hand-off wait of the two-warp chain kernel gives
+ * up after wait_limit_ns (at most 2 s, the limit of every other call), and
+ * producer_tiles >= 0 makes the producer warp stop after that many 8 KiB
+ * tiles (-1: all).  With fewer tiles than the data holds, the chain warp's
+ * wait runs out and the call returns FKV_ERR_TIMEOUT; the kernel returns
+ * cleanly, the hasher keeps the state it had before the call and the CUDA
+ * context stays usable.  Synchronous.  Used by the tests of the bounded
+ * waits; the data must be device memory, 8-byte aligned, for the two-warp
+ * path (other data takes the one-warp path, which has no hand-off). */
+int fkv_hasher_update_bounded(fkv_hasher *h, const void *data, int64_t size,
+                              uint64_t wait_limit_ns, int64_t producer_tiles,
+                              void *stream);
 int fkv_hasher_digest(fkv_hasher *h, uint64_t *out, void *stream);
 
 /* gen_hashes (hash.cpp:47-66): for block b, update the hasher with tokens
@@ -489,11 +502,18 @@ int fkv_cache_index_put(fkv_cache_index *ci, const int64_t *token_ids, const int
  * CPU / SSD tier; the n - m_c others are copied D2H into new CPU blocks
  * (inserted, ready after the copy when mark_ready); the n - m_s blocks the
  * SSD tier lacks get new SSD blocks (inserted, not ready).  Both takes must
- * succeed, else the put is empty and gives both allocations back.  Out:
- * num_skipped (m_c), num_transferred (D2H blocks), num_to_ssd (SSD blocks);
- * per block of the batch: cpu_block_ids (the CPU block holding it when it
- * is copied or goes to the SSD tier, else -1), ssd_block_ids (its new SSD
- * block, else -1), block_hashes.  The caller then writes each
+ * succeed, else the put is empty and gives both allocations back.  When a
+ * caller's eviction left the SSD tier behind the CPU tier (m_s < m_c), the
+ * SSD copy of a block below m_c comes from its cached CPU block; if such a
+ * block is not ready yet, the put is refused (empty, nothing allocated).
+ * Out: num_skipped (m_c), num_transferred (D2H blocks), num_to_ssd (SSD
+ * blocks); per block of the batch: cpu_block_ids, ssd_block_ids,
+ * block_hashes.  cpu_block_ids[i] differs from fkv_cache_index_put's: it is
+ * the new CPU block for a block copied D2H, the cached CPU block for a block
+ * below m_c that the SSD tier lacks (the H2DISK source, nothing is copied
+ * into it), and -1 for every other block (cached in both tiers, or in an
+ * empty put).  ssd_block_ids[i] is the block's new SSD block, else -1.
+ * The caller then writes each
  * (cpu_block_ids[i] -> ssd_block_ids[i]) pair to the SSD tier
  * (fkv_transfer_kv_blocks_ssd) and marks those blocks ready in `ssd`
  * (fkv_cache_index_set_ready), the H2DISK op and callback of the reference's

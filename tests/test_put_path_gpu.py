@@ -518,3 +518,111 @@ def test_two_tier_put_matches_the_reference(tmp_path, name):
     ioctx.close()
     ci.close()
     si.close()
+
+
+def _two_tier(tmp_path, tpb=4, n_cpu=64, n_ssd=64):
+    """A two-layer case with a CPU-tier index and an SSD-tier index over
+    files under tmp_path."""
+    from flexkv_b200.cache_index import SsdTier
+    from flexkv_b200.layout import KVCacheLayout, KVCacheLayoutType
+    from flexkv_b200.ssd import SsdStrides, allocate_ssd_files
+    case = Case("two_tier", 2, 1, 8, tpb, 256, n_cpu)
+    pools = Pools(case)
+    ssd_layout = KVCacheLayout(KVCacheLayoutType.LAYERWISE, 2, n_ssd, tpb, 1, 8, False)
+    files, per_file = allocate_ssd_files(ssd_layout, 2, str(tmp_path / "ssd"), max_blocks_per_file=n_ssd)
+    ioctx = c_ext.SSDIOCTX(files, len(files), 0, 0)
+    strides = SsdStrides.of(case.cpu_layout_obj(), ssd_layout, sum(len(v) for v in files.values()), 2)
+    ci, si = CpuCacheIndex(n_cpu, tpb), CpuCacheIndex(n_ssd, tpb)
+    return case, pools, ci, si, SsdTier(si, ioctx, strides, 2, per_file)
+
+
+def _ssd_holds_cpu_blocks(case, pools, ssd, pairs):
+    """Read the SSD blocks back into a zeroed pool at their CPU blocks and
+    compare every chunk with the CPU pool."""
+    st, s = case.strides(), ssd.strides
+    back = torch.zeros_like(pools.cpu).pin_memory()
+    cids = np.array([c for c, _ in pairs], dtype=np.int64)
+    sids = np.array([x for _, x in pairs], dtype=np.int64)
+    c_ext.transfer_kv_blocks_ssd(ssd.ioctx, [0, 1], back.data_ptr(), sids, cids, s.cpu_layer_stride_in_bytes,
+                                 s.cpu_kv_stride_in_bytes, s.ssd_layer_stride_in_bytes, s.ssd_kv_stride_in_bytes,
+                                 s.chunk_size_in_bytes, s.block_stride_in_bytes, True, ssd.num_blocks_per_file,
+                                 cpu_pool_bytes=back.numel() * back.element_size())
+    a, w = pools.cpu.numpy(), back.numpy()
+    for c in cids.tolist():
+        for l in range(2):
+            for k in range(2):
+                o = l * st["cpu_layer"] + k * st["cpu_kv"] + c * st["cpu_block"]
+                if not np.array_equal(a[o:o + st["cpu_chunk"]], w[o:o + st["cpu_chunk"]]):
+                    return False
+    return True
+
+
+def test_two_tier_put_rolls_the_ssd_tier_back_when_its_writes_fail(tmp_path, monkeypatch):
+    """An SSD write that fails (a fake of the SSD call raising, on the host)
+    leaves no SSD-tier entry pointing at an unwritten block and no SSD block
+    leaked; the CPU tier keeps its copy; the same put then succeeds."""
+    case, pools, ci, si, ssd = _two_tier(tmp_path)
+    rng = np.random.default_rng(5)
+    toks = [rng.integers(0, 32000, 4 * n).astype(np.int64) for n in (3, 5)]
+    gids = [np.arange(3, dtype=np.int64), np.arange(5, dtype=np.int64) + 10]
+    before = si.stats()
+
+    def failing(*a, **k):
+        raise OSError("injected SSD write failure")
+
+    monkeypatch.setattr(c_ext, "transfer_kv_blocks_ssd", failing)
+    with pytest.raises(OSError):
+        ci.put_two_tier(ssd, toks, gids, pools.layout)
+    monkeypatch.undo()
+    after = si.stats()
+    assert (after["num_free_blocks"], after["total_cached_blocks"]) == \
+        (before["num_free_blocks"], before["total_cached_blocks"])
+    assert si.match(toks).num_matched.tolist() == [0, 0]
+    assert ci.match(toks).num_ready.tolist() == [3, 5]  # the CPU tier's part stands
+    res = ci.put_two_tier(ssd, toks, gids, pools.layout)
+    assert res.num_transferred.tolist() == [0, 0] and res.num_to_ssd.tolist() == [0, 0]  # CPU holds them
+    assert si.match(toks).num_matched.tolist() == [0, 0]  # the reference moves nothing when CPU has all
+    toks2 = [np.concatenate([t, rng.integers(0, 32000, 4).astype(np.int64)]) for t in toks]
+    gids2 = [np.arange(4, dtype=np.int64) + 20, np.arange(6, dtype=np.int64) + 30]
+    res = ci.put_two_tier(ssd, toks2, gids2, pools.layout)
+    assert res.num_transferred.tolist() == [1, 1] and res.num_to_ssd.tolist() == [4, 6]
+    pairs = [(c, x) for r in range(2) for c, x in zip(res.h2disk_cpu_blocks[r].tolist(), res.ssd_blocks[r].tolist())]
+    assert _ssd_holds_cpu_blocks(case, pools, ssd, pairs)
+    assert si.match(toks2).num_ready.tolist() == [4, 6]
+    ssd.ioctx.close()
+    ci.close()
+    si.close()
+
+
+def test_two_tier_put_after_ssd_only_eviction(tmp_path):
+    """The SSD tier evicted alone (m_s < m_c): the SSD copy of a block below
+    m_c comes from its cached CPU block.  While that block is not ready the
+    put is refused and allocates nothing; once it is ready the put writes
+    the SSD tier, whose bytes then equal the CPU blocks."""
+    case, pools, ci, si, ssd = _two_tier(tmp_path)
+    rng = np.random.default_rng(9)
+    a = rng.integers(0, 32000, 4 * 3).astype(np.int64)
+    res = ci.put_two_tier(ssd, [a], [np.arange(3, dtype=np.int64)], pools.layout, mark_ready=False)
+    assert res.num_transferred.tolist() == [3] and res.num_to_ssd.tolist() == [3]
+    pools.expect_d2h(res.gpu_blocks[0], res.cpu_blocks[0])
+    held = si.remove(res.block_hashes[0])
+    si.recycle(held[held >= 0])
+    ab = np.concatenate([a, rng.integers(0, 32000, 4 * 2).astype(np.int64)])
+    c_before, s_before = ci.stats(), si.stats()
+    res = ci.put_two_tier(ssd, [ab], [np.arange(5, dtype=np.int64) + 8], pools.layout)
+    assert (int(res.num_skipped[0]), int(res.num_transferred[0]), int(res.num_to_ssd[0])) == (0, 0, 0)
+    c_after, s_after = ci.stats(), si.stats()
+    for k in ("num_free_blocks", "total_cached_blocks"):
+        assert (c_after[k], s_after[k]) == (c_before[k], s_before[k]), k
+    ci.set_ready(res.block_hashes[0][:3])
+    res = ci.put_two_tier(ssd, [ab], [np.arange(5, dtype=np.int64) + 8], pools.layout)
+    assert (int(res.num_skipped[0]), int(res.num_transferred[0]), int(res.num_to_ssd[0])) == (3, 2, 5)
+    pools.expect_d2h(res.gpu_blocks[0], res.cpu_blocks[0])
+    assert pools.pool_matches()
+    pairs = list(zip(res.h2disk_cpu_blocks[0].tolist(), res.ssd_blocks[0].tolist()))
+    assert len(pairs) == 5
+    assert _ssd_holds_cpu_blocks(case, pools, ssd, pairs)
+    assert si.match([ab]).num_ready.tolist() == [5]
+    ssd.ioctx.close()
+    ci.close()
+    si.close()
