@@ -1656,6 +1656,125 @@ def run_reference(args, ws, rank, local, cfg, layout):
     return out, S
 
 
+SPLIT_VARIANTS = [
+    # (label, SM budget, copy-engine threshold per (layer,kv) row or None = default, loads in flight, ce-only)
+    ("sm_only_2sms", 2, 0, 16, False),
+    ("sm_only_8sms", 8, 0, 16, False),
+    ("sm_only_16sms", 16, 0, 16, False),
+    ("hybrid_4sms_256k", 4, 256 << 10, 16, False),
+    ("hybrid_4sms_1m", 4, 1 << 20, 16, False),
+    ("hybrid_8sms_1m", 8, 1 << 20, 16, False),
+    ("hybrid_16sms_1m", 16, 1 << 20, 16, False),
+    ("hybrid_16sms_1m_unroll8", 16, 1 << 20, 8, False),
+    ("copy_engines_only", -1, None, 16, True),
+]
+
+
+def split_sweep(args, ws, rank, local, cfg, layout):
+    """The split between copy-engine runs and the SM kernel, measured: each
+    variant's plans are built once, then every variant is timed in turn for
+    three rounds (interleaved, so box drift hits all alike); each direction
+    alone and both in flight together; with N ranks every rank runs each
+    timing at once (barrier before each).  Also the host link's contiguous
+    cudaMemcpyAsync peak and the bound the batch pattern allows: its joint
+    runs at that peak and the rest at the best measured rate for single
+    blocks.  One JSON line (rank 0); per-rank figures at N > 1."""
+    from flexkv_b200 import c_ext
+    if cfg["kind"] != "batch":
+        raise SystemExit("--split-sweep runs on the batch workloads (cfg2_llama3_8b, cfg5_dsv3_mla)")
+    S = Setup(cfg, layout, ws, local, args.cpu_blocks, args.gpu_alloc)
+    stream = torch.cuda.current_stream()
+    side = torch.cuda.Stream()
+    variants = SPLIT_VARIANTS
+    plans = {}
+    for label, sms, thr, unroll, ce_only in variants:
+        os.environ["FKV_UNROLL"] = str(unroll)
+        try:
+            kw = {} if thr is None else {"ce_min_run_bytes": thr}
+            plans[label] = [[c_ext.TransferPlan(torch.from_numpy(g), S.ptrs, S.g_kv, S.g_blk, torch.from_numpy(c),
+                                                S.cpu, S.c_kv, S.c_layer, S.c_blk, S.chunk, 0, sms, h2d, ce_only,
+                                                S.mla, gpu_layer_bytes=S.gpu_layer_bytes, **kw)
+                             for g, c, h2d in ops] for ops in S.steps]
+        finally:
+            os.environ.pop("FKV_UNROLL", None)
+    stats = {label: plans[label][0][0].stats() for label, *_ in variants}
+
+    def timed(fn):
+        barrier(ws)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b)
+
+    res = {label: {"h2d": [], "d2h": [], "duplex": []} for label, *_ in variants}
+    for label in plans:  # warm-up
+        for ops in plans[label]:
+            for p in ops:
+                p.execute(stream=stream)
+    torch.cuda.synchronize()
+    for _ in range(3):
+        for label in plans:
+            for s, ops in enumerate(plans[label]):
+                for (g, c, h2d), p in zip(S.steps[s], ops):
+                    ms = timed(lambda: p.execute(stream=stream))
+                    res[label]["h2d" if h2d else "d2h"].append(len(g) * S.block_bytes / ms / 1e6)
+
+                def both():
+                    e = torch.cuda.Event()
+                    e.record(stream)
+                    side.wait_event(e)
+                    ops[0].execute(stream=stream)
+                    ops[1].execute(stream=side)
+                    j = torch.cuda.Event()
+                    j.record(side)
+                    stream.wait_event(j)
+                res[label]["duplex"].append(sum(S.step_bytes.values()) / timed(both) / 1e6)
+    for label in plans:
+        for ops in plans[label]:
+            for p in ops:
+                p.close()
+    lp = measure_link_peaks(S, stream, sync=lambda: barrier(ws))
+    mine = [statistics.median(res[label][d]) for label, *_ in variants for d in ("h2d", "d2h", "duplex")]
+    mine += [lp["h2d"], lp["d2h"], lp["duplex_total"]]
+    allr = gather_over_ranks(ws, mine)
+    out = None
+    if rank == 0:
+        keys = [(label, d) for label, *_ in variants for d in ("h2d", "d2h", "duplex")]
+        table = {}
+        for i, (label, d) in enumerate(keys):
+            vals = [round(x[i], 2) for x in allr]
+            table.setdefault(label, {})[d] = vals[0] if ws == 1 else {"per_rank": vals, "box": round(sum(vals), 2)}
+        for label, sms, thr, unroll, ce_only in variants:
+            table[label].update(sm_budget=sms, ce_min_run_bytes=thr, unroll=unroll, copy_engines_only=ce_only,
+                                ce_fraction_h2d=round(stats[label]["ce_bytes"] /
+                                                      max(1, stats[label]["ce_bytes"] + stats[label]["sm_bytes"]), 3),
+                                ce_copies_h2d=stats[label]["ce_copies"])
+        lk = [[round(x[-3], 2), round(x[-2], 2), round(x[-1], 2)] for x in allr]
+        run_frac = max(stats[label]["ce_bytes"] / max(1, stats[label]["ce_bytes"] + stats[label]["sm_bytes"])
+                       for label, *_ in variants if not label.startswith("copy"))
+        r0 = lambda label, d: table[label][d] if ws == 1 else table[label][d]["per_rank"][0]  # noqa: E731
+        single = {d: max(r0(label, d) for label, *_ in variants if label.startswith("sm_only"))
+                  for d in ("h2d", "d2h")}
+        bound = {d: round(1.0 / (run_frac / lk[0][i] + (1 - run_frac) / single[d]), 2)
+                 for i, d in enumerate(("h2d", "d2h"))}
+        best = {d: max(r0(label, d) for label, *_ in variants) for d in ("h2d", "d2h", "duplex")}
+        out = {"split_sweep": table, "workload": args.config, "layout": layout, "gpu_alloc": args.gpu_alloc,
+               "n_gpus": ws, "cpu_pool_blocks": S.cpu_blocks,
+               "link_contiguous_copy": {"per_rank": lk, "how": "one contiguous cudaMemcpyAsync of up to 2 GiB "
+                                        "each way and both at once, every rank at once, median of 3"},
+               "pattern_bound": {"gbs": bound, "run_fraction_of_bytes": round(run_frac, 3),
+                                 "single_block_rate": single,
+                                 "how": "the batch's joint runs at the contiguous-copy peak and the rest at the "
+                                        "best SM-only rate, rank 0"},
+               "best_measured": best, "best_over_bound": {d: round(best[d] / bound[d], 4) for d in bound},
+               "how": "plans built once per variant, three interleaved rounds over the four steps, median; "
+                      "device time (CUDA events); duplex = the step's H2D and D2H batch in flight together"}
+    S.close()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -1682,6 +1801,9 @@ def main():
                     help="only the CPU-tier put-path measurement (one JSON line; --config picks the shape)")
     ap.add_argument("--tp", type=int, default=0,
                     help="TP ranks for cfg3 (one process drives them; default: all visible GPUs)")
+    ap.add_argument("--split-sweep", action="store_true",
+                    help="time the copy-engine/SM split variants on the --config batch workload (one JSON line; "
+                         "under torchrun every rank at once)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the link-peak, duplex and hash measurements (profiling runs)")
     args = ap.parse_args()
@@ -1703,6 +1825,17 @@ def main():
             print(json.dumps({"put_path": dict(measure_put_path(S), workload=args.config)}), flush=True)
         finally:
             S.close()
+        return
+    if args.split_sweep:
+        ws, rank, local = dist_setup()
+        cfg = dict(CONFIGS[args.config])
+        out = split_sweep(args, ws, rank, local, cfg, args.layout or cfg["layout"])
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        if ws > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
         return
     if args.impl == "reference" and int(os.environ.get("RANK", "0")) != 0:
         return  # the reference arm runs on rank 0 only

@@ -49,8 +49,8 @@ int get_ctx(int device, ThreadDeviceCtx **out) {
   FKV_CUDA(cudaGetDevice(&prev));
   if (prev != device) FKV_CUDA(cudaSetDevice(device));
   cudaError_t e = cudaEventCreateWithFlags(&ctx->fork_event, cudaEventDisableTiming);
-  if (e == cudaSuccess)
-    e = cudaEventCreateWithFlags(&ctx->staging_free, cudaEventDisableTiming);
+  for (int i = 0; e == cudaSuccess && i < ThreadDeviceCtx::kStagingSlots; ++i)
+    e = cudaEventCreateWithFlags(&ctx->staging[i].free, cudaEventDisableTiming);
   if (prev != device) cudaSetDevice(prev);
   if (e != cudaSuccess) return fail_cuda(e, "cudaEventCreateWithFlags");
   *out = ctx.get();
@@ -79,26 +79,34 @@ int ensure_side_streams(ThreadDeviceCtx *ctx, int n) {
 }
 
 int acquire_staging(ThreadDeviceCtx *ctx, size_t bytes, char **out) {
-  if (ctx->staging_pending) {
-    FKV_CUDA(cudaEventSynchronize(ctx->staging_free));
-    ctx->staging_pending = false;
+  const int i = ctx->staging_next;
+  ThreadDeviceCtx::StagingSlot &sl = ctx->staging[i];
+  if (sl.pending) {
+    FKV_CUDA(cudaEventSynchronize(sl.free));
+    sl.pending = false;
   }
-  if (bytes > ctx->staging_cap) {
-    if (ctx->staging) FKV_CUDA(cudaFreeHost(ctx->staging));
-    ctx->staging = nullptr;
-    ctx->staging_cap = 0;
+  if (bytes > sl.cap) {
+    if (sl.buf) FKV_CUDA(cudaFreeHost(sl.buf));
+    sl.buf = nullptr;
+    sl.cap = 0;
     size_t cap = 4096;
     while (cap < bytes) cap <<= 1;
-    FKV_CUDA(cudaHostAlloc((void **)&ctx->staging, cap, cudaHostAllocPortable));
-    ctx->staging_cap = cap;
+    FKV_CUDA(cudaHostAlloc((void **)&sl.buf, cap, cudaHostAllocPortable));
+    sl.cap = cap;
   }
-  *out = ctx->staging;
+  ctx->staging_cur = i;
+  *out = sl.buf;
   return FKV_OK;
 }
 
 int release_staging(ThreadDeviceCtx *ctx, cudaStream_t stream) {
-  FKV_CUDA(cudaEventRecord(ctx->staging_free, stream));
-  ctx->staging_pending = true;
+  const int i = ctx->staging_cur;
+  if (i < 0) return fail(FKV_ERR_INVALID_ARG, "release_staging without acquire_staging");
+  ThreadDeviceCtx::StagingSlot &sl = ctx->staging[i];
+  FKV_CUDA(cudaEventRecord(sl.free, stream));
+  sl.pending = true;
+  ctx->staging_cur = -1;
+  ctx->staging_next = (i + 1) % ThreadDeviceCtx::kStagingSlots;
   return FKV_OK;
 }
 
@@ -109,10 +117,12 @@ cudaMemPool_t g_pools[64] = {nullptr};
 
 int scratch_alloc(int device, size_t bytes, cudaStream_t s, void **out) {
   if (device < 0) FKV_CUDA(cudaGetDevice(&device));
+  if (device >= 64)  // one pool per device ordinal below 64; never alias another device's pool
+    return fail(FKV_ERR_INVALID_ARG, "device ordinal " + std::to_string(device) + " is outside [0, 64)");
   cudaMemPool_t pool;
   {
     std::lock_guard<std::mutex> lk(g_pool_mu);
-    pool = g_pools[device & 63];
+    pool = g_pools[device];
     if (!pool) {
       cudaMemPoolProps props;
       std::memset(&props, 0, sizeof(props));
@@ -123,7 +133,7 @@ int scratch_alloc(int device, size_t bytes, cudaStream_t s, void **out) {
       FKV_CUDA(cudaMemPoolCreate(&pool, &props));
       uint64_t keep = UINT64_MAX;
       FKV_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
-      g_pools[device & 63] = pool;
+      g_pools[device] = pool;
     }
   }
   FKV_CUDA(cudaMallocFromPoolAsync(out, bytes < 256 ? 256 : bytes, pool, s));

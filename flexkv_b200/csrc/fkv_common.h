@@ -42,11 +42,20 @@ struct ThreadDeviceCtx {
   std::vector<cudaStream_t> side_streams;  // copy-engine streams
   std::vector<cudaEvent_t> join_events;    // one per side stream
   cudaEvent_t fork_event = nullptr;
-  // Pinned staging for small uploads (plan tables, hash state).
-  char *staging = nullptr;
-  size_t staging_cap = 0;
-  cudaEvent_t staging_free = nullptr;  // recorded after the last upload read it
-  bool staging_pending = false;
+  // Pinned staging for small uploads (plan tables, hash state): a ring of
+  // slots used in turn, each freed by an event recorded after the upload
+  // that read it, so up to kStagingSlots asynchronous calls (on any mix of
+  // streams) are in flight before a call waits for an old upload.
+  static constexpr int kStagingSlots = 8;
+  struct StagingSlot {
+    char *buf = nullptr;
+    size_t cap = 0;
+    cudaEvent_t free = nullptr;  // recorded after the upload that read this slot
+    bool pending = false;
+  };
+  StagingSlot staging[kStagingSlots];
+  int staging_next = 0;  // slot the next acquire takes
+  int staging_cur = -1;  // slot handed out by the last acquire, until its release
 };
 
 // Context of the calling thread for `device` (current device if -1).
@@ -61,9 +70,12 @@ bool profiling();
 double now_us();
 // Ensure `n` side streams exist in ctx.
 int ensure_side_streams(ThreadDeviceCtx *ctx, int n);
-// Pinned staging buffer of at least `bytes`, safe to overwrite now.
+// Pinned staging buffer of at least `bytes`, safe to overwrite now (the
+// next slot of the thread's ring; waits only if that slot's last upload has
+// not run yet).
 int acquire_staging(ThreadDeviceCtx *ctx, size_t bytes, char **out);
-// Mark that an async copy on `stream` reads the staging buffer.
+// Mark that an async copy on `stream` reads the buffer the last
+// acquire_staging returned.
 int release_staging(ThreadDeviceCtx *ctx, cudaStream_t stream);
 
 // Plan and enqueue one transfer on `s` without synchronizing (transfer.cu).

@@ -32,16 +32,32 @@ namespace fkv {
 namespace {
 
 constexpr int kThreads = 256;          // 8 warps per CTA
-constexpr int kDefaultSms = 16;        // SM budget when transfer_sms == -1
-// Defaults from interleaved A/B runs on B200 (Llama-3-8B shape, 2048-block
-// batches): runs of >= 1 MiB per (layer,kv) row on the copy engines,
-// concurrent with the SM kernel, beat SM-only by 1-3% in both directions;
-// 512 KiB and 2 MiB thresholds and serial schedules do not.  When a run
-// folds into one descriptor across all layers (uniform layer stride), rows
-// from 128 KiB up go to the copy engines (H2D +2.7% over the unfolded
-// default); folding every block onto the copy engines is slower than the SM
-// kernel (2-D copies of 32 KiB rows) and is used only when asked for.
+// Defaults from interleaved A/B runs on one B200 (Llama-3-8B shape,
+// 2048-block batches with half the blocks in joint runs; DeepSeek-V3 MLA
+// batches; Qwen2-7B-shaped scattered 16 KiB chunks; each direction alone and
+// both in flight together):
+//  * SM budget (transfer_sms == -1): 8 SMs for a synchronous call, 16 for an
+//    asynchronous one or a plan.  Two SMs already fill the link on their
+//    own.  While copy-engine runs share the link, fewer SMs leave it more of
+//    the copy engines' larger requests: alone, H2D moves 51.3 GB/s with 8
+//    against 50.6 with 16.  With the other direction in flight 16 SMs are
+//    faster (73.5-74.5 against 71.9-72.9 GB/s for both directions).  A
+//    synchronous call is the only transfer its thread has in flight (the
+//    pattern of FlexKV's worker); asynchronous calls and plans usually share
+//    the link with the other direction.
+//  * Copy-engine threshold per (layer,kv) row of a run: 1 MiB; 256 KiB for
+//    H2D when the caller asks for 4 SMs or fewer (the only budget where the
+//    smaller runs pay off); 512 KiB, 2 MiB and serial schedules are slower.
+//  * 16 loads in flight per lane (UNROLL): one pass moves 8 KiB per warp, a
+//    16 KiB chunk takes two passes instead of four (scattered 16 KiB chunks,
+//    both directions in flight: +4 %; 32 KiB chunks: within noise).
+constexpr int kDefaultSmsSync = 8;
+constexpr int kDefaultSmsAsync = 16;
+constexpr int kDefaultSms = kDefaultSmsSync;  // device-side id lists (synchronous put/get paths)
+constexpr int kFewSms = 4;
+constexpr int kDefaultUnroll = 16;
 constexpr int64_t kDefaultCeMinRunBytes = 1ll << 20;
+constexpr int64_t kDefaultCeMinRunBytesFewSms = 256ll << 10;
 constexpr int64_t kDefaultCeMinRunBytesFolded = 128ll << 10;
 constexpr int kDefaultCeStreams = 2;
 constexpr int kMaxCeStreams = 8;
@@ -168,7 +184,7 @@ __global__ void __launch_bounds__(kThreads) kv_copy_devn_kernel(CopyParams p, co
   p.n = n;
   p.per_layer = kv_dim * n;
   p.num_chunks = num_layers * p.per_layer;
-  copy_body<H2D, 8, false>(p);
+  copy_body<H2D, kDefaultUnroll, false>(p);
 }
 
 struct CeCopy {
@@ -394,7 +410,12 @@ int build_host_plan(const fkv_transfer_desc &d, int device, HostPlan &hp) {
   // Split into copy-engine runs and SM chunks.
   const bool ce_all = d.use_ce_transfer != 0;
   const int64_t thr_user = d.ce_min_run_bytes >= 0 ? d.ce_min_run_bytes : env_i64("FKV_CE_MIN_RUN_BYTES", -1);
-  const int64_t thr = kDefaultCeMinRunBytes;
+  // The SM budget asked for (-1: the default, decided after the split).
+  const int sms_req = d.transfer_sms > 0 ? d.transfer_sms : env_int("FKV_TRANSFER_SMS", -1);
+  // The lower H2D threshold pays only while few SMs share the link with the
+  // copy engines (at the default 8 SMs the 1 MiB threshold is faster).
+  const int64_t thr = (hp.h2d && sms_req > 0 && sms_req <= kFewSms) ? kDefaultCeMinRunBytesFewSms
+                                                                    : kDefaultCeMinRunBytes;
   const int64_t thr_folded = kDefaultCeMinRunBytesFolded;
   int mp = 0;
   if (int rc = max_pitch(device, &mp)) return rc;
@@ -497,10 +518,9 @@ int build_host_plan(const fkv_transfer_desc &d, int device, HostPlan &hp) {
   if (!hp.sm_gpu.empty()) {
     ThreadDeviceCtx *ctx = nullptr;
     if (int rc = get_ctx(device, &ctx)) return rc;
-    int sms = d.transfer_sms;
-    if (sms <= 0) sms = env_int("FKV_TRANSFER_SMS", kDefaultSms);
+    int sms = sms_req > 0 ? sms_req : (d.synchronous ? kDefaultSmsSync : kDefaultSmsAsync);
     sms = std::min(sms, ctx->num_sms);
-    hp.unroll_idx = variant_index(env_int("FKV_UNROLL", 8), env_int("FKV_LD_PF256", 0));
+    hp.unroll_idx = variant_index(env_int("FKV_UNROLL", kDefaultUnroll), env_int("FKV_LD_PF256", 0));
     int occ = 1;
     if (int rc = ctas_per_sm(device, hp.h2d, hp.unroll_idx, &occ)) return rc;
     const int64_t chunks = L * KV * (int64_t)hp.sm_gpu.size();
@@ -1088,7 +1108,7 @@ extern "C" int fkv_transfer_kv_blocks_noalloc(
   FKV_CUDA(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device));
   int sms = transfer_sms > 0 ? std::min(transfer_sms, num_sms) : std::min(kDefaultSms, num_sms);
   const bool h2d = is_host_to_device != 0;
-  const int variant = variant_index(8, 0);
+  const int variant = variant_index(kDefaultUnroll, 0);
   int occ = 1;
   if (int rc = ctas_per_sm(device, h2d, variant, &occ)) return rc;
   const int64_t warps_per_cta = kThreads / 32;
