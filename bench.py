@@ -1775,7 +1775,18 @@ def split_sweep(args, ws, rank, local, cfg, layout):
     return out
 
 
+def claim_stdout():
+    """Keep stdout for the one JSON line: everything else written to file
+    descriptor 1 from here on (NCCL's version banner, library notices) goes
+    to stderr.  Returns the stream the JSON line is printed on."""
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    return os.fdopen(saved, "w")
+
+
 def main():
+    out_stream = claim_stdout()
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -1812,17 +1823,17 @@ def main():
         args.warmup = 3
     if args.hash_only:
         torch.cuda.set_device(0)
-        print(json.dumps({"hash": measure_hash()}), flush=True)
+        print(json.dumps({"hash": measure_hash()}), file=out_stream, flush=True)
         return
     if args.ssd_only:
-        print(json.dumps({"ssd": measure_ssd()}), flush=True)
+        print(json.dumps({"ssd": measure_ssd()}), file=out_stream, flush=True)
         return
     if args.put_only:
         torch.cuda.set_device(0)
         cfg = dict(CONFIGS[args.config])
         S = Setup(cfg, args.layout or cfg["layout"], 1, 0, args.cpu_blocks, args.gpu_alloc)
         try:
-            print(json.dumps({"put_path": dict(measure_put_path(S), workload=args.config)}), flush=True)
+            print(json.dumps({"put_path": dict(measure_put_path(S), workload=args.config)}), file=out_stream, flush=True)
         finally:
             S.close()
         return
@@ -1831,7 +1842,7 @@ def main():
         cfg = dict(CONFIGS[args.config])
         out = split_sweep(args, ws, rank, local, cfg, args.layout or cfg["layout"])
         if rank == 0:
-            print(json.dumps(out), flush=True)
+            print(json.dumps(out), file=out_stream, flush=True)
         if ws > 1:
             import torch.distributed as dist
             dist.barrier()
@@ -1865,7 +1876,7 @@ def main():
     if S is not None:
         S.close()
     if rank == 0 and out is not None:
-        print(json.dumps(out), flush=True)
+        print(json.dumps(out), file=out_stream, flush=True)
     if ws > 1:
         import torch.distributed as dist
         dist.barrier()
