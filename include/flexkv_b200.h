@@ -120,7 +120,11 @@ typedef struct fkv_transfer_desc {
   int num_layers;
   int is_host_to_device;
   int is_mla;
-  int transfer_sms;       /* -1 = default                                  */
+  int transfer_sms;       /* SMs for the copy kernel; -1 = default: 8 for a
+                             synchronous call, 16 for an asynchronous one or
+                             a plan (measured A/B: fewer SMs leave the copy
+                             engines more of the link while one direction
+                             runs alone; 16 keep both directions fuller)  */
   int use_ce_transfer;    /* 1 = copy engines only                         */
   int synchronous;        /* 1 = stream-synchronize before returning       */
   const int64_t *gpu_block_ids;
@@ -136,7 +140,8 @@ typedef struct fkv_transfer_desc {
   int64_t chunk_size_in_bytes;
   int64_t cpu_pool_bytes;    /* >0: bounds-check every CPU chunk           */
   int64_t gpu_layer_bytes;   /* >0: bounds-check every GPU chunk per layer */
-  int64_t ce_min_run_bytes;  /* <0 default (1 MiB; 128 KiB for a run that
+  int64_t ce_min_run_bytes;  /* <0 default (1 MiB; 256 KiB for H2D when
+                                transfer_sms is 1-4; 128 KiB for a run that
                                 folds into one descriptor across all
                                 layers); 0 = SM kernel only; else runs whose
                                 per-(layer,kv) row reaches this many bytes
