@@ -411,7 +411,10 @@ int build_host_plan(const fkv_transfer_desc &d, int device, HostPlan &hp) {
   const bool ce_all = d.use_ce_transfer != 0;
   const int64_t thr_user = d.ce_min_run_bytes >= 0 ? d.ce_min_run_bytes : env_i64("FKV_CE_MIN_RUN_BYTES", -1);
   // The SM budget asked for (-1: the default, decided after the split).
-  const int sms_req = d.transfer_sms > 0 ? d.transfer_sms : env_int("FKV_TRANSFER_SMS", -1);
+  // Order: the caller's transfer_sms, FKV_TRANSFER_SMS_H2D / _D2H, FKV_TRANSFER_SMS, the default.
+  const int sms_dir = env_int(hp.h2d ? "FKV_TRANSFER_SMS_H2D" : "FKV_TRANSFER_SMS_D2H", -1);
+  const int sms_req = d.transfer_sms > 0 ? d.transfer_sms
+                                         : (sms_dir > 0 ? sms_dir : env_int("FKV_TRANSFER_SMS", -1));
   // The lower H2D threshold pays only while few SMs share the link with the
   // copy engines (at the default 8 SMs the 1 MiB threshold is faster).
   const int64_t thr = (hp.h2d && sms_req > 0 && sms_req <= kFewSms) ? kDefaultCeMinRunBytesFewSms
