@@ -79,9 +79,11 @@ int acquire_staging(ThreadDeviceCtx *ctx, size_t bytes, char **out);
 int release_staging(ThreadDeviceCtx *ctx, cudaStream_t stream);
 
 // Plan and enqueue one transfer on `s` without synchronizing (transfer.cu).
-// The SM kernel's id table is staged in `ext_stage` (page-locked host
-// memory of ext_cap bytes that the caller keeps untouched until `s` passes
-// this point), or in the thread's own staging buffer when ext_stage is null.
+// An op whose SM part fits the kernel's parameters (up to 128 blocks and 96
+// layers) carries its id table there.  Otherwise the table is staged in
+// `ext_stage` (page-locked host memory of ext_cap bytes that the caller
+// keeps untouched until `s` passes this point), or in the thread's own
+// staging ring when ext_stage is null.
 int transfer_enqueue(const fkv_transfer_desc &d, cudaStream_t s, char *ext_stage, size_t ext_cap);
 // Upper bound of the staging bytes transfer_enqueue needs for `d`.
 size_t transfer_stage_bytes(const fkv_transfer_desc &d);

@@ -187,6 +187,33 @@ __global__ void __launch_bounds__(kThreads) kv_copy_devn_kernel(CopyParams p, co
   copy_body<H2D, kDefaultUnroll, false>(p);
 }
 
+// Small ops carry their id table inside the kernel's parameters instead of a
+// device buffer: no scratch allocation and no table upload before the
+// kernel can start (a per-call cost of a few to ten microseconds that
+// matters for ops of a few blocks).  The parameters are __grid_constant__,
+// so the copy reads the arrays in place through their generic addresses.
+// Capacity: kInlineMaxBlocks blocks on the SM path and kInlineMaxLayers
+// layers; the whole struct stays under the classic 4 KiB parameter limit.
+constexpr int kInlineMaxBlocks = 128;
+constexpr int kInlineMaxLayers = 96;
+
+struct InlineCopyParams {
+  CopyParams p;  // its table pointers are replaced by the arrays below
+  int64_t layer_ptrs[kInlineMaxLayers];
+  int64_t gpu_ids[kInlineMaxBlocks];
+  int64_t cpu_ids[kInlineMaxBlocks];
+};
+static_assert(sizeof(InlineCopyParams) <= 4000, "inline copy parameters must fit the 4 KiB limit");
+
+template <bool H2D>
+__global__ void __launch_bounds__(kThreads) kv_copy_inline_kernel(const __grid_constant__ InlineCopyParams q) {
+  CopyParams p = q.p;
+  p.layer_ptrs = reinterpret_cast<char *const *>(q.layer_ptrs);
+  p.gpu_ids = q.gpu_ids;
+  p.cpu_ids = q.cpu_ids;
+  copy_body<H2D, kDefaultUnroll, false>(p);
+}
+
 struct CeCopy {
   char *dst;
   const char *src;
@@ -556,9 +583,11 @@ CopyParams make_params(const HostPlan &hp, char *dev_table) {
   CopyParams p{};
   const size_t L = hp.num_layers, n = hp.sm_gpu.size();
   int64_t *t = reinterpret_cast<int64_t *>(dev_table);
-  p.layer_ptrs = reinterpret_cast<char *const *>(t);
-  p.gpu_ids = t + L;
-  p.cpu_ids = t + L + n;
+  if (t) {
+    p.layer_ptrs = reinterpret_cast<char *const *>(t);
+    p.gpu_ids = t + L;
+    p.cpu_ids = t + L + n;
+  }
   p.cpu_base = hp.cpu_dev_base;
   p.gpu_kv_stride = hp.gkv;
   p.gpu_block_stride = hp.gbs;
@@ -578,6 +607,36 @@ int launch_copy(bool h2d, int variant, int grid, const CopyParams &p, cudaStream
   FKV_CUDA(cudaLaunchKernel(k, dim3(grid), dim3(kThreads), args, 0, s));
   note_launch();
   return FKV_OK;
+}
+
+int launch_inline_copy(bool h2d, int grid, const InlineCopyParams &q, cudaStream_t s) {
+  const void *k = h2d ? (const void *)kv_copy_inline_kernel<true> : (const void *)kv_copy_inline_kernel<false>;
+  void *args[] = {const_cast<InlineCopyParams *>(&q)};
+  FKV_CUDA(cudaLaunchKernel(k, dim3(grid), dim3(kThreads), args, 0, s));
+  note_launch();
+  return FKV_OK;
+}
+
+// Whether the SM part of a host plan can carry its table in the kernel's
+// parameters (the default kernel variant only).
+// FKV_INLINE_TABLE=0 turns the path off (the table then goes through a
+// device buffer like larger ops).
+bool inline_table_fits(const HostPlan &hp) {
+  static const bool enabled = env_int("FKV_INLINE_TABLE", 1) != 0;
+  return enabled && hp.num_layers <= kInlineMaxLayers && (int64_t)hp.sm_gpu.size() <= kInlineMaxBlocks &&
+         hp.unroll_idx == variant_index(kDefaultUnroll, 0);
+}
+
+void fill_inline(const HostPlan &hp, const fkv_transfer_desc &d, InlineCopyParams &q) {
+  std::memset(&q, 0, sizeof(q));
+  q.p = make_params(hp, nullptr);
+  q.p.layer_ptrs = nullptr;  // the kernel points these at the arrays below
+  q.p.gpu_ids = nullptr;
+  q.p.cpu_ids = nullptr;
+  const size_t L = hp.num_layers, n = hp.sm_gpu.size();
+  for (size_t l = 0; l < L; ++l) q.layer_ptrs[l] = (int64_t)(uintptr_t)d.gpu_layer_ptrs[l];
+  std::memcpy(q.gpu_ids, hp.sm_gpu.data(), n * 8);
+  std::memcpy(q.cpu_ids, hp.sm_cpu.data(), n * 8);
 }
 
 // Fork the side streams from `s`, enqueue the copy-engine descriptors on
@@ -624,11 +683,17 @@ int join_ce(ThreadDeviceCtx *ctx, int nstreams, bool h2d, cudaStream_t s) {
 // A serial order keeps the two kinds of host-link traffic apart.
 int enqueue_transfer(ThreadDeviceCtx *ctx, bool h2d, int variant, int grid, const CopyParams *p,
                      bool has_sm, const std::vector<CeCopy> &ce, int nstreams, int schedule,
-                     cudaStream_t s, cudaEvent_t ev_start, cudaEvent_t ev_end) {
+                     cudaStream_t s, cudaEvent_t ev_start, cudaEvent_t ev_end,
+                     const InlineCopyParams *iq = nullptr) {
   auto kernel = [&]() -> int {
     if (ev_start) FKV_CUDA(cudaEventRecord(ev_start, s));
-    if (has_sm)
-      if (int rc = launch_copy(h2d, variant, grid, *p, s)) return rc;
+    if (has_sm) {
+      if (iq) {
+        if (int rc = launch_inline_copy(h2d, grid, *iq, s)) return rc;
+      } else if (int rc = launch_copy(h2d, variant, grid, *p, s)) {
+        return rc;
+      }
+    }
     if (ev_end) FKV_CUDA(cudaEventRecord(ev_end, s));
     return FKV_OK;
   };
@@ -673,6 +738,14 @@ int transfer_enqueue(const fkv_transfer_desc &d, cudaStream_t s, char *ext_stage
   if (int rc = get_ctx(device, &ctx)) return rc;
   char *dev_table = nullptr;
   CopyParams p{};
+  if (!hp.sm_gpu.empty() && inline_table_fits(hp)) {
+    // Small op: the table rides in the kernel's parameters (no allocation, no
+    // upload); a caller's staging slice, if given, simply goes unused.
+    InlineCopyParams q;
+    fill_inline(hp, d, q);
+    return enqueue_transfer(ctx, hp.h2d, hp.unroll_idx, hp.grid, nullptr, true, hp.ce, hp.num_ce_streams,
+                            hp.ce_schedule, s, nullptr, nullptr, &q);
+  }
   if (!hp.sm_gpu.empty()) {
     const size_t tb = table_bytes(hp);
     char *stage = ext_stage;
